@@ -1,0 +1,390 @@
+#!/usr/bin/env python3
+"""Benchmark of the EXL3 trellis encoder on B200.
+
+Workload (the encoder sweep): 65,536 16x16 tiles per GPU of
+N(0,1) weights scaled per (tile, row) by LogNormal(0, 0.5), K=2 (headline,
+the reference's published 1,711.5 tiles/s on Arc B580 is for this K), mul1
+codebook, tail-biting two-pass encode with packed output. One step encodes the
+whole batch. Synthetic seeded data; the reference evaluates no dataset here.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N > 1 runs one rank per GPU under torch.distributed.run; every rank encodes
+its own 65,536 tiles (weak scaling, no data-path collective); the reported
+value is all ranks' tiles / the slowest rank's device time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime as _dt
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "encoder tiles/s at K=2/4 (1/2/4/8 B200); seconds per 4096x4096 layer"
+PUBLISHED_K2_TILES_PER_S = 1711.5     # Arc B580, K=2 mul1, 65,536 tiles
+ACS_PER_TILE = 2 * 256 * 65536        # candidate add-compare-selects per tile (both passes)
+FP16_OPS_PER_ACS = 3                  # sub, fma, compare per candidate
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--K", type=int, default=2)
+    ap.add_argument("--tiles", type=int, default=65536)
+    ap.add_argument("--chunk", type=int, default=8192, help="tiles per workspace chunk")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-k4", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def make_tiles(n, seed, device):
+    import torch
+
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    base = torch.randn((n, 16, 16), generator=g)
+    scale = torch.exp(0.5 * torch.randn((n, 16, 1), generator=g))
+    return (base * scale).reshape(n, 256).to(device)
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            for name, val in zip(names, r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "samples": len(rows), "reasons": sorted(reasons)}
+
+
+def lib_timing():
+    from exl3_intel_arc_quantizer_b200._ext import lib
+
+    h = lib()
+    h.exl3_timing_end.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
+                                  ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64)]
+    return h
+
+
+def fp16x2_peak():
+    import torch
+
+    from exl3_intel_arc_quantizer_b200._ext import lib
+
+    h = lib()
+    h.exl3_probe_fp16x2_rate.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.c_void_p]
+    best = 0.0
+    for _ in range(3):
+        v = ctypes.c_double(0.0)
+        rc = h.exl3_probe_fp16x2_rate(ctypes.byref(v), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        if rc == 0:
+            best = max(best, v.value)
+    return best
+
+
+def cpu_baseline(K, threads=None, seconds_target=12.0, impl_tag="port"):
+    """C oracle (plain-C restatement of the reference encoder), all host
+    threads, on a bounded sample of the same workload."""
+    import numpy as np
+
+    from oracle.trellis_oracle import COracle
+
+    threads = threads or os.cpu_count() or 1
+    o = COracle(K, 2)
+    probe = make_tiles(threads, 99, "cpu").numpy()
+    t0 = time.perf_counter()
+    o.encode_batch(probe, threads=threads)
+    per_round = max(1e-3, time.perf_counter() - t0)
+    rounds = max(1, int(seconds_target / per_round))
+    n = threads * rounds
+    tiles = make_tiles(n, 7, "cpu").numpy()
+    t0 = time.perf_counter()
+    r = o.encode_batch(tiles, threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tiles/s", "cores": int(r["threads"]), "kind": impl_tag,
+            "sample": f"{n} tiles of the config-2 distribution, K={K}, C restatement of the "
+                      f"reference encoder (oracle/trellis_oracle.c), {dt:.1f}s"}
+
+
+def run_reference(args):
+    """Reference arm: the reference encoder's algorithm on the host cores
+    (C restatement in oracle/, every host thread), bounded samples."""
+    world, rank, local = dist_env()
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    from oracle.trellis_oracle import COracle
+
+    o = COracle(args.K, 2)
+    per_step = threads * 2
+    tiles = make_tiles(per_step, 7, "cpu").numpy()
+    for _ in range(args.warmup):
+        o.encode_batch(tiles[:threads], threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        r = o.encode_batch(tiles, threads=threads)
+    dt = time.perf_counter() - t0
+    value = per_step * args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tiles/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"encoder sweep (config 2) K={args.K} mul1 L=256, "
+                               f"{per_step} tiles per step (bounded sample)", "K": args.K},
+        "cpu_baseline": {"value": value, "unit": "tiles/s", "cores": int(r["threads"]),
+                         "kind": "port",
+                         "sample": f"{per_step} tiles/step x {args.steps} steps, C restatement "
+                                   "of the reference encoder (reference is Python/SYCL; its "
+                                   "checkout is not on the GPU host)"},
+        "e2e": {"value": value, "unit": "tiles/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=_dt.timedelta(seconds=300), device_id=device)
+
+    from exl3_intel_arc_quantizer_b200._ext import ext
+    from exl3_intel_arc_quantizer_b200.xpu_quantizer import ScratchArena, XPUTrellisEncoder
+
+    K, n = args.K, args.tiles
+    enc = XPUTrellisEncoder(K=K, cb=2, device_index=local,
+                            arena=ScratchArena(device_index=local, default_cap_b=args.chunk))
+    x = make_tiles(n, 1234 + rank, device)
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=device)  # > L2 (126 MB)
+
+    for _ in range(args.warmup):
+        enc.encode_device(x)
+    torch.cuda.synchronize()
+
+    timing = lib_timing()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    timing.exl3_timing_begin()
+    step_ms = []
+    for _ in range(args.steps):
+        flush.zero_()                         # evict L2 between timed steps
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        enc.encode_device(x)
+        e1.record()
+        e1.synchronize()
+        step_ms.append(e0.elapsed_time(e1))
+    torch.cuda.synchronize()
+    acs_ms, tb_ms = ctypes.c_double(), ctypes.c_double()
+    acs_n, total_n = ctypes.c_int64(), ctypes.c_int64()
+    timing.exl3_timing_end(ctypes.byref(acs_ms), ctypes.byref(tb_ms), ctypes.byref(acs_n),
+                           ctypes.byref(total_n))
+    clk = clocks.stop()
+    total_ms = sum(step_ms)
+    if world > 1:
+        t = torch.tensor([total_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        dist.barrier()
+    value = world * n * args.steps / (total_ms / 1e3)
+
+    # secondary: K=4 throughput (same workload, same timing rules)
+    k4 = None
+    if not args.no_k4 and K != 4:
+        enc4 = XPUTrellisEncoder(K=4, cb=2, device_index=local,
+                                 arena=ScratchArena(device_index=local, default_cap_b=args.chunk))
+        for _ in range(2):
+            enc4.encode_device(x)
+        ms4 = []
+        for _ in range(max(2, args.steps // 2)):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            enc4.encode_device(x)
+            e1.record()
+            e1.synchronize()
+            ms4.append(e0.elapsed_time(e1))
+        k4 = world * n * len(ms4) / (sum(ms4) / 1e3)
+        enc4.arena.release()
+
+    # e2e through the op binding with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        host_in = x.cpu().pin_memory()
+        h_w = torch.empty((n, 256), dtype=torch.float32).pin_memory()
+        h_i = torch.empty((n, 256), dtype=torch.int16).pin_memory()
+        h_p = torch.empty((n, 16 * K), dtype=torch.int16).pin_memory()
+        d_in = torch.empty_like(x)
+        d_w = torch.empty_like(x)
+        d_i = torch.empty((n, 256), dtype=torch.int16, device=device)
+        d_p = torch.empty((n, 16 * K), dtype=torch.int16, device=device)
+        ws, per, adm = enc.arena.acquire(K, 256, args.chunk)
+        e = ext()
+
+        def one():
+            d_in.copy_(host_in, non_blocking=True)
+            e.encode_tiles(d_in, d_w, d_i, d_p, None, ws[: adm * per], K, 2)
+            h_w.copy_(d_w, non_blocking=True)
+            h_i.copy_(d_i, non_blocking=True)
+            h_p.copy_(d_p, non_blocking=True)
+
+        for _ in range(2):
+            one()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            one()
+        e1.record()
+        e1.synchronize()
+        t_e2e = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([t_e2e], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t_e2e = float(t.item())
+        e2e = {"value": world * n * args.steps / (t_e2e / 1e3), "unit": "tiles/s",
+               "h2d_bytes_per_step": int(host_in.numel() * 4),
+               "d2h_bytes_per_step": int(h_w.numel() * 4 + h_i.numel() * 2 + h_p.numel() * 2)}
+
+    peak = fp16x2_peak()
+    tiles_timed = n * args.steps
+    achieved = tiles_timed * ACS_PER_TILE * FP16_OPS_PER_ACS / (acs_ms.value / 1e3)
+    traffic = None
+    tfile = REPO / "profiles" / f"encoder_k{K}_dram_per_launch.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("dram_bytes_per_tile")
+        if traffic is not None:
+            traffic = traffic * (min(args.chunk, n))
+    roofline = {
+        "bound": "fp16_alu",
+        "achieved": achieved / 1e9, "peak": peak / 1e9, "unit": "Gop/s",
+        "frac": achieved / peak if peak else None,
+        "peak_source": "measured live: exl3_probe_fp16x2_rate (fma.rn.f16x2 at full occupancy)",
+        "work": f"{ACS_PER_TILE} candidate ACS/tile x {FP16_OPS_PER_ACS} fp16 ops (sub, fma, "
+                "compare)",
+        "kernel": "exl3::acs_kernel (pass 1 + pass 2)",
+        "acs_share_of_step": acs_ms.value / max(1e-9, total_ms / max(1, world)),
+        "traffic": traffic,
+        "traffic_unit": "bytes per launch (ncu dram read+write)",
+    }
+    bp_bytes_per_tile = 256 * (4096 if K <= 3 else 2048)
+    roofline["hbm_backpointer_gbs"] = (tiles_timed * bp_bytes_per_tile * 1.5
+                                       / (acs_ms.value / 1e3) / 1e9)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(K)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tiles/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": (value / PUBLISHED_K2_TILES_PER_S) if K == 2 else None,
+            "dtype": "f16", "data": "synthetic",
+            "config": {"workload": f"encoder sweep (config 2): {n} tiles/GPU of N(0,1) x "
+                                   f"LogNormal(0,0.5) row scales, K={K}, mul1, L=256, "
+                                   "tail-biting 2-pass + packed output",
+                       "K": K, "tiles_per_gpu": n, "chunk_tiles": args.chunk,
+                       "l2": "flushed between timed steps (512 MiB write)",
+                       "parallelism": f"tiles sharded, {world} rank(s), no collective"},
+            "k4_tiles_per_s": k4,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": int(total_n.value),
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    enc.arena.release()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,81 @@
+"""Loader for the native layer.
+
+The product path has no CPU fallback: every operation that needs the CUDA
+kernels calls :func:`ext` (or :func:`lib`), which raises if the shipped
+binaries are missing or stale and cannot be rebuilt, or if no CUDA device is
+present.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import importlib.machinery
+import importlib.util
+import threading
+
+from . import _build
+
+_LOCK = threading.Lock()
+_EXT = None
+_LIB = None
+
+
+class NativeUnavailable(RuntimeError):
+    """The sm_100a kernels cannot be used in this process."""
+
+
+def lib() -> ctypes.CDLL:
+    """``libexl3k.so`` through ctypes (C ABI of ``include/exl3k.h``)."""
+    global _LIB
+    with _LOCK:
+        if _LIB is None:
+            path = _build.library_path()
+            if not _build._stamp_ok(path, _build.library_digest()):
+                _build.build_library()
+            _LIB = ctypes.CDLL(str(path), mode=ctypes.RTLD_GLOBAL)
+            _declare(_LIB)
+        return _LIB
+
+
+def _declare(handle: ctypes.CDLL) -> None:
+    c = ctypes
+    handle.exl3_last_error.restype = c.c_char_p
+    handle.exl3_version.restype = c.c_char_p
+    handle.exl3_quantize_tiles_ws_bytes.restype = c.c_size_t
+    handle.exl3_quantize_tiles_ws_bytes.argtypes = [c.c_int64, c.c_int, c.c_int]
+
+
+def ext():
+    """The PyTorch binding module (``exl3_b200_ext``)."""
+    global _EXT
+    if _EXT is not None:
+        return _EXT
+    import torch  # noqa: F401  (libtorch symbols must be loaded first)
+
+    lib()
+    with _LOCK:
+        if _EXT is None:
+            path = _build.extension_path()
+            if not _build._stamp_ok(path, _build.extension_digest()):
+                _build.build_extension()
+            loader = importlib.machinery.ExtensionFileLoader(_build.EXT_NAME, str(path))
+            spec = importlib.util.spec_from_file_location(_build.EXT_NAME, str(path), loader=loader)
+            module = importlib.util.module_from_spec(spec)
+            loader.exec_module(module)
+            _EXT = module
+    return _EXT
+
+
+def require_cuda(device=None):
+    """Raise unless a CUDA device is usable; returns a ``torch.device``."""
+    import torch
+
+    if not torch.cuda.is_available():
+        raise NativeUnavailable(
+            "no CUDA device: the EXL3 B200 kernels have no CPU fallback")
+    if device is None:
+        return torch.device("cuda", torch.cuda.current_device())
+    dev = torch.device(device)
+    if dev.type != "cuda":
+        raise NativeUnavailable(f"device {dev} is not a CUDA device")
+    return dev

@@ -1,0 +1,864 @@
+// EXL3 trellis Viterbi tile encoder for B200 (sm_100a).
+//
+// Algorithm restated from the reference CPU encoder
+// (exl3_quant/reference_encoder.py:130-324) and its SYCL kernel
+// (csrc/quantize_xpu/quantize_kernels.sycl:82-360):
+//   * 16-bit shift-register states, K bits per weight, S = 65536 >> K edges;
+//     for edge e and branch k: state = (k << (16-K)) | e,
+//     pred = state >> K = (k << (16-2K)) | (e >> K);
+//   * metric  d = fp16(v - w);  cost = fp16_fma(d, d, cost_prev[pred]);
+//   * winner  = first k (ascending) with strictly smaller cost;
+//   * two tail-biting passes: (roll = L/2, unconstrained) -> argmin ->
+//     traceback to ring index 0 = end_state; (roll = 0, step 0 masked to
+//     pred == end_state) -> traceback emitting states.
+//
+// B200 design (not a port):
+//   * one tile per CTA iteration, 512 threads, persistent CTAs (one per SM);
+//   * all 65536 codebook values of the tile's trellis live in registers
+//     (64 packed half2 per thread) for the whole kernel, so the inner loop
+//     never decodes the codebook;
+//   * each thread owns adjacent edge pairs (one half2 lane each): both lanes
+//     share every predecessor, so one broadcast cost feeds a packed
+//     sub / fma / compare / select sequence;
+//   * the fp16 cost vector ping-pongs in shared memory (one barrier per step);
+//   * backpointers are the chosen branch k only (K bits, not the reference's
+//     int16 predecessor), written with coalesced 32-bit stores; pass 1 records
+//     them only for the half of the ring the end_state traceback visits;
+//   * steps whose backpointers are never read use a packed min (3 ops per
+//     candidate pair) instead of compare-and-select;
+//   * a tile containing NaN switches to the exact compare-and-select form on
+//     every step, which reproduces the reference's NaN stickiness.
+#include "common.cuh"
+
+#include <mutex>
+#include <vector>
+
+namespace exl3 {
+
+constexpr int kNT = 512;  // threads per ACS CTA
+
+template <int K>
+struct Geo {
+  static constexpr int S = 1 << (16 - K);          // tracked edges
+  static constexpr int Kr = 16 - K;                // state = (k << Kr) | e
+  static constexpr int GB = 16 - 2 * K;            // pred = (k << GB) | g
+  static constexpr int Q = 1 << K;                 // branches per edge
+  static constexpr bool SPLIT = (K >= 7);          // branches split over lanes
+  static constexpr int EPT = SPLIT ? 2 : S / kNT;  // edges per thread
+  static constexpr int NP = EPT / 2;               // edge pairs per thread
+  static constexpr int QT = SPLIT ? 64 : Q;        // branches per thread
+  static constexpr int R = Q / QT;                 // lanes per edge pair
+  static constexpr int CP = SPLIT ? 1 : (K == 1 ? 4 : (NP < 8 ? NP : 8));  // pairs per chunk
+  static constexpr int NCH = NP / CP;                       // chunks per step
+  static constexpr int CG = SPLIT ? 1 : (((2 * CP) >> K) > 0 ? ((2 * CP) >> K) : 1);
+  static constexpr int CPW = (K == 1) ? 16 : (K == 2) ? 8 : (K <= 4) ? 4 : 2;
+  static constexpr int NW = SPLIT ? 1 : (NP + CPW - 1) / CPW;  // bp words/thread
+  // backpointer bytes per trellis step of one tile
+  static constexpr int BPS = SPLIT ? (S / 2) * 2 : NW * kNT * 4;
+  static constexpr int NCB = NP * QT;              // codebook half2 registers
+  static_assert(NCB == 64, "codebook register budget");
+};
+
+__host__ __device__ constexpr int bp_step_bytes(int K) {
+  return K == 1 ? Geo<1>::BPS : K == 2 ? Geo<2>::BPS : K == 3 ? Geo<3>::BPS
+       : K == 4 ? Geo<4>::BPS : K == 5 ? Geo<5>::BPS : K == 6 ? Geo<6>::BPS
+       : K == 7 ? Geo<7>::BPS : Geo<8>::BPS;
+}
+
+__device__ __forceinline__ uint32_t kconst(int k) {
+  return (uint32_t)k | ((uint32_t)k << 16);
+}
+
+// Codebook values of this thread's candidates, packed per edge pair.
+template <int K>
+__device__ __forceinline__ void init_codebook(uint32_t (&cbv)[64], int cb, int t) {
+  using G = Geo<K>;
+  if constexpr (!G::SPLIT) {
+#pragma unroll
+    for (int p = 0; p < G::NP; ++p) {
+      const uint32_t e0 = (uint32_t)(t * G::EPT + 2 * p);
+#pragma unroll
+      for (int k = 0; k < G::Q; ++k) {
+        const uint32_t s0 = ((uint32_t)k << G::Kr) | e0;
+        cbv[p * G::Q + k] = (uint32_t)cb_state_bits(cb, s0) |
+                            ((uint32_t)cb_state_bits(cb, s0 + 1) << 16);
+      }
+    }
+  } else {
+    const uint32_t P = (uint32_t)(t / G::R), r = (uint32_t)(t % G::R);
+    const uint32_t e0 = 2 * P;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+      const uint32_t k = 64 * r + j;
+      const uint32_t s0 = (k << G::Kr) | e0;
+      cbv[j] = (uint32_t)cb_state_bits(cb, s0) |
+               ((uint32_t)cb_state_bits(cb, s0 + 1) << 16);
+    }
+  }
+}
+
+// Backpointer storage modes.
+enum BpMode { BP_NONE = 0, BP_COMPACT = 1, BP_PRED16 = 2 };
+
+// One ACS step for K <= 6: thread owns NP adjacent edge pairs and all Q
+// branches of each.
+//   FIRST : step 0 (no accumulated cost; optional wrap mask on pred)
+//   BPM   : what to record for the traceback
+//   EXACT : compare-and-select on every branch (NaN-faithful)
+template <int K, bool FIRST, int BPM, bool EXACT>
+__device__ __forceinline__ void step_pairs(const uint32_t (&cbv)[64], uint32_t w2,
+                                           const uint16_t* __restrict__ cin,
+                                           uint16_t* __restrict__ cout,
+                                           void* __restrict__ bp_step, int t,
+                                           int pre_state) {
+  using G = Geo<K>;
+  uint32_t bpw[G::NW];
+#pragma unroll
+  for (int w = 0; w < G::NW; ++w) bpw[w] = 0;
+
+#pragma unroll
+  for (int c = 0; c < G::NCH; ++c) {
+    const int e_base = t * G::EPT + 2 * c * G::CP;
+    const int g_base = e_base >> K;
+    constexpr int PCW = (G::CG + 1) / 2;
+    uint32_t pc[G::Q][PCW];
+    if constexpr (!FIRST) {
+#pragma unroll
+      for (int k = 0; k < G::Q; ++k) {
+        const uint16_t* src = cin + (k << G::GB) + g_base;
+        if constexpr (G::CG == 8) {
+          const uint4 v = *reinterpret_cast<const uint4*>(src);
+          pc[k][0] = v.x; pc[k][1] = v.y; pc[k][2] = v.z; pc[k][3] = v.w;
+        } else if constexpr (G::CG == 4) {
+          const uint2 v = *reinterpret_cast<const uint2*>(src);
+          pc[k][0] = v.x; pc[k][1] = v.y;
+        } else if constexpr (G::CG == 2) {
+          pc[k][0] = *reinterpret_cast<const uint32_t*>(src);
+        } else {
+          pc[k][0] = (uint32_t)(*src);
+        }
+      }
+    }
+    uint32_t res[G::CP];
+#pragma unroll
+    for (int p = 0; p < G::CP; ++p) {
+      const int gi = (G::CG == 1) ? 0 : ((2 * p) >> K);
+      const int pp = c * G::CP + p;  // pair index within the thread
+      uint32_t best = 0, idx = 0;
+#pragma unroll
+      for (int k = 0; k < G::Q; ++k) {
+        uint32_t P = 0;
+        if constexpr (!FIRST) {
+          const uint32_t word = pc[k][gi >> 1];
+          P = (gi & 1) ? h2_hi2(word) : h2_lo2(word);
+        }
+        const uint32_t d = h2_sub(cbv[pp * G::Q + k], w2);
+        uint32_t cst = h2_fma(d, d, P);
+        if constexpr (FIRST) {
+          if (pre_state >= 0) {
+            const int g = (e_base + 2 * p) >> K;
+            cst = (((k << G::GB) | g) == pre_state) ? cst : kHInf2;
+          }
+        }
+        if (k == 0) {
+          best = cst;
+        } else if constexpr (BPM != BP_NONE || EXACT) {
+          const uint32_t m = h2_lt_mask(cst, best);
+          best = EXACT ? bsel(m, cst, best) : h2_min(best, cst);
+          if constexpr (BPM != BP_NONE) idx = bsel(m, kconst(k), idx);
+        } else {
+          best = h2_min(best, cst);
+        }
+      }
+      res[p] = best;
+      if constexpr (BPM == BP_COMPACT) {
+        bpw[pp / G::CPW] |= idx << (K * (pp % G::CPW));
+      } else if constexpr (BPM == BP_PRED16) {
+        const uint32_t g = (uint32_t)((e_base + 2 * p) >> K);
+        reinterpret_cast<uint32_t*>(bp_step)[(e_base >> 1) + p] =
+            (idx << G::GB) | (g | (g << 16));
+      }
+    }
+    // results: CP packed pairs at edges [e_base, e_base + 2*CP)
+    uint32_t* dst = reinterpret_cast<uint32_t*>(cout + e_base);
+    if constexpr (G::CP >= 4) {
+#pragma unroll
+      for (int q = 0; q < G::CP / 4; ++q)
+        reinterpret_cast<uint4*>(dst)[q] =
+            make_uint4(res[4 * q], res[4 * q + 1], res[4 * q + 2], res[4 * q + 3]);
+    } else if constexpr (G::CP == 2) {
+      *reinterpret_cast<uint2*>(dst) = make_uint2(res[0], res[1]);
+    } else {
+      dst[0] = res[0];
+    }
+  }
+  if constexpr (BPM == BP_COMPACT) {
+    uint32_t* bw = reinterpret_cast<uint32_t*>(bp_step);
+#pragma unroll
+    for (int w = 0; w < G::NW; ++w) bw[w * kNT + t] = bpw[w];
+  }
+}
+
+// One ACS step for K >= 7: each edge pair is shared by R lanes, each lane
+// scanning 64 consecutive branches; lanes combine with warp shuffles, the
+// lower branch range winning ties (equivalent to one ascending scan).
+template <int K, bool FIRST, int BPM, bool EXACT>
+__device__ __forceinline__ void step_split(const uint32_t (&cbv)[64], uint32_t w2,
+                                           const uint16_t* __restrict__ cin,
+                                           uint16_t* __restrict__ cout,
+                                           void* __restrict__ bp_step, int t,
+                                           int pre_state) {
+  using G = Geo<K>;
+  const int P = t / G::R, r = t % G::R;
+  const int g = (2 * P) >> K;
+  const int k0 = 64 * r;
+  uint32_t best = kHInf2, idx = kconst(k0);
+#pragma unroll
+  for (int j8 = 0; j8 < 8; ++j8) {
+    uint32_t pc[8];
+    if constexpr (!FIRST) {
+      if constexpr (G::GB == 0) {
+        const uint4 v = *reinterpret_cast<const uint4*>(cin + k0 + 8 * j8);
+        pc[0] = v.x & 0xFFFFu; pc[1] = v.x >> 16; pc[2] = v.y & 0xFFFFu; pc[3] = v.y >> 16;
+        pc[4] = v.z & 0xFFFFu; pc[5] = v.z >> 16; pc[6] = v.w & 0xFFFFu; pc[7] = v.w >> 16;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) pc[j] = cin[((k0 + 8 * j8 + j) << G::GB) | g];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int jj = 8 * j8 + j;
+      const int k = k0 + jj;
+      const uint32_t P2 = FIRST ? 0u : h2_lo2(pc[j]);
+      const uint32_t d = h2_sub(cbv[jj], w2);
+      uint32_t cst = h2_fma(d, d, P2);
+      if constexpr (FIRST) {
+        if (pre_state >= 0) cst = (((k << G::GB) | g) == pre_state) ? cst : kHInf2;
+      }
+      if (jj == 0) {
+        // lane r = 0 seeds with branch 0 unconditionally (a NaN there sticks);
+        // the other lanes start from +inf and only take strictly smaller costs
+        const uint32_t m = h2_lt_mask(cst, best) | ((r == 0) ? 0xFFFFFFFFu : 0u);
+        best = bsel(m, cst, best);
+        if constexpr (BPM != BP_NONE) idx = bsel(m, kconst(k), idx);
+      } else if constexpr (BPM != BP_NONE || EXACT) {
+        const uint32_t m = h2_lt_mask(cst, best);
+        best = EXACT ? bsel(m, cst, best) : h2_min(best, cst);
+        if constexpr (BPM != BP_NONE) idx = bsel(m, kconst(k), idx);
+      } else {
+        best = h2_min(best, cst);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 1; off < G::R; off <<= 1) {
+    const uint32_t ob = __shfl_xor_sync(0xFFFFFFFFu, best, off);
+    const uint32_t oi = __shfl_xor_sync(0xFFFFFFFFu, idx, off);
+    const bool upper = (r & off) != 0;
+    const uint32_t lo_c = upper ? ob : best, hi_c = upper ? best : ob;
+    const uint32_t lo_i = upper ? oi : idx, hi_i = upper ? idx : oi;
+    const uint32_t m = h2_lt_mask(hi_c, lo_c);
+    best = bsel(m, hi_c, lo_c);
+    idx = bsel(m, hi_i, lo_i);
+  }
+  if (r == 0) {
+    reinterpret_cast<uint32_t*>(cout)[P] = best;
+    if constexpr (BPM == BP_COMPACT) {
+      reinterpret_cast<uint16_t*>(bp_step)[P] = (uint16_t)__byte_perm(idx, 0, 0x0020);
+    } else if constexpr (BPM == BP_PRED16) {
+      reinterpret_cast<uint32_t*>(bp_step)[P] =
+          (idx << G::GB) | ((uint32_t)g | ((uint32_t)g << 16));
+    }
+  }
+}
+
+template <int K, bool FIRST, int BPM, bool EXACT>
+__device__ __forceinline__ void acs_step(const uint32_t (&cbv)[64], uint32_t w2,
+                                         const uint16_t* cin, uint16_t* cout,
+                                         void* bp_step, int t, int pre_state) {
+  if constexpr (Geo<K>::SPLIT)
+    step_split<K, FIRST, BPM, EXACT>(cbv, w2, cin, cout, bp_step, t, pre_state);
+  else
+    step_pairs<K, FIRST, BPM, EXACT>(cbv, w2, cin, cout, bp_step, t, pre_state);
+}
+
+// Shared-memory layout of an ACS CTA.
+template <int K>
+struct Smem {
+  static constexpr size_t costs = 2ull * Geo<K>::S * sizeof(uint16_t);
+  static constexpr size_t tile = 256 * sizeof(uint32_t);
+  static constexpr size_t bytes = costs + tile;
+};
+
+// Load one tile: fp32 -> fp16 (round to nearest even), stored as {w, w}.
+// Returns nonzero (CTA-uniform) when any element is NaN.
+__device__ __forceinline__ int load_tile(const float* __restrict__ src, int L,
+                                         uint32_t* wt, int t) {
+  int nan = 0;
+  for (int i = t; i < L; i += kNT) {
+    const __half h = __float2half_rn(src[i]);
+    const uint32_t b = __half_as_ushort(h);
+    nan |= __hisnan(h) ? 1 : 0;
+    wt[i] = b | (b << 16);
+  }
+  return __syncthreads_or(nan);
+}
+
+// CTA-wide argmin over final costs: minimum cost, lowest edge on ties;
+// non-finite costs are skipped and an all-non-finite vector yields edge 0
+// (reference_encoder.py:206-214, quantize_kernels.sycl:161-234).
+template <int K>
+__device__ __forceinline__ int block_argmin(const uint16_t* costs, uint32_t* red, int t) {
+  using G = Geo<K>;
+  uint32_t key = 0xFFFFFFFFu;
+  for (int e = t; e < G::S; e += kNT) {
+    const uint32_t b = costs[e];
+    if ((b & 0x7C00u) != 0x7C00u) key = min(key, (b << 16) | (uint32_t)e);
+  }
+  key = __reduce_min_sync(0xFFFFFFFFu, key);
+  if ((t & 31) == 0) red[t >> 5] = key;
+  __syncthreads();
+  if (t < 32) {
+    uint32_t v = (t < kNT / 32) ? red[t] : 0xFFFFFFFFu;
+    v = __reduce_min_sync(0xFFFFFFFFu, v);
+    if (t == 0) red[0] = v;
+  }
+  __syncthreads();
+  const uint32_t v = red[0];
+  __syncthreads();
+  return v == 0xFFFFFFFFu ? 0 : (int)(v & 0xFFFFu);
+}
+
+// ---------------------------------------------------------------------------
+// Pass 1: roll = L/2, unconstrained. Records backpointers for ring indices
+// [0, L/2) (the steps i >= L/2 the end_state traceback walks) and the
+// argmin edge of the final costs.
+// ---------------------------------------------------------------------------
+template <int K, bool EXACT>
+__device__ __forceinline__ void run_pass1(const uint32_t (&cbv)[64], const uint32_t* wt,
+                                          uint16_t* cbuf0, uint16_t* cbuf1, uint8_t* bp,
+                                          int L, int t) {
+  using G = Geo<K>;
+  const int half = L / 2;
+  acs_step<K, true, BP_NONE, EXACT>(cbv, wt[half], nullptr, cbuf0, nullptr, t, -1);
+  __syncthreads();
+  for (int i = 1; i < half; ++i) {
+    const uint16_t* cin = (i & 1) ? cbuf0 : cbuf1;
+    uint16_t* cout = (i & 1) ? cbuf1 : cbuf0;
+    acs_step<K, false, BP_NONE, EXACT>(cbv, wt[i + half], cin, cout, nullptr, t, -1);
+    __syncthreads();
+  }
+  for (int i = half; i < L; ++i) {
+    const int ri = i - half;
+    const uint16_t* cin = (i & 1) ? cbuf0 : cbuf1;
+    uint16_t* cout = (i & 1) ? cbuf1 : cbuf0;
+    acs_step<K, false, BP_COMPACT, EXACT>(cbv, wt[ri], cin, cout,
+                                           bp + (size_t)ri * G::BPS, t, -1);
+    __syncthreads();
+  }
+}
+
+template <int K, bool EXACT>
+__device__ __forceinline__ void run_pass2(const uint32_t (&cbv)[64], const uint32_t* wt,
+                                          uint16_t* cbuf0, uint16_t* cbuf1, uint8_t* bp,
+                                          int L, int t, int pre) {
+  using G = Geo<K>;
+  acs_step<K, true, BP_COMPACT, EXACT>(cbv, wt[0], nullptr, cbuf0, bp, t, pre);
+  __syncthreads();
+  for (int i = 1; i < L; ++i) {
+    const uint16_t* cin = (i & 1) ? cbuf0 : cbuf1;
+    uint16_t* cout = (i & 1) ? cbuf1 : cbuf0;
+    acs_step<K, false, BP_COMPACT, EXACT>(cbv, wt[i], cin, cout,
+                                           bp + (size_t)i * G::BPS, t, -1);
+    __syncthreads();
+  }
+}
+
+template <int K, int PASS>
+__global__ void __launch_bounds__(kNT, 1)
+acs_kernel(const float* __restrict__ in, int n, int L, int cb,
+           uint8_t* __restrict__ bp, size_t bp_tile_bytes,
+           int32_t* __restrict__ best_edge,        // PASS 1 out
+           const int32_t* __restrict__ end_state,  // PASS 2 in
+           float* __restrict__ path_cost,          // PASS 2 out (nullable)
+           uint16_t* __restrict__ final_costs)     // (n, 2, S) fp16 (nullable)
+{
+  using G = Geo<K>;
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint16_t* cbuf0 = reinterpret_cast<uint16_t*>(smem);
+  uint16_t* cbuf1 = cbuf0 + G::S;
+  uint32_t* wt = reinterpret_cast<uint32_t*>(smem + Smem<K>::costs);
+  __shared__ uint32_t red[kNT / 32];
+  const int t = threadIdx.x;
+
+  uint32_t cbv[64];
+  init_codebook<K>(cbv, cb, t);
+
+  for (int tile = blockIdx.x; tile < n; tile += gridDim.x) {
+    const int nan = load_tile(in + (size_t)tile * L, L, wt, t);
+    uint8_t* tbp = bp + (size_t)tile * bp_tile_bytes;
+    const uint16_t* final_buf = ((L - 1) & 1) ? cbuf1 : cbuf0;
+    if constexpr (PASS == 1) {
+      if (nan) run_pass1<K, true>(cbv, wt, cbuf0, cbuf1, tbp, L, t);
+      else     run_pass1<K, false>(cbv, wt, cbuf0, cbuf1, tbp, L, t);
+      const int be = block_argmin<K>(final_buf, red, t);
+      if (t == 0) best_edge[tile] = be;
+    } else {
+      const int pre = end_state[tile];
+      if (nan) run_pass2<K, true>(cbv, wt, cbuf0, cbuf1, tbp, L, t, pre);
+      else     run_pass2<K, false>(cbv, wt, cbuf0, cbuf1, tbp, L, t, pre);
+      if (t == 0 && path_cost) path_cost[tile] = half_bits_to_float(final_buf[pre]);
+    }
+    if (final_costs) {
+      uint16_t* dst = final_costs + ((size_t)tile * 2 + (PASS - 1)) * G::S;
+      for (int e = t; e < G::S; e += kNT) dst[e] = final_buf[e];
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Traceback over compact backpointers.
+// ---------------------------------------------------------------------------
+template <int K>
+__device__ __forceinline__ int bp_branch(const uint8_t* step_base, int e) {
+  using G = Geo<K>;
+  if constexpr (!G::SPLIT) {
+    const int th = e / G::EPT, q = e % G::EPT;
+    const int p = q >> 1, b = q & 1;
+    const int w = p / G::CPW, pc = p % G::CPW;
+    const uint32_t word = reinterpret_cast<const uint32_t*>(step_base)[w * kNT + th];
+    return (int)((word >> (16 * b + K * pc)) & (G::Q - 1));
+  } else {
+    const uint32_t v = reinterpret_cast<const uint16_t*>(step_base)[e >> 1];
+    return (int)((v >> (8 * (e & 1))) & (G::Q - 1));
+  }
+}
+
+// Pass-1 traceback: from the argmin edge back through ring indices
+// L/2-1 .. 0; the edge reached is end_state (reference_encoder.py:216-251).
+template <int K>
+__global__ void tb1_kernel(const uint8_t* __restrict__ bp, size_t bp_tile_bytes, int n,
+                           int L, const int32_t* __restrict__ best_edge,
+                           int32_t* __restrict__ end_state) {
+  using G = Geo<K>;
+  const int tile = blockIdx.x * blockDim.x + threadIdx.x;
+  if (tile >= n) return;
+  const uint8_t* tbp = bp + (size_t)tile * bp_tile_bytes;
+  int e = best_edge[tile];
+  for (int ri = L / 2 - 1; ri >= 0; --ri) {
+    const int k = bp_branch<K>(tbp + (size_t)ri * G::BPS, e);
+    e = (k << G::GB) | (e >> K);
+  }
+  end_state[tile] = e;
+}
+
+// EXL3 container for one 16-element span: low K bits of each state,
+// MSB-first, 16 bits per word; written after the SWAP16 half-word exchange
+// (trellis_format.py:120-174).
+__device__ __forceinline__ void pack_span(const uint16_t* st16, int K, int span,
+                                          int16_t* out_tile) {
+  uint32_t acc = 0;
+  int nb = 0, j = K * span;
+  const uint32_t mask = (1u << K) - 1u;
+  for (int i = 0; i < 16; ++i) {
+    acc = (acc << K) | ((uint32_t)st16[16 * span + i] & mask);
+    nb += K;
+    if (nb >= 16) {
+      out_tile[j ^ 1] = (int16_t)((acc >> (nb - 16)) & 0xFFFFu);
+      nb -= 16;
+      acc &= (1u << nb) - 1u;
+      ++j;
+    }
+  }
+}
+
+// Pass-2 traceback: one warp per tile. Lane 0 walks the chain; the warp then
+// writes states, reconstruction and the packed container.
+constexpr int kTbWarps = 4;
+
+template <int K>
+__global__ void tb2_kernel(const uint8_t* __restrict__ bp, size_t bp_tile_bytes, int n,
+                           int L, int cb, const int32_t* __restrict__ end_state,
+                           float* __restrict__ out_w, int16_t* __restrict__ out_idx,
+                           int16_t* __restrict__ out_packed) {
+  using G = Geo<K>;
+  __shared__ uint16_t st[kTbWarps][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x * kTbWarps + warp;
+  if (tile >= n) return;
+  const uint8_t* tbp = bp + (size_t)tile * bp_tile_bytes;
+  if (lane == 0) {
+    int e = end_state[tile];
+    for (int i = L - 1; i >= 0; --i) {
+      const int k = bp_branch<K>(tbp + (size_t)i * G::BPS, e);
+      st[warp][i] = (uint16_t)((k << G::Kr) | e);
+      e = (k << G::GB) | (e >> K);
+    }
+  }
+  __syncwarp();
+  for (int i = lane; i < L; i += 32) {
+    const uint16_t s = st[warp][i];
+    out_idx[(size_t)tile * L + i] = (int16_t)s;
+    out_w[(size_t)tile * L + i] = half_bits_to_float(cb_state_bits(cb, s));
+  }
+  if (out_packed && L == 256 && lane < 16)
+    pack_span(st[warp], K, lane, out_packed + (size_t)tile * 16 * K);
+}
+
+// ---------------------------------------------------------------------------
+// Reference-layout split passes (int16 predecessors, every step recorded).
+// ---------------------------------------------------------------------------
+template <int K>
+__global__ void __launch_bounds__(kNT, 1)
+acs_ref_kernel(const float* __restrict__ in, int n, int L, int cb, int roll,
+               const int32_t* __restrict__ pre_states, int16_t* __restrict__ temp_edges,
+               uint16_t* __restrict__ temp_costs, int cost_slot) {
+  using G = Geo<K>;
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint16_t* cbuf0 = reinterpret_cast<uint16_t*>(smem);
+  uint16_t* cbuf1 = cbuf0 + G::S;
+  uint32_t* wt = reinterpret_cast<uint32_t*>(smem + Smem<K>::costs);
+  const int t = threadIdx.x;
+  uint32_t cbv[64];
+  init_codebook<K>(cbv, cb, t);
+  for (int tile = blockIdx.x; tile < n; tile += gridDim.x) {
+    load_tile(in + (size_t)tile * L, L, wt, t);
+    int16_t* te = temp_edges + (size_t)tile * L * G::S;
+    const int pre = pre_states[tile];
+    const int r0 = roll % L;
+    acs_step<K, true, BP_PRED16, true>(cbv, wt[r0], nullptr, cbuf0, te + (size_t)r0 * G::S,
+                                       t, pre);
+    __syncthreads();
+    for (int i = 1; i < L; ++i) {
+      int ri = i + roll;
+      if (ri >= L) ri -= L;
+      const uint16_t* cin = (i & 1) ? cbuf0 : cbuf1;
+      uint16_t* cout = (i & 1) ? cbuf1 : cbuf0;
+      acs_step<K, false, BP_PRED16, true>(cbv, wt[ri], cin, cout, te + (size_t)ri * G::S,
+                                          t, -1);
+      __syncthreads();
+    }
+    const uint16_t* final_buf = ((L - 1) & 1) ? cbuf1 : cbuf0;
+    uint16_t* dst = temp_costs + ((size_t)tile * 2 + cost_slot) * G::S;
+    for (int e = t; e < G::S; e += kNT) dst[e] = final_buf[e];
+    __syncthreads();
+  }
+}
+
+__global__ void ref_backward_kernel(const uint16_t* __restrict__ temp_costs,
+                                    const int16_t* __restrict__ temp_edges,
+                                    float* __restrict__ out_w, int16_t* __restrict__ out_idx,
+                                    int32_t* __restrict__ end_states, int n, int K, int cb,
+                                    int L, int roll, int cost_slot, int write_output) {
+  const int tile = blockIdx.x * blockDim.x + threadIdx.x;
+  if (tile >= n) return;
+  const int S = 65536 >> K;
+  const int16_t* te = temp_edges + (size_t)tile * L * S;
+  if (!write_output) {
+    const uint16_t* c = temp_costs + ((size_t)tile * 2 + cost_slot) * S;
+    uint32_t key = 0xFFFFFFFFu;
+    for (int e = 0; e < S; ++e) {
+      const uint32_t b = c[e];
+      if ((b & 0x7C00u) != 0x7C00u) key = min(key, (b << 16) | (uint32_t)e);
+    }
+    int edge = key == 0xFFFFFFFFu ? 0 : (int)(key & 0xFFFFu);
+    for (int i = L - 1; i >= 0; --i) {
+      int ri = i + roll;
+      if (ri >= L) ri -= L;
+      edge = (uint16_t)te[(size_t)ri * S + edge];
+      if (ri == 0) break;
+    }
+    end_states[tile] = edge;
+  } else {
+    int edge = end_states[tile];
+    for (int i = L - 1; i >= 0; --i) {
+      int ri = i + roll;
+      if (ri >= L) ri -= L;
+      const int prev = (uint16_t)te[(size_t)ri * S + edge];
+      const uint16_t s = (uint16_t)((prev << K) | edge);
+      edge = prev;
+      out_idx[(size_t)tile * L + ri] = (int16_t)s;
+      out_w[(size_t)tile * L + ri] = half_bits_to_float(cb_state_bits(cb, s));
+    }
+  }
+}
+
+__global__ void decode_codebook_kernel(int cb, uint16_t* __restrict__ out) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s < 65536) out[s] = cb_state_bits(cb, (uint32_t)s);
+}
+
+__global__ void pack_kernel(const int16_t* __restrict__ states, int16_t* __restrict__ packed,
+                            int n, int K) {
+  __shared__ uint16_t st[kTbWarps][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x * kTbWarps + warp;
+  if (tile >= n) return;
+  for (int i = lane; i < 256; i += 32) st[warp][i] = (uint16_t)states[(size_t)tile * 256 + i];
+  __syncwarp();
+  if (lane < 16) pack_span(st[warp], K, lane, packed + (size_t)tile * 16 * K);
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+namespace {
+
+// Optional launch timing (diagnostics): when enabled, every encoder launch is
+// bracketed by events on its own stream; exl3_timing_end resolves them.
+struct TimedLaunch {
+  int kind;  // 0 = ACS pass, 1 = traceback
+  cudaEvent_t start, stop;
+};
+std::mutex g_timing_mu;
+bool g_timing_on = false;
+std::vector<TimedLaunch> g_timed;
+
+struct LaunchTimer {
+  cudaStream_t s;
+  int kind;
+  cudaEvent_t a = nullptr, b = nullptr;
+  LaunchTimer(cudaStream_t stream, int k) : s(stream), kind(k) {
+    std::lock_guard<std::mutex> g(g_timing_mu);
+    if (!g_timing_on) return;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    cudaEventRecord(a, s);
+  }
+  ~LaunchTimer() {
+    if (!a) return;
+    cudaEventRecord(b, s);
+    std::lock_guard<std::mutex> g(g_timing_mu);
+    g_timed.push_back({kind, a, b});
+  }
+};
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+inline size_t tile_bp_bytes(int K, int L) { return align_up((size_t)L * bp_step_bytes(K)); }
+inline size_t tile_ws_bytes(int K, int L) { return tile_bp_bytes(K, L) + 8; }
+
+int validate(int K, int cb, int L) {
+  EXL3_REQUIRE(K >= 1 && K <= 8, "K must be in 1..8, got %d", K);
+  EXL3_REQUIRE(cb >= 0 && cb <= 2, "cb must be 0, 1 or 2, got %d", cb);
+  EXL3_REQUIRE(L == 256 || L == 160, "tile length L must be 256 or 160, got %d", L);
+  EXL3_REQUIRE(L != 160 || cb == 2, "tile length L=160 is only supported with mul1 (cb=2)");
+  return EXL3_OK;
+}
+
+template <int K>
+int set_smem_attrs() {
+  static int done_mask = 0;  // one bit per device (up to 32)
+  int dev = 0;
+  EXL3_CUDA(cudaGetDevice(&dev));
+  if (dev < 32 && (done_mask & (1 << dev))) return EXL3_OK;
+  const int bytes = (int)Smem<K>::bytes;
+  EXL3_CUDA(cudaFuncSetAttribute(acs_kernel<K, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  EXL3_CUDA(cudaFuncSetAttribute(acs_kernel<K, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  EXL3_CUDA(cudaFuncSetAttribute(acs_ref_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  if (dev < 32) done_mask |= (1 << dev);
+  return EXL3_OK;
+}
+
+template <int K>
+int encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t* out_packed,
+                  float* out_cost, int64_t n, int cb, int L, uint8_t* ws, size_t ws_bytes,
+                  cudaStream_t stream) {
+  int rc = set_smem_attrs<K>();
+  if (rc) return rc;
+  const size_t per_tile = tile_ws_bytes(K, L);
+  int64_t cap = (int64_t)(ws_bytes / per_tile);
+  EXL3_REQUIRE(cap >= 1, "workspace of %zu bytes is smaller than one tile (%zu bytes)",
+               ws_bytes, per_tile);
+  if (cap > n) cap = n;
+  if (cap > (1 << 30)) cap = 1 << 30;
+  const size_t bp_tile = tile_bp_bytes(K, L);
+  uint8_t* bp = ws;
+  int32_t* best_edge = reinterpret_cast<int32_t*>(ws + (size_t)cap * bp_tile);
+  int32_t* end_state = best_edge + cap;
+  const int sms = sm_count();
+  for (int64_t start = 0; start < n; start += cap) {
+    const int m = (int)((n - start) < cap ? (n - start) : cap);
+    const float* cin = in + start * L;
+    const int grid = m < sms ? m : sms;
+    {
+      LaunchTimer lt(stream, 0);
+      acs_kernel<K, 1><<<grid, kNT, Smem<K>::bytes, stream>>>(
+          cin, m, L, cb, bp, bp_tile, best_edge, nullptr, nullptr, nullptr);
+    }
+    EXL3_LAUNCHED();
+    {
+      LaunchTimer lt(stream, 1);
+      tb1_kernel<K><<<(m + 127) / 128, 128, 0, stream>>>(bp, bp_tile, m, L, best_edge, end_state);
+    }
+    EXL3_LAUNCHED();
+    {
+      LaunchTimer lt(stream, 0);
+      acs_kernel<K, 2><<<grid, kNT, Smem<K>::bytes, stream>>>(
+          cin, m, L, cb, bp, bp_tile, nullptr, end_state, out_cost ? out_cost + start : nullptr,
+          nullptr);
+    }
+    EXL3_LAUNCHED();
+    {
+      LaunchTimer lt(stream, 1);
+      tb2_kernel<K><<<(m + kTbWarps - 1) / kTbWarps, 32 * kTbWarps, 0, stream>>>(
+          bp, bp_tile, m, L, cb, end_state, out_w + start * L, out_idx + start * L,
+          out_packed ? out_packed + start * 16 * K : nullptr);
+    }
+    EXL3_LAUNCHED();
+  }
+  return EXL3_OK;
+}
+
+template <int K>
+int forward_ref_layout(const float* in, uint16_t* temp_costs, int16_t* temp_edges,
+                       const int32_t* pre_states, int64_t n, int cb, int L, int roll,
+                       int cost_slot, cudaStream_t stream) {
+  int rc = set_smem_attrs<K>();
+  if (rc) return rc;
+  const int sms = sm_count();
+  const int grid = n < sms ? (int)n : sms;
+  acs_ref_kernel<K><<<grid, kNT, Smem<K>::bytes, stream>>>(
+      in, (int)n, L, cb, roll, pre_states, temp_edges, temp_costs, cost_slot);
+  EXL3_LAUNCHED();
+  return EXL3_OK;
+}
+
+}  // namespace
+}  // namespace exl3
+
+using namespace exl3;
+
+#define EXL3_DISPATCH_K(K, FN, ...)                     \
+  switch (K) {                                          \
+    case 1: return FN<1>(__VA_ARGS__);                  \
+    case 2: return FN<2>(__VA_ARGS__);                  \
+    case 3: return FN<3>(__VA_ARGS__);                  \
+    case 4: return FN<4>(__VA_ARGS__);                  \
+    case 5: return FN<5>(__VA_ARGS__);                  \
+    case 6: return FN<6>(__VA_ARGS__);                  \
+    case 7: return FN<7>(__VA_ARGS__);                  \
+    case 8: return FN<8>(__VA_ARGS__);                  \
+    default: set_error("K must be in 1..8, got %d", K); \
+      return EXL3_EINVAL;                               \
+  }
+
+extern "C" int exl3_decode_codebook(int cb, uint16_t* out_lut, exl3_stream_t stream) {
+  EXL3_REQUIRE(cb >= 0 && cb <= 2, "cb must be 0, 1 or 2, got %d", cb);
+  EXL3_REQUIRE(out_lut != nullptr, "out_lut is NULL");
+  decode_codebook_kernel<<<256, 256, 0, (cudaStream_t)stream>>>(cb, out_lut);
+  EXL3_LAUNCHED();
+  return EXL3_OK;
+}
+
+extern "C" size_t exl3_quantize_tiles_ws_bytes(int64_t n, int K, int L) {
+  if (K < 1 || K > 8 || n < 0 || (L != 256 && L != 160)) return 0;
+  return (size_t)n * tile_ws_bytes(K, L);
+}
+
+extern "C" int exl3_quantize_tiles(const float* in, float* out_w, int16_t* out_idx,
+                                   int16_t* out_packed, float* out_cost, int64_t n, int K,
+                                   int cb, int L, void* ws, size_t ws_bytes,
+                                   exl3_stream_t stream) {
+  int rc = validate(K, cb, L);
+  if (rc) return rc;
+  EXL3_REQUIRE(n > 0, "num_tiles must be positive, got %lld", (long long)n);
+  EXL3_REQUIRE(n <= (int64_t)1 << 31, "num_tiles %lld too large", (long long)n);
+  EXL3_REQUIRE(in && out_w && out_idx, "input/output pointers must be non-NULL");
+  EXL3_REQUIRE(ws != nullptr, "workspace is NULL");
+  EXL3_REQUIRE(out_packed == nullptr || L == 256, "packed output requires L=256");
+  EXL3_DISPATCH_K(K, encode_chunks, in, out_w, out_idx, out_packed, out_cost, n, cb, L,
+                  static_cast<uint8_t*>(ws), ws_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int exl3_forward_pass_ref_layout(const float* in, uint16_t* temp_costs,
+                                            int16_t* temp_edges, const int32_t* pre_states,
+                                            int64_t n, int K, int cb, int L, int roll,
+                                            int cost_slot, exl3_stream_t stream) {
+  int rc = validate(K, cb, L);
+  if (rc) return rc;
+  EXL3_REQUIRE(n > 0, "num_tiles must be positive");
+  EXL3_REQUIRE(cost_slot == 0 || cost_slot == 1, "cost_slot must be 0 or 1");
+  EXL3_REQUIRE(roll >= 0 && roll < L, "roll must be in [0, L)");
+  EXL3_REQUIRE(in && temp_costs && temp_edges && pre_states, "NULL pointer argument");
+  EXL3_DISPATCH_K(K, forward_ref_layout, in, temp_costs, temp_edges, pre_states, n, cb, L,
+                  roll, cost_slot, (cudaStream_t)stream);
+}
+
+extern "C" int exl3_backward_pass_ref_layout(const uint16_t* temp_costs,
+                                             const int16_t* temp_edges, float* out_w,
+                                             int16_t* out_idx, int32_t* end_states,
+                                             int64_t n, int K, int cb, int L, int roll,
+                                             int cost_slot, int write_output,
+                                             exl3_stream_t stream) {
+  int rc = validate(K, cb, L);
+  if (rc) return rc;
+  EXL3_REQUIRE(n > 0, "num_tiles must be positive");
+  EXL3_REQUIRE(cost_slot == 0 || cost_slot == 1, "cost_slot must be 0 or 1");
+  EXL3_REQUIRE(roll >= 0 && roll < L, "roll must be in [0, L)");
+  EXL3_REQUIRE(temp_costs && temp_edges && end_states, "NULL pointer argument");
+  EXL3_REQUIRE(!write_output || (out_w && out_idx), "outputs required when write_output");
+  ref_backward_kernel<<<(int)((n + 127) / 128), 128, 0, (cudaStream_t)stream>>>(
+      temp_costs, temp_edges, out_w, out_idx, end_states, (int)n, K, cb, L, roll, cost_slot,
+      write_output);
+  EXL3_LAUNCHED();
+  return EXL3_OK;
+}
+
+extern "C" int exl3_pack_trellis(const int16_t* states, int16_t* packed, int64_t n, int K,
+                                 exl3_stream_t stream) {
+  EXL3_REQUIRE(K >= 1 && K <= 8, "K must be in 1..8, got %d", K);
+  EXL3_REQUIRE(n > 0 && states && packed, "bad arguments");
+  pack_kernel<<<(int)((n + kTbWarps - 1) / kTbWarps), 32 * kTbWarps, 0, (cudaStream_t)stream>>>(
+      states, packed, (int)n, K);
+  EXL3_LAUNCHED();
+  return EXL3_OK;
+}
+
+extern "C" int exl3_timing_begin(void) {
+  std::lock_guard<std::mutex> g(g_timing_mu);
+  for (auto& t : g_timed) {
+    cudaEventDestroy(t.start);
+    cudaEventDestroy(t.stop);
+  }
+  g_timed.clear();
+  g_timing_on = true;
+  return EXL3_OK;
+}
+
+extern "C" int exl3_timing_end(double* acs_ms, double* traceback_ms, int64_t* acs_launches,
+                               int64_t* total_launches) {
+  std::vector<TimedLaunch> v;
+  {
+    std::lock_guard<std::mutex> g(g_timing_mu);
+    g_timing_on = false;
+    v.swap(g_timed);
+  }
+  double a = 0.0, b = 0.0;
+  int64_t na = 0;
+  int rc = EXL3_OK;
+  for (auto& t : v) {
+    float ms = 0.f;
+    if (cudaEventSynchronize(t.stop) != cudaSuccess ||
+        cudaEventElapsedTime(&ms, t.start, t.stop) != cudaSuccess) {
+      set_error("timing event failed");
+      rc = EXL3_ECUDA;
+    }
+    if (t.kind == 0) {
+      a += ms;
+      ++na;
+    } else {
+      b += ms;
+    }
+    cudaEventDestroy(t.start);
+    cudaEventDestroy(t.stop);
+  }
+  if (acs_ms) *acs_ms = a;
+  if (traceback_ms) *traceback_ms = b;
+  if (acs_launches) *acs_launches = na;
+  if (total_launches) *total_launches = (int64_t)v.size();
+  return rc;
+}

@@ -1,0 +1,149 @@
+/*
+ * exl3k.h — C ABI of libexl3k, the B200 (sm_100a) kernels behind the EXL3
+ * conversion hot path: the 16x16-tile trellis Viterbi encoder, the LDLQ
+ * block-feedback helpers and the Hessian calibration accumulation.
+ *
+ * Conventions (mirroring the reference op binding
+ * csrc/quantize_xpu/quantize_xpu.cpp:73-101 of alpha2beta/EXL3_Intel_Arc_quantizer):
+ *   - the caller owns every buffer; all pointers are device pointers on the
+ *     current CUDA device unless a parameter says "host";
+ *   - work is enqueued asynchronously on `stream` (NULL = legacy default
+ *     stream); no entry point synchronizes the host;
+ *   - every entry point returns 0 on success and a negative status otherwise;
+ *     exl3_last_error() returns a thread-local description of the last
+ *     failure. No C++ exception crosses this boundary.
+ *
+ * Codebook selectors follow the reference: 0 = 3INST, 1 = MCG, 2 = MUL1
+ * (exl3_quant/trellis_format.py:33).
+ */
+#ifndef EXL3K_H
+#define EXL3K_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* exl3_stream_t; /* == cudaStream_t */
+
+enum {
+  EXL3_OK = 0,
+  EXL3_EINVAL = -22,   /* bad argument (shape, K, codebook, pointer) */
+  EXL3_ENOMEM = -12,   /* workspace too small for even one tile */
+  EXL3_ECUDA = -5,     /* a CUDA runtime call failed */
+  EXL3_ENOTSUP = -95   /* configuration not supported on this device */
+};
+
+/* Description of the last failure on the calling host thread. */
+const char* exl3_last_error(void);
+
+/* Library version string. */
+const char* exl3_version(void);
+
+/* ------------------------------------------------------------------ */
+/* Trellis encoder                                                     */
+/* ------------------------------------------------------------------ */
+
+/*
+ * Decode all 65536 states of codebook `cb` into fp16 bit patterns.
+ * Replaces decode_codebook(cb, out_lut) (quantize_xpu.cpp:105-110,
+ * kernel quantize_kernels.sycl:51-73 / 236-243).
+ */
+int exl3_decode_codebook(int cb, uint16_t* out_lut, exl3_stream_t stream);
+
+/*
+ * Bytes of device workspace needed to encode `n` tiles in one chunk.
+ * A smaller workspace is accepted by exl3_quantize_tiles, which then
+ * processes the tiles in chunks of floor(ws_bytes / per-tile bytes).
+ */
+size_t exl3_quantize_tiles_ws_bytes(int64_t n, int K, int L);
+
+/*
+ * Fused two-pass tail-biting Viterbi encode of `n` tiles of length L
+ * (256, or 160 with cb = MUL1), K bits per weight (1..8).
+ * Replaces quantize_tiles(...) (quantize_xpu.cpp:112-167) and the fused
+ * kernel FusedQuantizeKernel (quantize_kernels.sycl:245-360).
+ *
+ *   in          (n, L) float32, tile elements in encoder (tensor-core) order;
+ *               each value is rounded to fp16 (round-to-nearest-even)
+ *   out_w       (n, L) float32 reconstruction = codebook(state)
+ *   out_idx     (n, L) int16 bit patterns of the 16-bit trellis states
+ *   out_packed  (n, 16*K) int16, EXL3 bitstream words after SWAP16
+ *               (trellis_format.pack_trellis + swap16_storage); may be NULL;
+ *               only for L = 256
+ *   out_cost    (n) float32 fp16 path cost of the emitted path; may be NULL
+ *   ws          device workspace of ws_bytes bytes (see _ws_bytes)
+ */
+int exl3_quantize_tiles(const float* in, float* out_w, int16_t* out_idx,
+                        int16_t* out_packed, float* out_cost, int64_t n, int K,
+                        int cb, int L, void* ws, size_t ws_bytes,
+                        exl3_stream_t stream);
+
+/*
+ * Reference-layout split passes, kept for the traceback placements of the
+ * reference encoder (gpu_resident_split / d2h_cpu). They exchange the
+ * reference's own scratch layout:
+ *   temp_costs (B, 2, S) fp16 and temp_edges (B, L, S) int16 predecessor
+ *   edges, S = 65536 >> K.
+ *
+ * Forward ACS pass over n <= B tiles with ring rotation `roll` and wrap
+ * constraint pre_states[t] (-1 = none); writes every step's predecessor
+ * into temp_edges and the final costs into temp_costs[:, cost_slot].
+ * Replaces quantize_tiles_forward_pass (quantize_xpu.cpp:169-215).
+ */
+int exl3_forward_pass_ref_layout(const float* in, uint16_t* temp_costs,
+                                 int16_t* temp_edges, const int32_t* pre_states,
+                                 int64_t n, int K, int cb, int L, int roll,
+                                 int cost_slot, exl3_stream_t stream);
+
+/*
+ * Traceback over the reference scratch layout. write_output = 0: argmin of
+ * temp_costs[:, cost_slot] then walk back to ring index 0, writing
+ * end_states. write_output = 1: walk back from end_states writing out_w and
+ * out_idx. Replaces quantize_tiles_backward_pass (quantize_xpu.cpp:217-259).
+ */
+int exl3_backward_pass_ref_layout(const uint16_t* temp_costs,
+                                  const int16_t* temp_edges, float* out_w,
+                                  int16_t* out_idx, int32_t* end_states,
+                                  int64_t n, int K, int cb, int L, int roll,
+                                  int cost_slot, int write_output,
+                                  exl3_stream_t stream);
+
+/*
+ * Pack 16-bit states into the EXL3 container on the device:
+ * states (n, 256) int16 -> packed (n, 16*K) int16 (pack_trellis + SWAP16,
+ * trellis_format.py:120-174).
+ */
+int exl3_pack_trellis(const int16_t* states, int16_t* packed, int64_t n, int K,
+                      exl3_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* Diagnostics                                                         */
+/* ------------------------------------------------------------------ */
+
+/*
+ * Measured packed-fp16 FMA throughput of the current device (fp16 operations
+ * per second, one fma.rn.f16x2 = 2). Synchronizes `stream`. The encoder's
+ * add-compare-select runs on this pipe, so this is its roofline denominator.
+ * No counterpart in the reference (its roofline had no measured peak).
+ */
+int exl3_probe_fp16x2_rate(double* fp16_ops_per_s, exl3_stream_t stream);
+
+/*
+ * Launch timing for benchmarks (off by default). After exl3_timing_begin,
+ * every encoder kernel launch is bracketed by CUDA events on its own stream;
+ * exl3_timing_end synchronizes those events and returns the summed device
+ * time of the ACS passes and of the tracebacks, and the launch counts.
+ * No counterpart in the reference.
+ */
+int exl3_timing_begin(void);
+int exl3_timing_end(double* acs_ms, double* traceback_ms, int64_t* acs_launches,
+                    int64_t* total_launches);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXL3K_H */

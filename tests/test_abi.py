@@ -1,0 +1,102 @@
+"""The C-ABI library loads, exports every symbol its headers declare, and its
+host-side argument checks return the documented status codes (no GPU work is
+issued: validation happens before any CUDA call)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from exl3_intel_arc_quantizer_b200 import _build, _ext
+
+REPO = Path(__file__).resolve().parent.parent
+EINVAL, ENOMEM = -22, -12
+
+
+def declared_symbols():
+    names = set()
+    for h in (REPO / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names.update(re.findall(r"\b(exl3_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
+
+
+def test_library_builds_and_exports_every_declared_symbol():
+    lib = _ext.lib()
+    syms = declared_symbols()
+    assert "exl3_quantize_tiles" in syms and "exl3_last_error" in syms
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_library_is_sm100a_only_build():
+    assert "arch=compute_100a,code=sm_100a" in " ".join(_build.NVCC_FLAGS)
+    assert _ext.lib().exl3_version().decode().endswith("(sm_100a)")
+
+
+def test_workspace_size_formula():
+    from exl3_intel_arc_quantizer_b200.scratch_estimator import b200_workspace_bytes
+
+    lib = _ext.lib()
+    for K in range(1, 9):
+        for L in (256, 160):
+            assert lib.exl3_quantize_tiles_ws_bytes(7, K, L) == b200_workspace_bytes(K, L, 7)
+    assert lib.exl3_quantize_tiles_ws_bytes(1, 2, 256) == 256 * 4096 + 8  # 1 MiB of K=2 backpointers
+    assert lib.exl3_quantize_tiles_ws_bytes(1, 9, 256) == 0
+    assert lib.exl3_quantize_tiles_ws_bytes(1, 2, 128) == 0
+
+
+def test_argument_errors_return_status_and_message():
+    lib = _ext.lib()
+    f = lib.exl3_quantize_tiles
+    f.restype = ctypes.c_int
+    P = ctypes.c_void_p
+    f.argtypes = [P, P, P, P, P, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, P,
+                  ctypes.c_size_t, P]
+    dummy = P(16)
+    assert f(dummy, dummy, dummy, None, None, 4, 9, 2, 256, dummy, 1 << 20, None) == EINVAL
+    assert b"K must be in 1..8" in lib.exl3_last_error()
+    assert f(dummy, dummy, dummy, None, None, 4, 2, 1, 160, dummy, 1 << 20, None) == EINVAL
+    assert b"L=160" in lib.exl3_last_error()
+    assert f(dummy, dummy, dummy, None, None, 0, 2, 2, 256, dummy, 1 << 20, None) == EINVAL
+    assert f(dummy, dummy, dummy, None, None, 4, 2, 2, 256, None, 1 << 20, None) == EINVAL
+    assert f(dummy, dummy, dummy, dummy, None, 4, 2, 2, 160, dummy, 1 << 20, None) == EINVAL
+    g = lib.exl3_decode_codebook
+    g.restype = ctypes.c_int
+    g.argtypes = [ctypes.c_int, P, P]
+    assert g(3, dummy, None) == EINVAL
+
+
+def test_torch_binding_loads_and_validates_on_cpu_tensors():
+    import torch
+
+    e = _ext.ext()
+    for name in ("quantize_tiles", "quantize_tiles_forward_pass", "quantize_tiles_backward_pass",
+                 "decode_codebook", "encode_tiles", "pack_trellis"):
+        assert hasattr(e, name)
+    x = torch.zeros((1, 256))
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        e.quantize_tiles(x, x, torch.zeros((1, 256), dtype=torch.int16),
+                         torch.zeros((1, 2, 16384), dtype=torch.float16),
+                         torch.zeros((1, 256, 16384), dtype=torch.int16), 2, False, True)
+    with pytest.raises(RuntimeError, match="ambiguous codebook"):
+        e.quantize_tiles(x, x, torch.zeros((1, 256), dtype=torch.int16),
+                         torch.zeros((1, 2, 16384), dtype=torch.float16),
+                         torch.zeros((1, 256, 16384), dtype=torch.int16), 2, True, True)
+
+
+def test_product_has_no_cpu_encoder_path():
+    """Without a CUDA device the encoder raises instead of computing on the host."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("CUDA present")
+    import numpy as np
+
+    from exl3_intel_arc_quantizer_b200.xpu_quantizer import XPUTrellisEncoder
+
+    with pytest.raises(RuntimeError, match="no CUDA device"):
+        XPUTrellisEncoder(K=2).encode_tile(np.zeros(256, np.float32))

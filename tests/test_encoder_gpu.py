@@ -1,0 +1,254 @@
+"""GPU parity of the B200 trellis encoder (bit-exact integer/fp16 results).
+
+Mirrors the reference's device tests (tests/test_xpu_quantizer.py): codebook
+on device, bit-exact parity over K x codebooks, L=160, edge cases, partial
+chunks, validation, stream ordering, every traceback placement, plus
+reference-derived golden vectors and full-size (65,536-tile) properties.
+All device work goes through the C ABI (libexl3k) via the PyTorch binding.
+"""
+
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from exl3_intel_arc_quantizer_b200 import trellis_format as tf  # noqa: E402
+from exl3_intel_arc_quantizer_b200._ext import ext  # noqa: E402
+from exl3_intel_arc_quantizer_b200.xpu_quantizer import (  # noqa: E402
+    EncodingResult,
+    ScratchArena,
+    XPUTrellisEncoder,
+    verify_tile_encoding_quality,
+)
+from oracle.trellis_oracle import COracle  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _golden_input(enc_golden, case):
+    tiles = enc_golden[f"{case['name']}/tiles"]
+    return tiles[:, tf.tensor_core_perm()] if case["pre_permute"] else tiles
+
+
+def test_codebook_bit_exact_on_device():
+    for cb in (0, 1, 2):
+        out = torch.empty(65536, dtype=torch.float16, device=DEV)
+        ext().decode_codebook(cb, out)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy().view(np.uint16),
+                                      tf.codebook_lut(cb).view(np.uint16))
+
+
+def test_every_golden_case_bit_exact(manifest, enc_golden):
+    """Reference-encoded tiles (all K, codebooks, L, edge/non-finite cases)."""
+    for case in manifest["encoder"]:
+        name = case["name"]
+        enc = XPUTrellisEncoder(K=case["K"], cb=case["cb"], tile_len=case["L"])
+        x = torch.from_numpy(_golden_input(enc_golden, case)).to(DEV)
+        w, i, packed, cost = enc.encode_device(x)
+        torch.cuda.synchronize()
+        idx = i.cpu().numpy().view(np.uint16)
+        np.testing.assert_array_equal(idx, enc_golden[f"{name}/indices"], err_msg=name)
+        np.testing.assert_array_equal(w.cpu().numpy().astype(np.float16).view(np.uint16),
+                                      enc_golden[f"{name}/recon_perm"], err_msg=name)
+        np.testing.assert_array_equal(
+            np.float16(cost.cpu().numpy()).view(np.uint16), enc_golden[f"{name}/path_cost"],
+            err_msg=name)
+        mask = (65536 >> case["K"]) - 1
+        np.testing.assert_array_equal(idx[:, -1] & mask, enc_golden[f"{name}/end_state"])
+        if case["L"] == 256:
+            np.testing.assert_array_equal(packed.cpu().numpy().view(np.uint16),
+                                          enc_golden[f"{name}/packed"], err_msg=name)
+        enc.arena.release()
+
+
+def test_parity_across_k_and_codebooks_reference_recipe(manifest, enc_golden):
+    """test_xpu_quantizer.py:88-115 through encode_tile (pre_permute=True)."""
+    for case in manifest["encoder"]:
+        if not case["name"].startswith("parity_"):
+            continue
+        name = case["name"]
+        tile = enc_golden[f"{name}/tiles"][0]
+        enc = XPUTrellisEncoder(K=case["K"], cb=case["cb"])
+        try:
+            got = enc.encode_tile(tile)
+        finally:
+            enc.arena.release()
+        np.testing.assert_array_equal(got.output_indices, enc_golden[f"{name}/indices"][0])
+        np.testing.assert_array_equal(got.reconstructed.view(np.uint16),
+                                      enc_golden[f"{name}/recon"][0])
+        np.testing.assert_array_equal(got.packed, enc_golden[f"{name}/packed"][0])
+        assert got.end_state == enc_golden[f"{name}/end_state"][0]
+        assert np.float16(got.path_cost).view(np.uint16) == enc_golden[f"{name}/path_cost"][0]
+        assert abs(got.distortion - enc_golden[f"{name}/distortion"][0]) < 1e-5
+
+
+@pytest.mark.parametrize("K", [1, 2, 3, 4, 5, 6, 7, 8])
+def test_random_batch_matches_c_oracle(K):
+    """BASELINE config-2 distribution (N(0,1) x LogNormal(0,0.5) row scales)."""
+    n = 96 if K <= 6 else 48
+    rng = np.random.default_rng(4000 + K)
+    base = rng.standard_normal((n, 16, 16), dtype=np.float32)
+    scale = np.exp(0.5 * rng.standard_normal((n, 16, 1))).astype(np.float32)
+    tiles = (base * scale).reshape(n, 256)
+    enc = XPUTrellisEncoder(K=K, cb=tf.CB_MUL1)
+    w, i, packed, cost = enc.encode_device(torch.from_numpy(tiles).to(DEV))
+    ref = COracle(K, tf.CB_MUL1).encode_batch(tiles)
+    np.testing.assert_array_equal(i.cpu().numpy().view(np.uint16), ref["indices"])
+    np.testing.assert_array_equal(packed.cpu().numpy().view(np.uint16), ref["packed"])
+    np.testing.assert_array_equal(np.float16(cost.cpu().numpy()).view(np.uint16),
+                                  ref["path_cost"].view(np.uint16))
+    enc.arena.release()
+
+
+def test_chunked_workspace_matches_single_chunk():
+    """Partial chunks: 19 tiles through a workspace of 6 (chunks 6,6,6,1)."""
+    rng = np.random.default_rng(555)
+    tiles = rng.normal(0.0, 1.0, size=(19, 256)).astype(np.float32)
+    enc = XPUTrellisEncoder(K=3, cb=tf.CB_MUL1, wave_cap_override=4)
+    bd = enc.encode_batch_detailed(tiles, requested_b=6)
+    assert bd.admitted_b == 6 and bd.num_chunks == 4 and len(bd.results) == 19
+    ref = COracle(3, tf.CB_MUL1).encode_batch(tiles[:, tf.tensor_core_perm()])
+    for t, r in enumerate(bd.results):
+        np.testing.assert_array_equal(r.output_indices, ref["indices"][t])
+        np.testing.assert_array_equal(tf.decode_states(r.packed, 3), r.output_indices)
+        np.testing.assert_array_equal(tf.decode_tile_values(r.packed, 3).view(np.uint16),
+                                      r.reconstructed.view(np.uint16))
+    enc.arena.release()
+
+
+def test_all_traceback_modes_agree():
+    rng = np.random.default_rng(909)
+    tiles = rng.normal(0.0, 1.1, size=(4, 256)).astype(np.float32)
+    ref = COracle(2, tf.CB_MUL1).encode_batch(tiles[:, tf.tensor_core_perm()])
+    for mode in ("gpu_resident", "gpu_resident_split", "d2h_cpu", "usm_host"):
+        for sg in (16, 32):
+            enc = XPUTrellisEncoder(K=2, cb=tf.CB_MUL1, sg_size=sg, force_global_costs=(sg == 16))
+            bd = enc.encode_batch_detailed(tiles, requested_b=4, traceback_mode=mode)
+            enc.arena.release()
+            for t, r in enumerate(bd.results):
+                np.testing.assert_array_equal(r.output_indices, ref["indices"][t], err_msg=mode)
+                assert np.float16(r.path_cost).view(np.uint16) == ref["path_cost"][t].view(np.uint16)
+                np.testing.assert_array_equal(r.packed, ref["packed"][t])
+
+
+def test_forward_pass_reference_layout_matches_audits(manifest, fwd_golden):
+    """quantize_tiles_forward_pass writes the reference's int16 predecessor table."""
+    e = ext()
+    for case in manifest["forward"]:
+        name, K = case["name"], case["K"]
+        S = 65536 >> K
+        w = torch.from_numpy(fwd_golden[f"{name}/w16"].view(np.float16).astype(np.float32)).to(DEV)
+        costs = torch.zeros((1, 2, S), dtype=torch.float16, device=DEV)
+        edges = torch.zeros((1, 256, S), dtype=torch.int16, device=DEV)
+        pre = torch.tensor([case["pre_state"]], dtype=torch.int32, device=DEV)
+        e.quantize_tiles_forward_pass(w[None, :], costs, edges, pre, K, False, True,
+                                      case["roll"], 1)
+        torch.cuda.synchronize()
+        got_edges = edges[0].cpu().numpy().view(np.uint16)
+        assert hashlib.sha256(got_edges.tobytes()).hexdigest() == case["edges_sha256"], name
+        np.testing.assert_array_equal(costs[0, 1].cpu().numpy().view(np.uint16),
+                                      fwd_golden[f"{name}/costs"], err_msg=name)
+
+
+def test_quantize_tiles_reference_op_and_validation():
+    e = ext()
+    rng = np.random.default_rng(808)
+    raw = rng.normal(0.0, 0.5, size=(4, 256)).astype(np.float16).astype(np.float32)
+    in_t = torch.from_numpy(raw).to(DEV)
+    in_t.mul_(2.0)            # queued on the current stream, no host sync
+    out_w = torch.empty_like(in_t)
+    out_i = torch.empty((4, 256), dtype=torch.int16, device=DEV)
+    costs = torch.empty((4, 2, 8192), dtype=torch.float16, device=DEV)
+    edges = torch.empty((4, 256, 8192), dtype=torch.int16, device=DEV)
+    e.quantize_tiles(in_t, out_w, out_i, costs, edges, 3, False, True)
+    out_w.add_(1.0)
+    torch.cuda.synchronize()
+    ref = COracle(3, tf.CB_MUL1).encode_batch(raw * 2.0)
+    np.testing.assert_array_equal(out_i.cpu().numpy().view(np.uint16), ref["indices"])
+    np.testing.assert_allclose(out_w.cpu().numpy(), ref["recon"].astype(np.float32) + 1.0,
+                               atol=1e-5)
+    with pytest.raises(RuntimeError):
+        e.quantize_tiles(in_t, out_w, out_i, costs, edges, 3, True, True)
+    with pytest.raises(RuntimeError):
+        e.quantize_tiles(in_t.cpu(), out_w, out_i, costs, edges, 3, False, True)
+    with pytest.raises(RuntimeError):
+        e.quantize_tiles(in_t, out_w, out_i, costs, edges, 2, False, True)   # S mismatch
+    with pytest.raises(RuntimeError):
+        e.quantize_tiles(in_t, out_w, out_i, costs, edges, 3, False, True, 8)  # sg_size
+
+
+def test_encoder_validation():
+    with pytest.raises(ValueError):
+        XPUTrellisEncoder(K=0)
+    with pytest.raises(ValueError):
+        XPUTrellisEncoder(K=9)
+    with pytest.raises(ValueError):
+        XPUTrellisEncoder(K=2, cb=99)
+    with pytest.raises(ValueError):
+        XPUTrellisEncoder(K=2, tile_len=128)
+    with pytest.raises(ValueError):
+        XPUTrellisEncoder(K=2, cb=tf.CB_MCG, tile_len=160)
+    with pytest.raises(ValueError):
+        XPUTrellisEncoder(K=2, sg_size=8)
+    enc = XPUTrellisEncoder(K=2)
+    with pytest.raises(ValueError):
+        enc.encode_tile(np.zeros(100, dtype=np.float32))
+    with pytest.raises(ValueError):
+        enc.encode_batch(np.zeros((0, 256), dtype=np.float32))
+    with pytest.raises(ValueError):
+        enc.encode_batch(np.zeros((2, 256), dtype=np.float32), traceback_mode="bad")
+
+
+def test_edge_cases_and_tie_verification(enc_golden):
+    tiles = enc_golden["edge_k2/tiles"]
+    enc = XPUTrellisEncoder(K=2)
+    got = enc.encode_batch(tiles)
+    for t, r in enumerate(got):
+        ref = EncodingResult(
+            output_indices=enc_golden["edge_k2/indices"][t],
+            reconstructed=enc_golden["edge_k2/recon"][t].view(np.float16),
+            reconstructed_perm=enc_golden["edge_k2/recon_perm"][t].view(np.float16),
+            packed=enc_golden["edge_k2/packed"][t], end_state=int(enc_golden["edge_k2/end_state"][t]),
+            distortion=float(enc_golden["edge_k2/distortion"][t]), mse=0.0,
+            path_cost=float(enc_golden["edge_k2/path_cost"][t:t + 1].view(np.float16)[0]),
+            K=2, cb=tf.CB_MUL1)
+        chk = verify_tile_encoding_quality(r, ref, cost_atol=0.0)
+        assert chk["passed"] and chk["indices_identical"], chk
+    broken = got[-1]
+    broken.output_indices = broken.output_indices.copy()
+    broken.output_indices[10] ^= 1
+    assert not verify_tile_encoding_quality(broken, got[0])["ring_valid"]
+    enc.arena.release()
+
+
+@pytest.mark.parametrize("K", [2, 4])
+def test_full_size_properties(K):
+    """65,536 LogNormal-scaled tiles (config 2): tail-biting ring closes, every
+    reconstruction is the codebook value of its state, the container decodes
+    to the states, and a random 128-tile sample equals the C oracle."""
+    n = 65536
+    g = torch.Generator(device="cpu").manual_seed(K)
+    base = torch.randn((n, 16, 16), generator=g)
+    scale = torch.exp(0.5 * torch.randn((n, 16, 1), generator=g))
+    tiles = (base * scale).reshape(n, 256).to(DEV)
+    enc = XPUTrellisEncoder(K=K, cb=tf.CB_MUL1)
+    w, i, packed, cost = enc.encode_device(tiles)
+    lut = torch.empty(65536, dtype=torch.float16, device=DEV)
+    ext().decode_codebook(tf.CB_MUL1, lut)
+    st = i.long() & 0xFFFF
+    mask = (65536 >> K) - 1
+    assert bool(((st & mask) == (torch.roll(st, -1, dims=1) >> K)).all())
+    assert torch.equal(lut[st].float(), w)
+    sample = torch.randperm(n, generator=g)[:128]
+    ref = COracle(K, tf.CB_MUL1).encode_batch(tiles[sample.to(DEV)].cpu().numpy())
+    np.testing.assert_array_equal(i[sample.to(DEV)].cpu().numpy().view(np.uint16), ref["indices"])
+    pk = packed.cpu().numpy().view(np.uint16)
+    for t in sample[:16].tolist():
+        np.testing.assert_array_equal(tf.decode_states(pk[t], K), st[t].cpu().numpy())
+    enc.arena.release()
