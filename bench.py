@@ -297,7 +297,7 @@ def run_b200(args):
 
         def one():
             d_in.copy_(host_in, non_blocking=True)
-            e.encode_tiles(d_in, d_w, d_i, d_p, None, ws[: adm * per], K, 2)
+            e.encode_tiles(d_in, d_w, d_i, d_p, None, ws, K, 2)
             h_w.copy_(d_w, non_blocking=True)
             h_i.copy_(d_i, non_blocking=True)
             h_p.copy_(d_p, non_blocking=True)
@@ -338,13 +338,17 @@ def run_b200(args):
         "peak_source": "measured live: exl3_probe_fp16x2_rate (fma.rn.f16x2 at full occupancy)",
         "work": f"{ACS_PER_TILE} candidate ACS/tile x {FP16_OPS_PER_ACS} fp16 ops (sub, fma, "
                 "compare)",
-        "kernel": "exl3::acs_kernel (pass 1 + pass 2)",
+        "kernel": "exl3::acs_pair_kernel (pass 1 + pass 2)" if K >= 2 else
+                  "exl3::acs_kernel (pass 1 + pass 2)",
         "acs_share_of_step": acs_ms.value / max(1e-9, total_ms / max(1, world)),
         "traffic": traffic,
         "traffic_unit": "bytes per launch (ncu dram read+write)",
     }
-    bp_bytes_per_tile = 256 * (4096 if K <= 3 else 2048)
-    roofline["hbm_backpointer_gbs"] = (tiles_timed * bp_bytes_per_tile * 1.5
+    from exl3_intel_arc_quantizer_b200.scratch_estimator import b200_backpointer_step_bytes
+
+    bp_bytes_per_tile = 384 * b200_backpointer_step_bytes(K)   # 128 pass-1 + 256 pass-2 steps
+    roofline["backpointer_bytes_per_tile"] = bp_bytes_per_tile
+    roofline["hbm_backpointer_gbs"] = (tiles_timed * bp_bytes_per_tile
                                        / (acs_ms.value / 1e3) / 1e9)
 
     cpu = None

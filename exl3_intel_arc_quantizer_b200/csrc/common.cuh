@@ -63,6 +63,22 @@ __device__ __forceinline__ uint32_t h2_fma(uint32_t a, uint32_t b, uint32_t c) {
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
   return d;
 }
+// {v, v} - w with v the low (HI = false) or high lane of `cb`. One asm block,
+// so the lane broadcast cannot be hoisted away from the subtraction (keeping
+// 128 broadcast copies of a thread's codebook live would exhaust registers).
+template <bool HI>
+__device__ __forceinline__ uint32_t h2_sub_bcast(uint32_t cb, uint32_t w) {
+  uint32_t d;
+  if (HI)
+    asm("{\n\t.reg .b16 l, h;\n\t.reg .b32 v;\n\tmov.b32 {l, h}, %1;\n\t"
+        "mov.b32 v, {h, h};\n\tsub.rn.f16x2 %0, v, %2;\n\t}"
+        : "=r"(d) : "r"(cb), "r"(w));
+  else
+    asm("{\n\t.reg .b16 l, h;\n\t.reg .b32 v;\n\tmov.b32 {l, h}, %1;\n\t"
+        "mov.b32 v, {l, l};\n\tsub.rn.f16x2 %0, v, %2;\n\t}"
+        : "=r"(d) : "r"(cb), "r"(w));
+  return d;
+}
 // IEEE minNum per lane; only used on NaN-free data.
 __device__ __forceinline__ uint32_t h2_min(uint32_t a, uint32_t b) {
   uint32_t d;

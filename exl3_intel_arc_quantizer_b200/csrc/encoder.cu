@@ -29,11 +29,13 @@
 //   * a tile containing NaN switches to the exact compare-and-select form on
 //     every step, which reproduces the reference's NaN stickiness.
 #include "common.cuh"
-
-#include <mutex>
-#include <vector>
+#include "encoder_shared.cuh"
 
 namespace exl3 {
+
+std::mutex g_timing_mu;
+bool g_timing_on = false;
+std::vector<TimedLaunch> g_timed;
 
 constexpr int kNT = 512;  // threads per ACS CTA
 
@@ -63,10 +65,6 @@ __host__ __device__ constexpr int bp_step_bytes(int K) {
   return K == 1 ? Geo<1>::BPS : K == 2 ? Geo<2>::BPS : K == 3 ? Geo<3>::BPS
        : K == 4 ? Geo<4>::BPS : K == 5 ? Geo<5>::BPS : K == 6 ? Geo<6>::BPS
        : K == 7 ? Geo<7>::BPS : Geo<8>::BPS;
-}
-
-__device__ __forceinline__ uint32_t kconst(int k) {
-  return (uint32_t)k | ((uint32_t)k << 16);
 }
 
 // Codebook values of this thread's candidates, packed per edge pair.
@@ -454,30 +452,8 @@ __global__ void tb1_kernel(const uint8_t* __restrict__ bp, size_t bp_tile_bytes,
   end_state[tile] = e;
 }
 
-// EXL3 container for one 16-element span: low K bits of each state,
-// MSB-first, 16 bits per word; written after the SWAP16 half-word exchange
-// (trellis_format.py:120-174).
-__device__ __forceinline__ void pack_span(const uint16_t* st16, int K, int span,
-                                          int16_t* out_tile) {
-  uint32_t acc = 0;
-  int nb = 0, j = K * span;
-  const uint32_t mask = (1u << K) - 1u;
-  for (int i = 0; i < 16; ++i) {
-    acc = (acc << K) | ((uint32_t)st16[16 * span + i] & mask);
-    nb += K;
-    if (nb >= 16) {
-      out_tile[j ^ 1] = (int16_t)((acc >> (nb - 16)) & 0xFFFFu);
-      nb -= 16;
-      acc &= (1u << nb) - 1u;
-      ++j;
-    }
-  }
-}
-
 // Pass-2 traceback: one warp per tile. Lane 0 walks the chain; the warp then
 // writes states, reconstruction and the packed container.
-constexpr int kTbWarps = 4;
-
 template <int K>
 __global__ void tb2_kernel(const uint8_t* __restrict__ bp, size_t bp_tile_bytes, int n,
                            int L, int cb, const int32_t* __restrict__ end_state,
@@ -606,40 +582,13 @@ __global__ void pack_kernel(const int16_t* __restrict__ states, int16_t* __restr
 // ---------------------------------------------------------------------------
 namespace {
 
-// Optional launch timing (diagnostics): when enabled, every encoder launch is
-// bracketed by events on its own stream; exl3_timing_end resolves them.
-struct TimedLaunch {
-  int kind;  // 0 = ACS pass, 1 = traceback
-  cudaEvent_t start, stop;
-};
-std::mutex g_timing_mu;
-bool g_timing_on = false;
-std::vector<TimedLaunch> g_timed;
-
-struct LaunchTimer {
-  cudaStream_t s;
-  int kind;
-  cudaEvent_t a = nullptr, b = nullptr;
-  LaunchTimer(cudaStream_t stream, int k) : s(stream), kind(k) {
-    std::lock_guard<std::mutex> g(g_timing_mu);
-    if (!g_timing_on) return;
-    cudaEventCreate(&a);
-    cudaEventCreate(&b);
-    cudaEventRecord(a, s);
-  }
-  ~LaunchTimer() {
-    if (!a) return;
-    cudaEventRecord(b, s);
-    std::lock_guard<std::mutex> g(g_timing_mu);
-    g_timed.push_back({kind, a, b});
-  }
-};
-
 constexpr size_t kAlign = 256;
 inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 inline size_t tile_bp_bytes(int K, int L) { return align_up((size_t)L * bp_step_bytes(K)); }
-inline size_t tile_ws_bytes(int K, int L) { return tile_bp_bytes(K, L) + 8; }
+inline size_t tile_ws_bytes(int K, int L) {
+  return K >= 2 ? pair_tile_ws_bytes(K, L) : tile_bp_bytes(K, L) + 8;
+}
 
 int validate(int K, int cb, int L) {
   EXL3_REQUIRE(K >= 1 && K <= 8, "K must be in 1..8, got %d", K);
@@ -756,6 +705,8 @@ extern "C" int exl3_decode_codebook(int cb, uint16_t* out_lut, exl3_stream_t str
 
 extern "C" size_t exl3_quantize_tiles_ws_bytes(int64_t n, int K, int L) {
   if (K < 1 || K > 8 || n < 0 || (L != 256 && L != 160)) return 0;
+  // K >= 2 encodes tiles in pairs: an odd count is rounded up to whole pairs
+  if (K >= 2) n = (n + 1) & ~(int64_t)1;
   return (size_t)n * tile_ws_bytes(K, L);
 }
 
@@ -770,8 +721,11 @@ extern "C" int exl3_quantize_tiles(const float* in, float* out_w, int16_t* out_i
   EXL3_REQUIRE(in && out_w && out_idx, "input/output pointers must be non-NULL");
   EXL3_REQUIRE(ws != nullptr, "workspace is NULL");
   EXL3_REQUIRE(out_packed == nullptr || L == 256, "packed output requires L=256");
-  EXL3_DISPATCH_K(K, encode_chunks, in, out_w, out_idx, out_packed, out_cost, n, cb, L,
-                  static_cast<uint8_t*>(ws), ws_bytes, (cudaStream_t)stream);
+  if (K >= 2)
+    return pair_encode(K, in, out_w, out_idx, out_packed, out_cost, n, cb, L,
+                       static_cast<uint8_t*>(ws), ws_bytes, (cudaStream_t)stream);
+  return encode_chunks<1>(in, out_w, out_idx, out_packed, out_cost, n, cb, L,
+                          static_cast<uint8_t*>(ws), ws_bytes, (cudaStream_t)stream);
 }
 
 extern "C" int exl3_forward_pass_ref_layout(const float* in, uint16_t* temp_costs,

@@ -1,0 +1,76 @@
+// Pieces shared by the single-tile (encoder.cu) and tile-pair (acs_pair.cu)
+// encoders: packing epilogue, launch timing, sizes.
+#pragma once
+
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+namespace exl3 {
+
+constexpr int kPairNT = 512;  // threads per tile-pair ACS CTA
+constexpr int kTbWarps = 4;   // tiles (warps) per traceback CTA
+
+__device__ __forceinline__ uint32_t kconst(int k) {
+  return (uint32_t)k | ((uint32_t)k << 16);
+}
+
+// EXL3 container for one 16-element span: low K bits of each state,
+// MSB-first, 16 bits per word; written after the SWAP16 half-word exchange
+// (trellis_format.py:120-174).
+__device__ __forceinline__ void pack_span(const uint16_t* st16, int K, int span,
+                                          int16_t* out_tile) {
+  uint32_t acc = 0;
+  int nb = 0, j = K * span;
+  const uint32_t mask = (1u << K) - 1u;
+  for (int i = 0; i < 16; ++i) {
+    acc = (acc << K) | ((uint32_t)st16[16 * span + i] & mask);
+    nb += K;
+    if (nb >= 16) {
+      out_tile[j ^ 1] = (int16_t)((acc >> (nb - 16)) & 0xFFFFu);
+      nb -= 16;
+      acc &= (1u << nb) - 1u;
+      ++j;
+    }
+  }
+}
+
+// Optional launch timing (diagnostics): when enabled, every encoder launch is
+// bracketed by events on its own stream; exl3_timing_end resolves them.
+struct TimedLaunch {
+  int kind;  // 0 = ACS pass, 1 = traceback
+  cudaEvent_t start, stop;
+};
+extern std::mutex g_timing_mu;
+extern bool g_timing_on;
+extern std::vector<TimedLaunch> g_timed;
+
+struct LaunchTimer {
+  cudaStream_t s;
+  int kind;
+  cudaEvent_t a = nullptr, b = nullptr;
+  LaunchTimer(cudaStream_t stream, int k) : s(stream), kind(k) {
+    std::lock_guard<std::mutex> g(g_timing_mu);
+    if (!g_timing_on) return;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    cudaEventRecord(a, s);
+  }
+  ~LaunchTimer() {
+    if (!a) return;
+    cudaEventRecord(b, s);
+    std::lock_guard<std::mutex> g(g_timing_mu);
+    g_timed.push_back({kind, a, b});
+  }
+};
+
+// tile-pair encoder (acs_pair.cu)
+int pair_bp_step_bytes(int K);
+size_t pair_bp_bytes(int K, int L);       // backpointer bytes of one tile pair
+size_t pair_tile_ws_bytes(int K, int L);  // workspace per tile (half a pair + scalars)
+int pair_encode(int K, const float* in, float* out_w, int16_t* out_idx, int16_t* out_packed,
+                float* out_cost, int64_t n, int cb, int L, uint8_t* ws, size_t ws_bytes,
+                cudaStream_t stream);
+
+}  // namespace exl3

@@ -109,20 +109,29 @@ class ScratchEstimator:
 
 
 def b200_backpointer_step_bytes(k: int) -> int:
-    """Backpointer bytes per trellis step of one tile in the B200 encoder
-    (mirrors ``Geo<K>::BPS`` in csrc/encoder.cu)."""
+    """Backpointer bytes per trellis step of one tile in the B200 encoder.
+
+    K = 1 encodes one tile per CTA (mirrors ``Geo<1>::BPS`` in csrc/encoder.cu);
+    K >= 2 encodes tile pairs, one per fp16 lane, and this is half of the
+    pair's step (``PGeo<K>::BPS`` in csrc/acs_pair.cu)."""
     if not 1 <= k <= 8:
         raise ValueError(f"K must be in 1..8, got {k}")
-    if k >= 7:
-        return (65536 >> k)            # one byte per edge
-    n_pairs = (65536 >> k) // 512 // 2
-    per_word = {1: 16, 2: 8, 3: 4, 4: 4}.get(k, 2)
-    words = -(-n_pairs // per_word)
-    return words * 512 * 4
+    if k == 1:
+        return 2 * 512 * 4
+    if k == 8:
+        return 256 * 4 // 2
+    edges = (65536 >> k) // 512                     # edges per thread
+    per_word = 8 if k == 2 else (4 if k <= 4 else 2)
+    words = -(-edges // per_word)
+    return words * 512 * 4 // 2
 
 
 def b200_workspace_bytes(k: int, t: int = 256, b: int = 1) -> int:
     """Device workspace of the B200 encoder for ``b`` tiles (matches
-    ``exl3_quantize_tiles_ws_bytes``)."""
-    per = -(-(t * b200_backpointer_step_bytes(k)) // 256) * 256 + 8
-    return b * per
+    ``exl3_quantize_tiles_ws_bytes``; K >= 2 rounds ``b`` up to whole pairs)."""
+    if k == 1:
+        per = -(-(t * b200_backpointer_step_bytes(k)) // 256) * 256 + 8
+        return b * per
+    pair = -(-(t * 2 * b200_backpointer_step_bytes(k)) // 256) * 256
+    b = b + (b & 1)
+    return b * (pair // 2 + 8)

@@ -134,7 +134,7 @@ class ScratchArena:
     ``allocator_hook``) fails, the batch halves down to 1 before a
     :class:`MemoryPressureError` is raised. The buffer is a uint8 tensor of
     compact backpointers; ``acquire`` returns ``(workspace, tile_bytes,
-    admitted_b)``.
+    admitted_b)`` where the workspace holds at least ``admitted_b`` tiles.
     """
 
     def __init__(self, policy: Optional[MemoryPolicy] = None, device_index: int = 0,
@@ -160,8 +160,12 @@ class ScratchArena:
         return 0 if self._ws is None else int(self._ws.numel())
 
     @staticmethod
-    def tile_bytes(k: int, tile_len: int = 256) -> int:
-        return int(ext().quantize_tiles_ws_bytes(1, int(k), int(tile_len)))
+    def workspace_bytes(k: int, tile_len: int = 256, b: int = 1) -> int:
+        return int(ext().quantize_tiles_ws_bytes(int(b), int(k), int(tile_len)))
+
+    @classmethod
+    def tile_bytes(cls, k: int, tile_len: int = 256) -> int:
+        return cls.workspace_bytes(k, tile_len, 2) // 2
 
     def _log(self, action, k, tile_len, req, adm, scratch, staging, snap=None):
         import torch
@@ -216,14 +220,14 @@ class ScratchArena:
             self.reuses += 1
             self._log("reuse", k, tile_len, target, target, self.resident_bytes,
                       distinct_staging_bytes)
-            return self._ws[: target * per], per, target
+            return self._ws, per, target
         if self._ws is not None:
             self.evictions += 1
             self.release()
         cand = target
         last_err: Optional[Exception] = None
         while cand >= 1:
-            need = cand * per
+            need = self.workspace_bytes(k, tile_len, cand)
             snap = capture_snapshot(self.device_index)
             ws = None
             try:
@@ -340,7 +344,7 @@ class XPUTrellisEncoder:
         packed = (torch.empty((n, 16 * self.K), dtype=torch.int16, device=dev)
                   if (want_packed and self.L == 256) else None)
         cost = torch.empty(n, dtype=torch.float32, device=dev)
-        ext().encode_tiles(x, out_w, out_i, packed, cost, ws[: admitted * per], self.K, self.cb)
+        ext().encode_tiles(x, out_w, out_i, packed, cost, ws, self.K, self.cb)
         return out_w, out_i, packed, cost
 
     # -- reference API ---------------------------------------------------------
@@ -412,12 +416,14 @@ class XPUTrellisEncoder:
             cost = torch.empty(num_tiles, dtype=torch.float32, device=dev)
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record()
-            ext().encode_tiles(x, out_w, out_i, packed, cost, ws[: admitted * per], self.K,
-                               self.cb)
+            ext().encode_tiles(x, out_w, out_i, packed, cost, ws, self.K, self.cb)
             ev1.record()
             ev1.synchronize()
             t_search = ev0.elapsed_time(ev1) / 1e3
-            chunks = -(-num_tiles // admitted)
+            per_chunk = max(1, int(ws.numel()) // per)
+            if self.K >= 2:
+                per_chunk = max(2, per_chunk & ~1)
+            chunks = -(-num_tiles // min(per_chunk, num_tiles))
 
         t0 = time.perf_counter()
         rec_perm = out_w.cpu().numpy().astype(np.float16)
