@@ -119,6 +119,23 @@ int exl3_backward_pass_ref_layout(const uint16_t* temp_costs,
 int exl3_pack_trellis(const int16_t* states, int16_t* packed, int64_t n, int K,
                       exl3_stream_t stream);
 
+/*
+ * exl3_quantize_tiles without a caller workspace, for callers that cannot
+ * allocate device memory (a host whose GPU memory is owned by another
+ * runtime's pool, or a plain C/FFI host without a device allocator that
+ * must not call cudaMalloc, which synchronizes the device). No counterpart
+ * in the reference. Same arguments and outputs as exl3_quantize_tiles minus
+ * the workspace; the scratch is a fixed 32 MiB + 4 KiB __device__ array held
+ * by every GPU that loads the library, shared by all calls: at most 32 tiles
+ * per call at K=2, L=256 (more at larger K), larger calls return EXL3_EINVAL.
+ * The first call on a device resolves the array's address (make it before
+ * any stream capture); calls that overlap on the GPU race on the scratch.
+ * Allocates nothing (no cudaMalloc/cudaFree).
+ */
+int exl3_quantize_tiles_noalloc(const float* in, float* out_w, int16_t* out_idx,
+                                int16_t* out_packed, float* out_cost, int64_t n, int K,
+                                int cb, int L, exl3_stream_t stream);
+
 /* ------------------------------------------------------------------ */
 /* Diagnostics                                                         */
 /* ------------------------------------------------------------------ */
