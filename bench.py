@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-k4", action="store_true")
+    ap.add_argument("--no-layer", action="store_true")
+    ap.add_argument("--layer-only", action="store_true",
+                    help="only the 4096x4096 K=4 layer measurement (config 3)")
     return ap.parse_args()
 
 
@@ -208,6 +211,65 @@ def run_reference(args):
     return 0
 
 
+def layer_config3(device, seed=0):
+    """W 4096x4096 bf16 N(0, 0.02^2) with 1% outlier
+    columns x8; X 2048x4096 bf16 N(0,1) with 32 outlier channels x20."""
+    import torch
+
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    W = torch.randn(4096, 4096, generator=g) * 0.02
+    W[:, torch.randperm(4096, generator=g)[:41]] *= 8.0
+    X = torch.randn(2048, 4096, generator=g)
+    X[:, torch.randperm(4096, generator=g)[:32]] *= 20.0
+    return W.to(torch.bfloat16).to(device), X.to(torch.bfloat16).to(device)
+
+
+def run_layer(device, K=4, reps=2):
+    """Seconds per 4096x4096 linear layer: Hessian (X^T X, finalize) and
+    quantize_linear_module (regularize, Hadamard, block-LDL, LDLQ with the
+    B200 encoder, reconstruction, metrics), each timed end to end."""
+    import torch
+
+    from exl3_intel_arc_quantizer_b200.calibration import hessian_accumulate_, hessian_finalize_
+    from exl3_intel_arc_quantizer_b200.layer_quant import quantize_linear_module
+    from exl3_intel_arc_quantizer_b200.ldlq import make_xpu_tile_encoder
+
+    W, X = layer_config3(device)
+    enc = make_xpu_tile_encoder(K=K, device_index=device.index or 0)
+    out = {}
+    for rep in range(reps + 1):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        H = torch.zeros(4096, 4096, dtype=torch.float32, device=device)
+        hessian_accumulate_(H, X)
+        hessian_finalize_(H, X.shape[0], 0.01, 1e-7)
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        res = quantize_linear_module("o_proj", W, H, K=K, tile_encoder=enc, skip_g_scale=True,
+                                     buf_size_k=128, block_size=16)
+        torch.cuda.synchronize()
+        t2 = time.perf_counter()
+        if rep > 0:   # first repetition is warm-up
+            out.setdefault("hessian_s", []).append(t1 - t0)
+            out.setdefault("layer_s", []).append(t2 - t1)
+            m = res.metrics
+            out["relative_frobenius_error"] = m.relative_frobenius_error
+            out["normalized_proxy_loss"] = m.normalized_proxy_loss
+            out["retries"] = m.retries
+    enc.encoder.arena.release()
+    return {
+        "workload": "config 3: 4096x4096 bf16 layer, K=4, Hessian from 2048x4096 bf16, "
+                    "skip_g_scale, buf 128, block 16",
+        "seconds_per_layer": min(out["layer_s"]),
+        "hessian_seconds": min(out["hessian_s"]),
+        "tiles": 65536, "K": K,
+        "relative_frobenius_error": out["relative_frobenius_error"],
+        "normalized_proxy_loss": out["normalized_proxy_loss"],
+        "reference_published_seconds": 43.0,
+        "reference_published_note": "Arc B580, K=2 o_proj with GSS (no K=4 figure published)",
+    }
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -222,6 +284,10 @@ def run_b200(args):
     from exl3_intel_arc_quantizer_b200.xpu_quantizer import ScratchArena, XPUTrellisEncoder
 
     K, n = args.K, args.tiles
+    if args.layer_only:
+        if rank == 0:
+            print(json.dumps({"layer": run_layer(device)}), flush=True)
+        return 0
     enc = XPUTrellisEncoder(K=K, cb=2, device_index=local,
                             arena=ScratchArena(device_index=local, default_cap_b=args.chunk))
     x = make_tiles(n, 1234 + rank, device)
@@ -354,6 +420,9 @@ def run_b200(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(K)
+    layer = None
+    if rank == 0 and not args.no_layer:
+        layer = run_layer(device)
 
     if rank == 0:
         line = {
@@ -369,6 +438,7 @@ def run_b200(args):
                        "l2": "flushed between timed steps (512 MiB write)",
                        "parallelism": f"tiles sharded, {world} rank(s), no collective"},
             "k4_tiles_per_s": k4,
+            "layer": layer,
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -52,6 +52,8 @@ void check_status(int rc, const char* what) {
 
 }  // namespace
 
+void register_linalg_ops(pybind11::module& m);  // torch_ext_linalg.cpp
+
 void decode_codebook(int64_t cb, at::Tensor out_lut) {
   TORCH_CHECK(cb >= 0 && cb <= 2, "cb must be 0, 1, or 2");
   const int64_t dev = check_cuda_tensor(out_lut, "out_lut", at::kHalf, 1);
@@ -277,4 +279,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("sg_size") = 32, "Single backward traceback pass on CUDA");
   m.def("pack_trellis", &pack_trellis, py::arg("states"), py::arg("packed"), py::arg("K"),
         "Pack 16-bit trellis states into the EXL3 container (SWAP16 storage)");
+  register_linalg_ops(m);
 }

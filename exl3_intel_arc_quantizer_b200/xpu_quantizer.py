@@ -176,6 +176,15 @@ class ScratchArena:
             action, k, tile_len, req, adm, scratch, staging, out,
             self.policy.usable_bytes(snap), snap.as_dict()))
 
+    def resident(self, k: int, tile_len: int, b: int):
+        """The resident workspace if it already serves (K, L, b tiles), else
+        None; no bookkeeping (hot loops such as LDLQ call this per block)."""
+        key = self._key
+        if (key is not None and key[0] == self.device_index and key[1] == k
+                and key[2] == tile_len and key[3] >= b):
+            return self._ws
+        return None
+
     def adaptive_batch_capacity(self, k: int, tile_len: int = 256,
                                 requested_b: Optional[int] = None,
                                 distinct_staging_bytes: int = 0) -> int:
@@ -216,7 +225,7 @@ class ScratchArena:
         key = self._key
         if (key is not None and key[0] == self.device_index and key[1] == k
                 and key[2] == tile_len and key[3] >= target):
-            torch.cuda.current_stream(self.device_index).synchronize()
+            # reuse is ordered on the stream the encoder launches on: no sync
             self.reuses += 1
             self._log("reuse", k, tile_len, target, target, self.resident_bytes,
                       distinct_staging_bytes)
@@ -338,7 +347,9 @@ class XPUTrellisEncoder:
         if n <= 0:
             raise ValueError(f"num_tiles must be positive, got {n}")
         cap = min(n, requested_b if requested_b is not None else self.arena.default_cap_b)
-        ws, per, admitted = self.arena.acquire(self.K, self.L, cap)
+        ws = self.arena.resident(self.K, self.L, cap)
+        if ws is None:
+            ws, _, _ = self.arena.acquire(self.K, self.L, cap)
         out_w = torch.empty_like(x)
         out_i = torch.empty((n, self.L), dtype=torch.int16, device=dev)
         packed = (torch.empty((n, 16 * self.K), dtype=torch.int16, device=dev)

@@ -137,6 +137,43 @@ int exl3_quantize_tiles_noalloc(const float* in, float* out_w, int16_t* out_idx,
                                 int cb, int L, exl3_stream_t stream);
 
 /* ------------------------------------------------------------------ */
+/* Floating-point stages                                               */
+/* ------------------------------------------------------------------ */
+
+/*
+ * In-place blockwise orthonormal Sylvester Hadamard on a row-major fp32
+ * (k, n) matrix: right = x @ H128/sqrt(128) on every 128-column block
+ * (n % 128 == 0), left = H128/sqrt(128) @ x on every 128-row block
+ * (k % 128 == 0). Replace blockwise_preapply_had_r_ / _l_
+ * (exl3_quant/hadamard.py:94-119).
+ */
+int exl3_had128_right(float* x, int64_t k, int64_t n, exl3_stream_t stream);
+int exl3_had128_left(float* x, int64_t k, int64_t n, exl3_stream_t stream);
+
+/*
+ * H += X^T X on the tensor cores (tcgen05, fp32 accumulation): X is a
+ * row-major (T, d) fp16 (dtype 0) or bf16 (dtype 1) matrix, 16-byte aligned,
+ * d % 8 == 0; H is a row-major fp32 (d, d) matrix. Only the upper-triangle
+ * 128x128 tiles are multiplied; the lower triangle is written by mirroring.
+ * err_flag (device int) is set to 1 if a CTA gave up waiting on its own
+ * tensor-core completion (it then skips its update). Replaces
+ * HessianCollector._accumulate (exl3_quant/calibration.py:337-352).
+ */
+int exl3_hessian_accumulate(float* H, const void* X, int dtype, int64_t T, int64_t d,
+                            int* err_flag, exl3_stream_t stream);
+
+/*
+ * Hessian finalize in place on an fp32 (d, d) sum of X^T X over `count`
+ * tokens: H /= count; diag += max(1e-8, lambda * mean(diag)); diagonal
+ * entries with |d| < zero_floor become zero_floor. damp_out (device, may be
+ * NULL) receives the damping added; scratch8 is 8 bytes of device scratch.
+ * Replaces HessianCollector.finalize (exl3_quant/calibration.py:359-407).
+ */
+int exl3_hessian_finalize(float* H, int64_t d, int64_t count, float damping_lambda,
+                          float zero_floor, float* damp_out, void* scratch8,
+                          exl3_stream_t stream);
+
+/* ------------------------------------------------------------------ */
 /* Diagnostics                                                         */
 /* ------------------------------------------------------------------ */
 

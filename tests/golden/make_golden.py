@@ -275,11 +275,35 @@ def gen_ldlq(pool, out):
     return [{"name": c[0], "K": c[1], "k": c[2], "n": c[3], "buf": c[4], "seed": c[5]} for c in cases]
 
 
+def gen_module(out):
+    """quantize_linear_module end to end (reference CPU path, reference encoder)."""
+    sys.path.insert(0, REF)
+    import torch
+    from exl3_quant import layer_quant as lqm
+    g = torch.Generator().manual_seed(31)
+    k, n = 128, 256
+    W = (torch.randn(n, k, generator=g) * 0.02)
+    W[:, torch.randperm(k, generator=g)[:2]] *= 8.0
+    X = torch.randn(512, k, generator=g)
+    X[:, torch.randperm(k, generator=g)[:3]] *= 20.0
+    H = (X.T @ X) / 512
+    H.diagonal().add_(0.01 * H.diagonal().mean())
+    res = lqm.quantize_linear_module("mod", W, H, K=2, skip_g_scale=True, buf_size_k=64)
+    m = res.metrics
+    np.savez_compressed(out / "module_golden.npz", W=W.numpy(), H=H.numpy(), w_hat=res.w_hat.numpy(),
+                        encoded=res.encoded.numpy(), su=res.su.numpy(), sv=res.sv.numpy(),
+                        reg_weight=res.regularize_result.weight.numpy(),
+                        L=res.ldl_result.transformed.numpy(),
+                        metrics=np.array([m.mse, m.relative_frobenius_error, m.tile_distortion,
+                                          m.proxy_loss, m.normalized_proxy_loss]))
+    return {"k": k, "n": n, "K": 2, "buf": 64, "seed": 31}
+
+
 def main():
     global REF
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
-    ap.add_argument("--only", default="", help="comma list: encoder,forward,format,float,ldlq")
+    ap.add_argument("--only", default="", help="comma list: encoder,forward,format,float,ldlq,module")
     ap.add_argument("--procs", type=int, default=os.cpu_count() or 1)
     args = ap.parse_args()
     REF = str(Path(args.reference).resolve())
@@ -301,6 +325,8 @@ def main():
             manifest["ldlq"] = gen_ldlq(pool, HERE)
         if not only or "encoder" in only:
             manifest["encoder"] = gen_encoder(pool, HERE)
+        if not only or "module" in only:
+            manifest["module"] = gen_module(HERE)
     files = {}
     for f in sorted(HERE.glob("*.npz")):
         files[f.name] = hashlib.sha256(f.read_bytes()).hexdigest()

@@ -1,0 +1,172 @@
+"""GPU parity of the floating-point stages around the encoder.
+
+Tolerances (floating point, stated per check):
+  * Hadamard (FWHT vs the reference's fp32 GEMM): max |diff| <= 1e-5 * max |x|
+  * Hessian accumulation: max relative error <= 1e-4 (products of fp16/bf16
+    are exact in fp32; only the summation order differs)
+  * regularize, block_ldl, finalize: relative 1e-4 / absolute 1e-4
+  * LDLQ with the B200 encoder on the reference's CPU op sequence: bit-exact
+  * fully GPU-native module: relative Frobenius distance of w_hat to the
+    reference's w_hat <= 1e-2, and quality metrics within 2% (a one-ulp
+    difference in a tile's fp16 input can move that tile's trellis path; the
+    distance is reported, not hidden)
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from exl3_intel_arc_quantizer_b200 import hadamard as hd  # noqa: E402
+from exl3_intel_arc_quantizer_b200.calibration import (  # noqa: E402
+    HessianCollector,
+    hessian_accumulate_,
+    hessian_finalize_,
+)
+from exl3_intel_arc_quantizer_b200.ldlq import block_ldl, ldlq, make_xpu_tile_encoder  # noqa: E402
+from exl3_intel_arc_quantizer_b200.regularize import regularize  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+
+
+def test_hadamard_matches_reference(float_golden):
+    x = torch.from_numpy(float_golden["had/x"]).to(DEV)
+    scale = float(x.abs().max())
+    for fn, key in ((hd.preapply_had_l, "had/l"), (hd.preapply_had_r, "had/r")):
+        got = fn(x).cpu()
+        assert (got - torch.from_numpy(float_golden[key])).abs().max() <= 1e-5 * scale
+    assert torch.allclose(hd.preapply_had_l(hd.preapply_had_l(x)), x, atol=1e-5)
+    assert torch.allclose(hd.preapply_had_r(hd.preapply_had_r(x)), x, atol=1e-5)
+    h = hd.hadamard(128, torch.float32, device=DEV)
+    blk = torch.block_diag(*([h] * 2))
+    assert torch.allclose(hd.preapply_had_r(x), x @ blk, atol=1e-5)
+    big = torch.randn(4096, 4096, device=DEV)
+    ref = (big.view(4096, 32, 128) @ h).view(4096, 4096)
+    assert (hd.preapply_had_r(big) - ref).abs().max() <= 1e-5 * big.abs().max()
+    with pytest.raises(ValueError):
+        hd.blockwise_preapply_had_l_(x.half())
+    with pytest.raises(ValueError):
+        hd.preapply_had_l(torch.zeros(100, 128, device=DEV))
+
+
+def test_regularize_matches_reference(float_golden):
+    w = torch.from_numpy(float_golden["reg/w"]).to(DEV)
+    su = torch.from_numpy(float_golden["reg/su_in"]).to(DEV)
+    sv = torch.from_numpy(float_golden["reg/sv_in"]).to(DEV)
+    hdiag = torch.from_numpy(float_golden["reg/hdiag"]).to(DEV)
+    r = regularize(w, su, sv, H_diag=hdiag, skip_g_scale=True)
+    for key, got in (("reg/weight", r.weight), ("reg/su", r.su), ("reg/sv", r.sv)):
+        ref = torch.from_numpy(float_golden[key])
+        assert torch.allclose(got.cpu(), ref, rtol=1e-4, atol=1e-5), key
+    assert [r.apply_out_scales, r.zeros] == list(float_golden["reg/flags"].astype(bool))
+    back = hd.weight_from_quantized(r.weight, r.su, r.sv)
+    assert (back - w).abs().max() < 1e-4
+
+
+def test_block_ldl_matches_reference(float_golden):
+    H = torch.from_numpy(float_golden["ldl/H"]).to(DEV)
+    r = block_ldl(H, block_size=16)
+    assert r.retries == 0
+    assert torch.allclose(r.cholesky.cpu(), torch.from_numpy(float_golden["ldl/chol"]), atol=1e-4)
+    assert torch.allclose(r.transformed.cpu(), torch.from_numpy(float_golden["ldl/L"]), atol=1e-4)
+
+
+def _max_rel(a, b):
+    return float((a - b).abs().max() / b.abs().max())
+
+
+def test_hessian_accumulate_and_finalize_match_reference(float_golden):
+    H = torch.zeros(128, 128, device=DEV)
+    for key in ("hess/x1", "hess/x2"):
+        x = torch.from_numpy(float_golden[key]).to(DEV)
+        hessian_accumulate_(H, x.reshape(-1, 128))
+    torch.cuda.synchronize()
+    assert _max_rel(H.cpu(), torch.from_numpy(float_golden["hess/raw"])) <= 1e-4
+    count = 3 * 40 + 2 * 24
+    damp = hessian_finalize_(H, count, 0.01, 1e-7)
+    assert _max_rel(H.cpu(), torch.from_numpy(float_golden["hess/final"])) <= 1e-4
+    assert abs(damp - float(float_golden["hess/damp"][0])) <= 1e-4 * abs(damp)
+
+
+@pytest.mark.parametrize("d,T,dtype", [(128, 64, torch.float16), (384, 1000, torch.bfloat16),
+                                       (200, 77, torch.float16), (4096, 2048, torch.bfloat16)])
+def test_hessian_accumulate_random(d, T, dtype):
+    g = torch.Generator(device="cpu").manual_seed(d + T)
+    x = torch.randn(T, d, generator=g).to(dtype).to(DEV)
+    x[:, :3] *= 20.0
+    H = torch.zeros(d, d, device=DEV)
+    hessian_accumulate_(H, x)
+    hessian_accumulate_(H, x)           # accumulates
+    xf = x.float()
+    ref = 2.0 * (xf.T @ xf)
+    assert _max_rel(H, ref) <= 1e-4
+    assert torch.equal(H, H.T)
+
+
+def test_collector_groups_share_hessians():
+    from exl3_intel_arc_quantizer_b200.calibration import TransformerDecoderLayer, make_rotary_embeddings
+
+    layer = TransformerDecoderLayer(128, 256, 4, 2).to(DEV).half().eval()
+    col = HessianCollector(layer, device=DEV)
+    with torch.no_grad():
+        layer(torch.randn(2, 16, 128, device=DEV).half(),
+              position_embeddings=make_rotary_embeddings(16, 32, device=DEV))
+    col.close()
+    hs, damp = col.finalize(damping_lambda=0.01)
+    assert set(hs) == {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj",
+                       "self_attn.o_proj", "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"}
+    assert torch.equal(hs["self_attn.q_proj"], hs["self_attn.k_proj"])
+    assert torch.equal(hs["mlp.gate_proj"], hs["mlp.up_proj"])
+    assert hs["mlp.down_proj"].shape == (256, 256)
+    assert all(bool((h.diagonal() > 0).all()) for h in hs.values())
+
+
+@pytest.mark.parametrize("name", ["k2_32x128", "k4_64x128"])
+def test_ldlq_reference_op_sequence_with_b200_encoder_is_bit_exact(ldlq_golden, name):
+    K, k, n, buf, seed = (int(v) for v in ldlq_golden[f"{name}/params"])
+    w = torch.from_numpy(ldlq_golden[f"{name}/weight"])
+    L = torch.from_numpy(ldlq_golden[f"{name}/L"])
+    res = ldlq(w, L, make_xpu_tile_encoder(K=K), buf_size_k=buf)   # CPU loop, GPU encoder
+    assert torch.equal(res.weight_q, torch.from_numpy(ldlq_golden[f"{name}/weight_q"]))
+    assert torch.equal(res.encoded, torch.from_numpy(ldlq_golden[f"{name}/encoded"]))
+
+
+def test_ldlq_gpu_native_close_to_reference(ldlq_golden):
+    name = "k4_64x128"
+    K, k, n, buf, seed = (int(v) for v in ldlq_golden[f"{name}/params"])
+    w = torch.from_numpy(ldlq_golden[f"{name}/weight"]).to(DEV)
+    L = torch.from_numpy(ldlq_golden[f"{name}/L"]).to(DEV)
+    res = ldlq(w, L, make_xpu_tile_encoder(K=K), buf_size_k=buf)
+    ref_q = torch.from_numpy(ldlq_golden[f"{name}/weight_q"])
+    rel = float(torch.linalg.norm(res.weight_q.cpu() - ref_q) / torch.linalg.norm(ref_q))
+    same = float((res.encoded.cpu() == torch.from_numpy(ldlq_golden[f"{name}/encoded"]))
+                 .all(dim=-1).float().mean())
+    print(f"gpu-native ldlq: rel frob {rel:.3e}, identical tiles {same:.3f}")
+    assert rel <= 1e-2
+
+
+def test_quantize_linear_module_close_to_reference(manifest):
+    from pathlib import Path
+
+    from exl3_intel_arc_quantizer_b200.layer_quant import quantize_linear_module
+
+    path = Path(__file__).parent / "golden" / "module_golden.npz"
+    if not path.exists():
+        pytest.skip("module golden not generated")
+    gm = np.load(path)
+    W = torch.from_numpy(gm["W"]).to(DEV)
+    H = torch.from_numpy(gm["H"]).to(DEV)
+    res = quantize_linear_module("mod", W, H, K=2, skip_g_scale=True, buf_size_k=64)
+    ref_w = torch.from_numpy(gm["w_hat"])
+    rel = float(torch.linalg.norm(res.w_hat.cpu() - ref_w) / torch.linalg.norm(ref_w))
+    same = float((res.encoded.cpu() == torch.from_numpy(gm["encoded"])).all(dim=-1).float().mean())
+    m = res.metrics
+    ref_m = gm["metrics"]
+    print(f"module: w_hat rel frob vs reference {rel:.3e}, identical tiles {same:.3f}, "
+          f"rel_frob_err {m.relative_frobenius_error:.5f} vs {ref_m[1]:.5f}")
+    assert rel <= 1e-2
+    assert abs(m.relative_frobenius_error - ref_m[1]) <= 0.02 * ref_m[1]
+    assert abs(m.proxy_loss - ref_m[3]) <= 0.02 * abs(ref_m[3])
