@@ -285,20 +285,23 @@ extern "C" int exl3_hessian_accumulate(float* H, const void* X, int dtype, int64
   const int nt = (int)((d + kHT - 1) / kHT);
   const int64_t ntiles = (int64_t)nt * (nt + 1) / 2;
   EXL3_REQUIRE(ntiles < (1ll << 31), "d too large");
-  static bool attr_set[2] = {false, false};
+  static uint32_t attr_done[2] = {0u, 0u};  // per dtype, one bit per device
+  int dev = 0;
+  EXL3_CUDA(cudaGetDevice(&dev));
+  const uint32_t bit = dev < 32 ? (1u << dev) : 0u;
   if (dtype == 0) {
-    if (!attr_set[0]) {
+    if (!(attr_done[0] & bit)) {
       EXL3_CUDA(cudaFuncSetAttribute(hessian_tc_kernel<__half, 0>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHSmem));
-      attr_set[0] = true;
+      attr_done[0] |= bit;
     }
     hessian_tc_kernel<__half, 0><<<(unsigned)ntiles, kHThreads, kHSmem, (cudaStream_t)stream>>>(
         static_cast<const __half*>(X), T, d, H, nt, err_flag);
   } else {
-    if (!attr_set[1]) {
+    if (!(attr_done[1] & bit)) {
       EXL3_CUDA(cudaFuncSetAttribute(hessian_tc_kernel<__nv_bfloat16, 1>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHSmem));
-      attr_set[1] = true;
+      attr_done[1] |= bit;
     }
     hessian_tc_kernel<__nv_bfloat16, 1><<<(unsigned)ntiles, kHThreads, kHSmem,
                                           (cudaStream_t)stream>>>(
