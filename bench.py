@@ -224,7 +224,7 @@ def layer_config3(device, seed=0):
     return W.to(torch.bfloat16).to(device), X.to(torch.bfloat16).to(device)
 
 
-def run_layer(device, K=4, reps=2):
+def run_layer(device, K=4, reps=2, skip_g_scale=True):
     """Seconds per 4096x4096 linear layer: Hessian (X^T X, finalize) and
     quantize_linear_module (regularize, Hadamard, block-LDL, LDLQ with the
     B200 encoder, reconstruction, metrics), each timed end to end."""
@@ -245,8 +245,8 @@ def run_layer(device, K=4, reps=2):
         hessian_finalize_(H, X.shape[0], 0.01, 1e-7)
         torch.cuda.synchronize()
         t1 = time.perf_counter()
-        res = quantize_linear_module("o_proj", W, H, K=K, tile_encoder=enc, skip_g_scale=True,
-                                     buf_size_k=128, block_size=16)
+        res = quantize_linear_module("o_proj", W, H, K=K, tile_encoder=enc,
+                                     skip_g_scale=skip_g_scale, buf_size_k=128, block_size=16)
         torch.cuda.synchronize()
         t2 = time.perf_counter()
         if rep > 0:   # first repetition is warm-up
@@ -256,17 +256,20 @@ def run_layer(device, K=4, reps=2):
             out["relative_frobenius_error"] = m.relative_frobenius_error
             out["normalized_proxy_loss"] = m.normalized_proxy_loss
             out["retries"] = m.retries
+            out["g_scale"] = m.g_scale
     enc.encoder.arena.release()
+    gss = "skip_g_scale" if skip_g_scale else f"global-scale search (g={out['g_scale']:.4f})"
     return {
-        "workload": "config 3: 4096x4096 bf16 layer, K=4, Hessian from 2048x4096 bf16, "
-                    "skip_g_scale, buf 128, block 16",
+        "workload": f"config 3: 4096x4096 bf16 layer, K={K}, Hessian from 2048x4096 bf16, "
+                    f"{gss}, buf 128, block 16",
         "seconds_per_layer": min(out["layer_s"]),
         "hessian_seconds": min(out["hessian_s"]),
         "tiles": 65536, "K": K,
         "relative_frobenius_error": out["relative_frobenius_error"],
         "normalized_proxy_loss": out["normalized_proxy_loss"],
-        "reference_published_seconds": 43.0,
-        "reference_published_note": "Arc B580, K=2 o_proj with GSS (no K=4 figure published)",
+        "reference_published_seconds": 43.0 if (K == 2 and not skip_g_scale) else None,
+        "reference_published_note": "Arc B580, 4096x4096 o_proj, K=2 with global-scale search "
+                                    "(reports/discrete_phase_c.md); no K=4 figure is published",
     }
 
 
@@ -286,7 +289,9 @@ def run_b200(args):
     K, n = args.K, args.tiles
     if args.layer_only:
         if rank == 0:
-            print(json.dumps({"layer": run_layer(device)}), flush=True)
+            print(json.dumps({"layer": run_layer(device),
+                              "layer_k2_gss": run_layer(device, K=2, skip_g_scale=False)}),
+                  flush=True)
         return 0
     enc = XPUTrellisEncoder(K=K, cb=2, device_index=local,
                             arena=ScratchArena(device_index=local, default_cap_b=args.chunk))
@@ -394,9 +399,11 @@ def run_b200(args):
     traffic = None
     tfile = REPO / "profiles" / f"encoder_k{K}_dram_per_launch.json"
     if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get("dram_bytes_per_tile")
-        if traffic is not None:
-            traffic = traffic * (min(args.chunk, n))
+        per = json.loads(tfile.read_text()).get("dram_bytes_per_tile_per_pass")
+        if per is not None:
+            # one ACS launch = one pass over a chunk; scaled from the ncu
+            # capture's 296 tiles (backpointer writes grow with the tile count)
+            traffic = per * min(args.chunk, n)
     roofline = {
         "bound": "fp16_alu",
         "achieved": achieved / 1e9, "peak": peak / 1e9, "unit": "Gop/s",
@@ -408,7 +415,8 @@ def run_b200(args):
                   "exl3::acs_kernel (pass 1 + pass 2)",
         "acs_share_of_step": acs_ms.value / max(1e-9, total_ms / max(1, world)),
         "traffic": traffic,
-        "traffic_unit": "bytes per launch (ncu dram read+write)",
+        "traffic_unit": "bytes per ACS launch (ncu dram read+write, 296-tile capture scaled "
+                        "to the chunk)",
     }
     from exl3_intel_arc_quantizer_b200.scratch_estimator import b200_backpointer_step_bytes
 
@@ -420,9 +428,10 @@ def run_b200(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(K)
-    layer = None
+    layer = layer2 = None
     if rank == 0 and not args.no_layer:
         layer = run_layer(device)
+        layer2 = run_layer(device, K=2, skip_g_scale=False)
 
     if rank == 0:
         line = {
@@ -439,6 +448,7 @@ def run_b200(args):
                        "parallelism": f"tiles sharded, {world} rank(s), no collective"},
             "k4_tiles_per_s": k4,
             "layer": layer,
+            "layer_k2_gss": layer2,
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
