@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-k4", action="store_true")
     ap.add_argument("--no-layer", action="store_true")
+    ap.add_argument("--hessian-only", action="store_true",
+                    help="time the Hessian accumulation on config 4 shapes and exit")
+    ap.add_argument("--hessian-tokens", type=int, default=262144)
     ap.add_argument("--layer-only", action="store_true",
                     help="only the 4096x4096 K=4 layer measurement (config 3)")
     return ap.parse_args()
@@ -273,6 +276,53 @@ def run_layer(device, K=4, reps=2, skip_g_scale=True):
     }
 
 
+def run_hessian(device, tokens=262144, dims=(4096, 12288), steps=3, warmup=2):
+    """Hessian accumulation H += X^T X (tcgen05 kernel) on BASELINE config 4
+    shapes: `tokens` bf16 activation rows, one group per width in `dims`.
+    FLOPs are reported as 2*T*d^2 (full square; the kernel computes the upper
+    triangle of 128x128 tiles and mirrors it, 2*T*d*(d+128)/2 MMA flops)."""
+    import torch
+
+    from exl3_intel_arc_quantizer_b200._ext import ext
+
+    peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) \
+        if (REPO / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("bf16_tflops", 1590.0)
+    out = []
+    for d in dims:
+        g = torch.Generator(device=device).manual_seed(d)
+        X = torch.randn(tokens, d, generator=g, device=device, dtype=torch.bfloat16)
+        H = torch.zeros(d, d, dtype=torch.float32, device=device)
+        err = torch.zeros(1, dtype=torch.int32, device=device)
+        for _ in range(warmup):
+            ext().hessian_accumulate_(H, X, err)
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        for e0, e1 in ev:
+            e0.record()
+            ext().hessian_accumulate_(H, X, err)
+            e1.record()
+        torch.cuda.synchronize()
+        ms = min(e0.elapsed_time(e1) for e0, e1 in ev)
+        nt = (d + 127) // 128
+        mma_flops = 2.0 * tokens * (nt * (nt + 1) // 2) * 128 * 128
+        full = 2.0 * tokens * d * d
+        # accuracy spot check on a 256x256 corner against an fp32 product
+        xs = X[:, :256].float()
+        ref = (warmup + steps) * (xs.T @ xs)
+        rel = float((H[:256, :256] - ref).abs().max() / ref.abs().max())
+        out.append({"tokens": tokens, "d": d, "ms": ms,
+                    "tflops_full_square": full / ms / 1e9,
+                    "tflops_mma": mma_flops / ms / 1e9,
+                    "frac_mma_of_measured_bf16": mma_flops / ms / 1e9 / peak,
+                    "err_flag": int(err.item()), "corner_max_rel_err": rel})
+        del X, H
+        torch.cuda.empty_cache()
+    return {"workload": "config 4 Hessian groups, bf16 activations, fp32 H",
+            "peak_bf16_tflops_measured": peak, "groups": out}
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -287,6 +337,11 @@ def run_b200(args):
     from exl3_intel_arc_quantizer_b200.xpu_quantizer import ScratchArena, XPUTrellisEncoder
 
     K, n = args.K, args.tiles
+    if args.hessian_only:
+        if rank == 0:
+            print(json.dumps({"hessian": run_hessian(device, tokens=args.hessian_tokens)}),
+                  flush=True)
+        return 0
     if args.layer_only:
         if rank == 0:
             print(json.dumps({"layer": run_layer(device),

@@ -12,16 +12,11 @@
 // diag += max(1e-8, lambda * mean(diag)), diag entries with |d| < floor set to
 // floor.
 #include "common.cuh"
+#include "hadamard.cuh"
 
 namespace exl3 {
 
 namespace {
-
-// Sylvester order: butterfly partner of element i at stride h is i ^ h, the
-// lower index keeps the sum.
-__device__ __forceinline__ float bfly(float mine, float other, bool upper) {
-  return upper ? (other - mine) : (mine + other);
-}
 
 // x @ H on 128-column blocks: one warp per (row, block); lane l holds
 // elements l, l+32, l+64, l+96 of the block.
@@ -35,17 +30,7 @@ __global__ void had_right_kernel(float* __restrict__ x, int64_t k, int64_t n, fl
   float v[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) v[q] = p[lane + 32 * q];
-#pragma unroll
-  for (int h = 1; h < 32; h <<= 1) {
-    const bool up = (lane & h) != 0;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) v[q] = bfly(v[q], __shfl_xor_sync(0xFFFFFFFFu, v[q], h), up);
-  }
-  // strides 32 and 64 live inside the thread (element index bits 5 and 6)
-  {
-    const float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
-    v[0] = a0 + a2; v[1] = a1 + a3; v[2] = a0 - a2; v[3] = a1 - a3;
-  }
+  fwht128_warp(v, lane);
 #pragma unroll
   for (int q = 0; q < 4; ++q) p[lane + 32 * q] = v[q] * scale;
 }
@@ -67,14 +52,7 @@ __global__ void had_left_kernel(float* __restrict__ x, int64_t k, int64_t n, flo
     float v[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) v[q] = tile[lane + 32 * q][c];
-#pragma unroll
-    for (int h = 1; h < 32; h <<= 1) {
-      const bool up = (lane & h) != 0;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) v[q] = bfly(v[q], __shfl_xor_sync(0xFFFFFFFFu, v[q], h), up);
-    }
-    const float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
-    v[0] = a0 + a2; v[1] = a1 + a3; v[2] = a0 - a2; v[3] = a1 - a3;
+    fwht128_warp(v, lane);
 #pragma unroll
     for (int q = 0; q < 4; ++q) tile[lane + 32 * q][c] = v[q] * scale;
   }

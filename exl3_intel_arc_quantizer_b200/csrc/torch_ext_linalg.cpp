@@ -69,7 +69,61 @@ void hessian_accumulate_(at::Tensor H, at::Tensor X, at::Tensor err_flag) {
         "hessian_accumulate");
 }
 
+void unpack_trellis(at::Tensor trellis, at::Tensor states, int64_t K) {
+  TORCH_CHECK(trellis.is_cuda() && trellis.is_contiguous() && trellis.scalar_type() == at::kShort,
+              "trellis must be a contiguous int16 CUDA tensor");
+  TORCH_CHECK(states.is_cuda() && states.is_contiguous() && states.scalar_type() == at::kShort,
+              "states must be a contiguous int16 CUDA tensor");
+  TORCH_CHECK(trellis.device() == states.device(), "trellis and states must be on the same device");
+  TORCH_CHECK(K >= 1 && K <= 8, "K must be in 1..8");
+  TORCH_CHECK(trellis.numel() % (16 * K) == 0, "trellis size must be a multiple of 16*K");
+  const int64_t ntiles = trellis.numel() / (16 * K);
+  TORCH_CHECK(states.numel() == ntiles * 256, "states must hold 256 entries per tile");
+  c10::cuda::CUDAGuard g(trellis.device());
+  check(exl3_unpack_trellis(trellis.data_ptr<int16_t>(), states.data_ptr<int16_t>(), ntiles,
+                            (int)K, cur_stream(trellis)),
+        "unpack_trellis");
+}
+
+void decode_weight(at::Tensor trellis, at::Tensor su, at::Tensor sv, at::Tensor out,
+                   c10::optional<at::Tensor> out_w_hat, int64_t K, int64_t cb) {
+  TORCH_CHECK(trellis.is_cuda() && trellis.is_contiguous() && trellis.scalar_type() == at::kShort &&
+                  trellis.dim() == 3,
+              "trellis must be a contiguous (tiles_k, tiles_n, 16*K) int16 CUDA tensor");
+  TORCH_CHECK(trellis.size(2) == 16 * K, "trellis last dimension ", trellis.size(2),
+              " does not match 16 * K = ", 16 * K);
+  const int64_t k = trellis.size(0) * 16, n = trellis.size(1) * 16;
+  TORCH_CHECK(su.is_cuda() && sv.is_cuda() && su.is_contiguous() && sv.is_contiguous(),
+              "su and sv must be contiguous CUDA tensors");
+  TORCH_CHECK(su.scalar_type() == sv.scalar_type() &&
+                  (su.scalar_type() == at::kHalf || su.scalar_type() == at::kFloat),
+              "su and sv must both be float16 or both float32");
+  TORCH_CHECK(su.numel() == k && sv.numel() == n, "su must have ", k, " elements and sv ", n);
+  check_f32_cuda_2d(out, "out");
+  TORCH_CHECK(out.size(0) == k && out.size(1) == n, "out must be (", k, ", ", n, ")");
+  float* wh = nullptr;
+  if (out_w_hat.has_value()) {
+    check_f32_cuda_2d(*out_w_hat, "out_w_hat");
+    TORCH_CHECK(out_w_hat->size(0) == k && out_w_hat->size(1) == n, "out_w_hat must be (", k, ", ",
+                n, ")");
+    wh = out_w_hat->data_ptr<float>();
+  }
+  for (const at::Tensor* t : {&su, &sv, &out})
+    TORCH_CHECK(t->device() == trellis.device(), "all tensors must be on the same device");
+  c10::cuda::CUDAGuard g(trellis.device());
+  check(exl3_decode_weight(trellis.data_ptr<int16_t>(), su.data_ptr(), sv.data_ptr(),
+                           su.scalar_type() == at::kFloat ? 1 : 0, out.data_ptr<float>(), wh,
+                           trellis.size(0), trellis.size(1), (int)K, (int)cb, cur_stream(out)),
+        "decode_weight");
+}
+
 void register_linalg_ops(pybind11::module& m) {
+  m.def("unpack_trellis", &unpack_trellis, pybind11::arg("trellis"), pybind11::arg("states"),
+        pybind11::arg("K"), "Container words -> 16-bit states");
+  m.def("decode_weight", &decode_weight, pybind11::arg("trellis"), pybind11::arg("su"),
+        pybind11::arg("sv"), pybind11::arg("out"), pybind11::arg("out_w_hat") = pybind11::none(),
+        pybind11::arg("K"), pybind11::arg("cb"),
+        "Original-basis weight from the EXL3 container and scales in one pass");
   m.def("hessian_accumulate_", &hessian_accumulate_, pybind11::arg("H"), pybind11::arg("X"),
         pybind11::arg("err_flag"), "In-place H += X^T X on the tensor cores");
   m.def("had128_right_", &had128_right_, "In-place x @ H128/sqrt(128) on 128-column blocks");

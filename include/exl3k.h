@@ -137,6 +137,31 @@ int exl3_quantize_tiles_noalloc(const float* in, float* out_w, int16_t* out_idx,
                                 int cb, int L, exl3_stream_t stream);
 
 /* ------------------------------------------------------------------ */
+/* Storage side: container unpack and weight decode                    */
+/* ------------------------------------------------------------------ */
+
+/*
+ * Container words -> 16-bit states: trellis (ntiles, 16*K) int16 in SWAP16
+ * storage order -> states (ntiles, 256) int16. Replaces
+ * unpack_module_trellis (exl3_quant/serialization.py:65-84).
+ */
+int exl3_unpack_trellis(const int16_t* trellis, int16_t* states, int64_t ntiles, int K,
+                        exl3_stream_t stream);
+
+/*
+ * Original-basis weight from the stored EXL3 parameters in one pass:
+ * trellis (tiles_k, tiles_n, 16*K) int16 (4-byte aligned), su (k) and sv (n)
+ * scales as fp16 (scale_dtype 0, the stored .suh/.svh) or fp32 (1) ->
+ * out (k, n) fp32 row-major = H_l(w_hat) * su -> H_r -> * sv, with
+ * k = 16*tiles_k and n = 16*tiles_n multiples of 128. out_w_hat (nullable)
+ * receives the transformed-basis reconstruction w_hat. Replaces
+ * decode_weight_from_storage (exl3_quant/serialization.py:227-266).
+ */
+int exl3_decode_weight(const int16_t* trellis, const void* su, const void* sv, int scale_dtype,
+                       float* out, float* out_w_hat, int64_t tiles_k, int64_t tiles_n, int K,
+                       int cb, exl3_stream_t stream);
+
+/* ------------------------------------------------------------------ */
 /* Floating-point stages                                               */
 /* ------------------------------------------------------------------ */
 

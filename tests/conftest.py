@@ -66,3 +66,21 @@ def float_golden():
 @pytest.fixture(scope="session")
 def ldlq_golden():
     return np.load(GOLDEN / "ldlq_golden.npz")
+
+
+@pytest.fixture(scope="session")
+def golden_dir():
+    return GOLDEN
+
+
+@pytest.fixture(scope="session")
+def module_golden_arrays():
+    return np.load(GOLDEN / "module_golden.npz")
+
+
+@pytest.fixture(scope="session")
+def storage_golden():
+    path = GOLDEN / "storage_golden.npz"
+    if not path.exists():
+        pytest.skip("storage golden not generated")
+    return np.load(path)

@@ -13,6 +13,8 @@ Every vector comes from the reference's own CPU code path:
   * format   — exl3_quant.trellis_format (codebook_lut, pack_trellis, swap16)
   * ldlq     — exl3_quant.ldlq.block_ldl / ldlq with make_reference_tile_encoder
   * float    — hadamard / regularize / calibration.HessianCollector
+  * storage  — exl3_quant.serialization (pack/unpack_module_trellis,
+               build_layer_tensors, decode_weight_from_storage)
 
 Inputs are seeded synthetic data with the shapes and distributions of the
 reference's tests and of the benchmark configurations.
@@ -299,11 +301,63 @@ def gen_module(out):
     return {"k": k, "n": n, "K": 2, "buf": 64, "seed": 31}
 
 
+def gen_storage(out):
+    """serialization.py: module packing, unpacking and weight decode.
+
+    * module: the module golden's encoded states and scales through
+      pack_module_trellis, build_layer_tensors (keys/shapes/dtypes) and
+      decode_weight_from_storage (fp16 stored scales);
+    * rand_K{K}_{cb}: random container words (8x8 tiles, 128x128 weight),
+      random positive scales, unpacked and decoded for every K and codebook.
+    """
+    sys.path.insert(0, REF)
+    import torch
+    from exl3_quant import serialization as ser
+    from exl3_quant.layer_quant import QuantizedModuleResult
+
+    arrays = {}
+    gm = np.load(out / "module_golden.npz")
+    enc = torch.from_numpy(gm["encoded"])
+    trellis = ser.pack_module_trellis(enc, K=2)
+    suh = torch.from_numpy(gm["su"]).flatten().to(torch.float16)
+    svh = torch.from_numpy(gm["sv"]).flatten().to(torch.float16)
+    arrays["module/trellis"] = trellis.numpy()
+    arrays["module/unpacked"] = ser.unpack_module_trellis(trellis, K=2).numpy()
+    arrays["module/decoded"] = ser.decode_weight_from_storage(trellis, suh, svh, K=2, cb=2).numpy()
+    res = QuantizedModuleResult.__new__(QuantizedModuleResult)
+    res.K, res.cb, res.encoded = 2, 2, enc
+    res.su, res.sv = torch.from_numpy(gm["su"]), torch.from_numpy(gm["sv"])
+    tensors, storage = ser.build_layer_tensors({"self_attn.o_proj": res}, layer_idx=3)
+    keys = sorted(tensors)
+    arrays["module/layer_keys"] = np.array(keys)
+    arrays["module/layer_shapes"] = np.array([json.dumps(list(tensors[k].shape)) for k in keys])
+    arrays["module/layer_dtypes"] = np.array([str(tensors[k].dtype) for k in keys])
+    arrays["module/storage_json"] = np.array(json.dumps(storage, sort_keys=True))
+    rng = np.random.default_rng(77)
+    cases = []
+    for K in range(1, 9):
+        cb = (2, 1, 0)[K % 3]
+        words = rng.integers(0, 65536, size=(8, 8, 16 * K), dtype=np.uint32).astype(np.uint16)
+        tr = torch.from_numpy(words.view(np.int16).copy())
+        su = torch.from_numpy(rng.uniform(0.5, 2.0, 128).astype(np.float16))
+        sv = torch.from_numpy((rng.uniform(0.5, 2.0, 128) * rng.choice([-1, 1], 128))
+                              .astype(np.float16))
+        name = f"rand_K{K}_cb{cb}"
+        arrays[f"{name}/trellis"] = tr.numpy()
+        arrays[f"{name}/suh"], arrays[f"{name}/svh"] = su.numpy(), sv.numpy()
+        arrays[f"{name}/unpacked"] = ser.unpack_module_trellis(tr, K=K).numpy()
+        arrays[f"{name}/decoded"] = ser.decode_weight_from_storage(tr, su, sv, K=K, cb=cb).numpy()
+        arrays[f"{name}/params"] = np.array([K, cb])
+        cases.append(name)
+    np.savez_compressed(out / "storage_golden.npz", **arrays)
+    return {"module": "module_golden encoded K=2 mul1", "random": cases}
+
+
 def main():
     global REF
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
-    ap.add_argument("--only", default="", help="comma list: encoder,forward,format,float,ldlq,module")
+    ap.add_argument("--only", default="", help="comma list: encoder,forward,format,float,ldlq,module,storage")
     ap.add_argument("--procs", type=int, default=os.cpu_count() or 1)
     args = ap.parse_args()
     REF = str(Path(args.reference).resolve())
@@ -327,6 +381,8 @@ def main():
             manifest["encoder"] = gen_encoder(pool, HERE)
         if not only or "module" in only:
             manifest["module"] = gen_module(HERE)
+        if not only or "storage" in only:
+            manifest["storage"] = gen_storage(HERE)
     files = {}
     for f in sorted(HERE.glob("*.npz")):
         files[f.name] = hashlib.sha256(f.read_bytes()).hexdigest()
