@@ -5,269 +5,362 @@
 // in fp32, so tcgen05 kind::f16 MMAs with fp32 accumulation compute the same
 // sums up to summation order.
 //
-// Design:
-//   * one CTA per 128x128 tile of the upper triangle of H (i0 <= j0); the
-//     lower triangle is written by mirroring, halving the MMA work;
-//   * A = X[:, i0:i0+128]^T and B = X[:, j0:j0+128]^T are both MN-major
-//     (X is row-major (tokens, d)), staged into shared memory in the
-//     canonical no-swizzle MN-major layout (8 K-rows x 16 B core matrices)
-//     by 16-byte cp.async copies, 4 stages of 64 tokens, 2 chunks prefetched;
-//   * one thread issues tcgen05.mma (M=128, N=128, K=16) into a 128-column
-//     TMEM accumulator; tcgen05.commit arrives on the stage's mbarrier when
-//     the MMAs reading that stage are done, which releases it for reuse;
-//   * epilogue: tcgen05.ld 32x32b, fused H += acc (and the mirrored block).
-// Every mbarrier wait is bounded; on timeout the CTA records an error flag,
-// still frees its TMEM and returns.
+// Design (one CTA per 128 x 256 tile of H that reaches the upper triangle;
+// 6 warps with fixed roles):
+//   * warp 0 (one lane) streams X through TMA: per 64-token chunk, the
+//     128-column A slab X[t:t+64, i0:i0+128] and the 256-column B slab
+//     X[t:t+64, j0:j0+256] as 64 x 64 boxes with 128-byte swizzle, straight
+//     into the canonical MN-major SW128 operand layout; 4 stages of 48 KiB;
+//   * warp 1 allocates 512 TMEM columns (two 128 x 256 fp32 accumulators)
+//     and one lane issues tcgen05.mma (M=128, N=256, K=16) per 16 tokens;
+//     tcgen05.commit frees each stage and, every 8192 tokens (a segment),
+//     hands the finished accumulator to the epilogue and switches to the
+//     other one;
+//   * warps 2-5 drain a finished accumulator (tcgen05.ld), stage each 32x32
+//     block in shared memory and add it into H with 16-byte
+//     red.global.add.v4.f32: the element (r, c) for c >= r and its mirror
+//     (c, r) for c > r, while the MMAs of the next segment run.
+// Draining every segment bounds the length of each tensor-core accumulation
+// chain (its additions are not round-to-nearest, so long chains drift) and
+// leaves H symmetric after every call. Each element of H is updated by one
+// thread in a fixed order (other tiles only add +0.0 to it), so results are
+// deterministic.
+// Every wait is bounded by the global timer; a role that gives up records
+// the error flag and the others stop at their next wait; the CTA then waits
+// (bounded) for its own TMA copies and MMAs before it frees TMEM and exits.
+#include <cuda.h>
 #include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
 
 #include "common.cuh"
 
 namespace exl3 {
 namespace {
 
-constexpr int kHT = 128;           // tile (M = N)
-constexpr int kHK = 64;            // tokens per stage
-constexpr int kHStages = 4;        // smem stages
-constexpr int kHPD = 2;            // prefetch distance (chunks in flight ahead of the MMA)
-constexpr int kHThreads = 128;     // 4 warps: loaders, MMA issuer (thread 0), epilogue
-constexpr int kStageBytes = kHT * kHK * 2;   // 16 KiB per operand per stage
-constexpr uint32_t kWaitLimit = 1u << 24;    // bounded mbarrier polls (~1 s)
+constexpr int kBM = 128;                 // tile rows (i)
+constexpr int kBN = 256;                 // tile columns (j)
+constexpr int kBK = 64;                  // tokens per stage
+constexpr int kStages = 4;
+constexpr int kSegChunks = 128;          // 8192 tokens per accumulator segment
+constexpr int kThreads = 192;
+constexpr int kABytes = kBM * kBK * 2;   // 16 KiB
+constexpr int kBBytes = kBN * kBK * 2;   // 32 KiB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kBoxBytes = 64 * kBK * 2;  // one 64-column x 64-token box, 8 KiB
+constexpr int kStgPitch = 33;
+constexpr int kStgBytes = 4 * 32 * kStgPitch * 4;
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-// canonical MN-major, no swizzle: core matrix (8 MN elems x 8 K rows) = 128 B;
-// LBO = stride between K-groups, SBO = stride between MN-groups (bytes).
-constexpr uint32_t kLBO = 128;                  // K-groups adjacent
-constexpr uint32_t kSBO = (kHK / 8) * 128;      // 1024 B per MN-group (8 K-groups)
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
-__device__ __forceinline__ uint64_t make_desc(uint32_t saddr) {
+// MN-major, 128-byte swizzle: 64-element MN blocks LBO apart, 8-row K groups
+// SBO apart (canonical Swizzle<3,4,3> o ((8,8,m),(8,k)):((1,8,LBO),(64,SBO))
+// in elements).
+constexpr uint32_t kLBO = kBoxBytes;  // next 64 columns = next TMA box
+constexpr uint32_t kSBO = 1024;       // 8 tokens x 128 B
+
+__device__ __forceinline__ uint64_t make_desc_sw128(uint32_t saddr) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFF);
   d |= (uint64_t)((kLBO >> 4) & 0x3FFF) << 16;
   d |= (uint64_t)((kSBO >> 4) & 0x3FFF) << 32;
-  d |= (uint64_t)1 << 46;                        // descriptor version (sm_100)
-  // base offset 0, lbo mode 0, layout type 0 = SWIZZLE_NONE
+  d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;  // layout SWIZZLE_128B
   return d;
 }
 
-// kind::f16 instruction descriptor: D f32, A/B f16 or bf16, both MN-major,
-// M = 128, N = 128.
+// kind::f16: D f32, A/B f16 or bf16, both MN-major, M = 128, N = 256
 __host__ __device__ constexpr uint32_t make_idesc(int ab_bf16) {
-  return (1u << 4)                      // c_format f32
-       | ((uint32_t)ab_bf16 << 7)       // a_format
-       | ((uint32_t)ab_bf16 << 10)      // b_format
-       | (1u << 15)                     // a major = MN
-       | (1u << 16)                     // b major = MN
-       | ((uint32_t)(kHT >> 3) << 17)   // N >> 3
-       | ((uint32_t)(kHT >> 4) << 24);  // M >> 4
+  return (1u << 4) | ((uint32_t)ab_bf16 << 7) | ((uint32_t)ab_bf16 << 10) | (1u << 15) |
+         (1u << 16) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
 }
 
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
 }
 
-// true when the phase completed, false after kWaitLimit polls
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
+// true when the phase completed; false on timeout (which raises the abort
+// flag) or when another role has aborted
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          bool sleep) {
+  const uint64_t t0 = gtimer();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_test(bar, parity)) return true;
+    if ((it & 63u) == 63u) {
+      if (*abort_flag) return false;
+      if (gtimer() - t0 > kWaitNs) {
+        *abort_flag = 1;
+        return false;
+      }
+    }
+    if (sleep) __nanosleep(64);
+  }
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  const int n = valid ? 16 : 0;  // 0 source bytes -> 16 zero bytes
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n)
+// the same wait for the shutdown path: ignores the abort flag
+__device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = gtimer();
+  while (!mbar_test(bar, parity)) {
+    if (gtimer() - t0 > kWaitNs) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float e) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(e)
                : "memory");
 }
 
-// Stage the (tokens t0..t0+64) x (columns c0..c0+128) slab of X into the
-// canonical MN-major layout. 1024 chunks of 16 B; lanes cover 8 K-rows x
-// 4 MN-groups so each warp's writes hit every bank once per 128 B.
-template <typename T>
-__device__ __forceinline__ void load_slab(const T* __restrict__ X, int64_t T_tokens, int64_t d,
-                                          int64_t t0, int64_t c0, uint32_t sbase, int tid) {
-  const int lane = tid & 31, warp = tid >> 5;
-  const int r = lane & 7, gsub = lane >> 3;
-#pragma unroll
-  for (int it = 0; it < 8; ++it) {
-    // 4 warps x 8 iterations x (8 rows x 4 groups) = 64 rows x 16 groups
-    const int idx = it * 4 + warp;          // 0..31
-    const int kgrp = idx & 7;               // which 8-token group
-    const int ggrp = idx >> 3;              // which 4 MN-groups (0..3)
-    const int k = kgrp * 8 + r;             // token within stage
-    const int g = ggrp * 4 + gsub;          // MN-group (8 columns)
-    const int64_t t = t0 + k;
-    const int64_t c = c0 + g * 8;
-    const bool valid = (t < T_tokens) && (c < d);
-    const T* src = valid ? (X + t * d + c) : X;
-    const uint32_t dst = sbase + (uint32_t)g * kSBO + (uint32_t)kgrp * kLBO + (uint32_t)r * 16;
-    cp_async16(dst, src, valid);
-  }
-}
-
-template <typename T, int BF16>
-__global__ void __launch_bounds__(kHThreads, 1)
-hessian_tc_kernel(const T* __restrict__ X, int64_t T_tokens, int64_t d, float* __restrict__ H,
-                  int ntiles_1d, int* __restrict__ err_flag) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ uint64_t mma_bar[kHStages];
-  __shared__ uint32_t tmem_base_slot;
-  __shared__ int abort_flag;
-  const int tid = threadIdx.x;
-
-  // upper-triangle tile from the linear block index
-  int bi = 0, rem = blockIdx.x;
-  while (rem >= ntiles_1d - bi) {
-    rem -= ntiles_1d - bi;
+// i-block bi (128 rows) pairs with the j-blocks bj >= bi/2 (256 columns):
+// the ones that reach column >= row somewhere
+__device__ __forceinline__ void tile_of(int idx, int nbj, int& bi, int& bj) {
+  bi = 0;
+  for (;;) {
+    const int cnt = nbj - (bi >> 1);
+    if (idx < cnt) break;
+    idx -= cnt;
     ++bi;
   }
-  const int bj = bi + rem;
-  const int64_t i0 = (int64_t)bi * kHT, j0 = (int64_t)bj * kHT;
+  bj = (bi >> 1) + idx;
+}
 
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + kHStages * kStageBytes;
+template <int BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, int64_t d,
+                   float* __restrict__ H, int nbj, int* __restrict__ err_flag) {
+  extern __shared__ uint8_t dsm_raw[];
+  // 1024-byte alignment for the swizzled operand tiles
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* stage_base = smem;
+  float* stg = reinterpret_cast<float*>(smem + kStages * kStageBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kStgBytes);
+  // bars: full[4], empty[4], accf[2], acce[2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  int bi, bj;
+  tile_of(blockIdx.x, nbj, bi, bj);
+  const int i0 = bi * kBM, j0 = bj * kBN;
+  const int nchunks = (int)((T_tokens + kBK - 1) / kBK);
+  const int nseg = (nchunks + kSegChunks - 1) / kSegChunks;
+
+  auto full = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty = [&](int s) { return smem_u32(&bars[kStages + s]); };
+  auto accf = [&](int b) { return smem_u32(&bars[2 * kStages + b]); };
+  auto acce = [&](int b) { return smem_u32(&bars[2 * kStages + 2 + b]); };
 
   if (tid == 0) {
-    for (int s = 0; s < kHStages; ++s) mbar_init(&mma_bar[s], 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf(b), 1);
+      mbar_init(acce(b), 4);
+    }
+    *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    abort_flag = 0;
   }
-  if (tid < 32) {  // warp 0 allocates 128 TMEM columns
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                 ::"r"(smem_u32(&tmem_base_slot)), "r"(kHT));
+                 ::"r"(smem_u32(tmem_slot)), "r"(2 * kBN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const uint32_t tmem = tmem_base_slot;
+  const uint32_t tmem = *tmem_slot;
 
-  const int nchunks = (int)((T_tokens + kHK - 1) / kHK);
-  const uint32_t idesc = make_idesc(BF16);
-
-  // prologue: the first kHPD chunks
-  for (int s = 0; s < kHPD; ++s) {
-    if (s < nchunks) {
-      const int64_t t0 = (int64_t)s * kHK;
-      load_slab<T>(X, T_tokens, d, t0, i0, smem_u32(sA + s * kStageBytes), tid);
-      load_slab<T>(X, T_tokens, d, t0, j0, smem_u32(sB + s * kStageBytes), tid);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  }
-
-  // Stage s is reused every kHStages chunks; before refilling it for chunk
-  // cn the MMAs of chunk cn - kHStages (= c - 2) must be done. Every commit is
-  // waited exactly once, in order, so the per-stage parity stays in step.
-  uint32_t phase_bits = 0;
-  for (int c = 0; c < nchunks; ++c) {
-    const int s = c % kHStages;
-    const int cn = c + kHPD;
-    if (cn < nchunks) {
-      const int sn = cn % kHStages;
-      if (cn >= kHStages) {
-        if (!mbar_wait_bounded(&mma_bar[sn], (phase_bits >> sn) & 1u)) atomicExch(&abort_flag, 1);
-        phase_bits ^= (1u << sn);
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+      int issued = 0;
+      for (int c = 0; c < nchunks; ++c) {
+        const int s = c % kStages, r = c / kStages;
+        if (r > 0 && !mbar_wait(empty(s), (r - 1) & 1, abort_flag, false)) break;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full(s)),
+                     "r"(kStageBytes)
+                     : "memory");
+        const uint32_t a = smem_u32(stage_base + s * kStageBytes);
+        const uint32_t b = a + kABytes;
+        const int t0 = c * kBK;
+        tma_load_2d(a, &xmap, i0, t0, full(s));
+        tma_load_2d(a + kBoxBytes, &xmap, i0 + 64, t0, full(s));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tma_load_2d(b + q * kBoxBytes, &xmap, j0 + 64 * q, t0, full(s));
+        issued = c + 1;
       }
-      const int64_t t0 = (int64_t)cn * kHK;
-      load_slab<T>(X, T_tokens, d, t0, i0, smem_u32(sA + sn * kStageBytes), tid);
-      load_slab<T>(X, T_tokens, d, t0, j0, smem_u32(sB + sn * kStageBytes), tid);
+      // stopped early: every copy in flight must land before the CTA exits
+      if (issued < nchunks) {
+        const int first = issued > kStages ? issued - kStages : 0;
+        for (int c = first; c < issued; ++c) mbar_drain(full(c % kStages), (c / kStages) & 1);
+      }
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    asm volatile("cp.async.wait_group %0;" ::"n"(kHPD) : "memory");
-    // generic-proxy smem writes -> visible to the tensor core (async proxy)
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();
-    if (abort_flag) break;
-    if (tid == 0) {
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(BF16);
+      int last_commit = -1;
+      for (int c = 0; c < nchunks; ++c) {
+        const int s = c % kStages, r = c / kStages;
+        const int seg = c / kSegChunks, buf = seg & 1;
+        const bool seg_first = (c % kSegChunks) == 0;
+        const bool seg_last = (c % kSegChunks) == kSegChunks - 1 || c == nchunks - 1;
+        if (seg_first && seg >= 2) {
+          if (!mbar_wait(acce(buf), ((seg >> 1) - 1) & 1, abort_flag, false)) break;
+        }
+        if (!mbar_wait(full(s), r & 1, abort_flag, false)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a0 = smem_u32(stage_base + s * kStageBytes);
+        const uint32_t b0 = a0 + kABytes;
+        const uint32_t dacc = tmem + (uint32_t)(buf * kBN);
+#pragma unroll
+        for (int ks = 0; ks < kBK / 16; ++ks) {
+          const uint64_t da = make_desc_sw128(a0 + ks * 2 * kSBO);
+          const uint64_t db = make_desc_sw128(b0 + ks * 2 * kSBO);
+          const uint32_t accum = (seg_first && ks == 0) ? 0u : 1u;
+          asm volatile(
+              "{\n\t.reg .pred p;\n\t"
+              "setp.ne.b32 p, %4, 0;\n\t"
+              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+              ::"r"(dacc), "l"(da), "l"(db), "r"(idesc), "r"(accum));
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                     ::"r"(empty(s)) : "memory");
+        if (seg_last)
+          asm volatile(
+              "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+              ::"r"(accf(buf)) : "memory");
+        last_commit = c;
+      }
+      // stopped early: the MMAs in flight must finish before TMEM is freed
+      if (last_commit >= 0 && last_commit < nchunks - 1)
+        mbar_drain(empty(last_commit % kStages), (last_commit / kStages) & 1);
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5 ----------------
+    const int quarter = warp & 3;  // this warp may read TMEM lanes 32*quarter .. +31
+    const int row_base = i0 + 32 * quarter;
+    float* my_stg = stg + (warp - 2) * 32 * kStgPitch;
+    for (int seg = 0; seg < nseg; ++seg) {
+      const int buf = seg & 1;
+      const bool ok = mbar_wait(accf(buf), (seg >> 1) & 1, abort_flag, true);
+      if (!__all_sync(0xFFFFFFFFu, ok)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t a0 = smem_u32(sA + s * kStageBytes), b0 = smem_u32(sB + s * kStageBytes);
-#pragma unroll
-      for (int ks = 0; ks < kHK / 16; ++ks) {
-        // K slice of 16 tokens = K-groups 2ks, 2ks+1
-        const uint64_t da = make_desc(a0 + ks * 2 * kLBO);
-        const uint64_t db = make_desc(b0 + ks * 2 * kLBO);
-        const uint32_t accum = (c > 0 || ks > 0) ? 1u : 0u;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "setp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-            ::"r"(tmem), "l"(da), "l"(db), "r"(idesc), "r"(accum));
-      }
-      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                   ::"r"(smem_u32(&mma_bar[s])) : "memory");
-    }
-    __syncwarp();
-  }
-  asm volatile("cp.async.wait_all;" ::: "memory");
-  __syncthreads();
-
-  // drain: commits of chunks c >= nchunks - kHStages were not waited above
-  bool ok = !abort_flag;
-  if (ok) {
-    const int first = nchunks > kHStages ? nchunks - kHStages : 0;
-    for (int c = first; c < nchunks; ++c) {
-      const int s = c % kHStages;
-      if (!mbar_wait_bounded(&mma_bar[s], (phase_bits >> s) & 1u)) ok = false;
-      phase_bits ^= (1u << s);
-    }
-  }
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  __syncthreads();
-  ok = ok && !abort_flag;
-
-  if (ok && nchunks > 0) {
-    const int warp = tid >> 5, lane = tid & 31;
-    const int64_t row = i0 + warp * 32 + lane;   // TMEM lane = tile row
 #pragma unroll 1
-    for (int cb = 0; cb < kHT; cb += 32) {
-      uint32_t v[32];
-      const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)cb;
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-          "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-          "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
-            "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
-            "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]),
-            "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-            "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
-            "=r"(v[30]), "=r"(v[31])
-          : "r"(taddr));
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      if (row < d) {
+      for (int cb = 0; cb < kBN; cb += 32) {
+        uint32_t v[32];
+        const uint32_t taddr =
+            tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(buf * kBN + cb);
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+            "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+              "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]),
+              "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]),
+              "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+              "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
+              "=r"(v[30]), "=r"(v[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          const int64_t col = j0 + cb + q;
-          if (col < d) {
-            const float a = __uint_as_float(v[q]);
-            H[row * d + col] += a;
-            if (bi != bj) H[col * d + row] += a;
+        for (int q = 0; q < 32; ++q) my_stg[lane * kStgPitch + q] = __uint_as_float(v[q]);
+        __syncwarp();
+        const int col0 = j0 + cb;
+        const int sub = lane >> 3, quad = (lane & 7) * 4;
+        // direct (r, c), c >= r: 8 lanes per row, 4 columns per lane
+#pragma unroll 2
+        for (int it = 0; it < 8; ++it) {
+          const int rr = it * 4 + sub;
+          const int r = row_base + rr, c = col0 + quad;
+          if (r < d && c < d && c + 3 >= r) {
+            const float* s = my_stg + rr * kStgPitch + quad;
+            red_add4(H + (int64_t)r * d + c, (c >= r) ? s[0] : 0.f, (c + 1 >= r) ? s[1] : 0.f,
+                     (c + 2 >= r) ? s[2] : 0.f, s[3]);
           }
         }
+        // mirror (c, r), c > r: 8 lanes per column, 4 rows per lane
+#pragma unroll 2
+        for (int it = 0; it < 8; ++it) {
+          const int q = it * 4 + sub;
+          const int c = col0 + q, r = row_base + quad;
+          if (r < d && c < d && c > r) {
+            const float* s = my_stg + quad * kStgPitch + q;
+            red_add4(H + (int64_t)c * d + r, s[0], (c > r + 1) ? s[kStgPitch] : 0.f,
+                     (c > r + 2) ? s[2 * kStgPitch] : 0.f, (c > r + 3) ? s[3 * kStgPitch] : 0.f);
+          }
+        }
+        __syncwarp();
       }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0)
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(acce(buf)) : "memory");
     }
   }
-  if (!ok && tid == 0) atomicExch(err_flag, 1);
+
+  __syncwarp();
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (tid < 32)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kHT));
+  if (tid == 0 && *abort_flag) atomicExch(err_flag, 1);
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kBN));
+  }
 }
 
-constexpr size_t kHSmem = 2ull * kHStages * kStageBytes;  // 128 KiB
+constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + kStgBytes + 12 * 8 + 16;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
 
 }  // namespace
 }  // namespace exl3
@@ -279,33 +372,50 @@ extern "C" int exl3_hessian_accumulate(float* H, const void* X, int dtype, int64
   EXL3_REQUIRE(H && X && err_flag, "NULL pointer argument");
   EXL3_REQUIRE(dtype == 0 || dtype == 1, "dtype must be 0 (fp16) or 1 (bf16), got %d", dtype);
   EXL3_REQUIRE(d > 0 && d % 8 == 0, "d (%lld) must be a positive multiple of 8", (long long)d);
-  EXL3_REQUIRE(T >= 0, "token count must be non-negative");
+  EXL3_REQUIRE(d < (1ll << 20), "d too large");
+  EXL3_REQUIRE(T >= 0 && T < (1ll << 31) - 64, "token count must be in [0, 2^31 - 64)");
   EXL3_REQUIRE(reinterpret_cast<uintptr_t>(X) % 16 == 0, "X must be 16-byte aligned");
+  EXL3_REQUIRE(reinterpret_cast<uintptr_t>(H) % 16 == 0, "H must be 16-byte aligned");
   if (T == 0) return EXL3_OK;
-  const int nt = (int)((d + kHT - 1) / kHT);
-  const int64_t ntiles = (int64_t)nt * (nt + 1) / 2;
-  EXL3_REQUIRE(ntiles < (1ll << 31), "d too large");
+  const int nbi = (int)((d + kBM - 1) / kBM);
+  const int nbj = (int)((d + kBN - 1) / kBN);
+  int64_t ntiles = 0;
+  for (int bi = 0; bi < nbi; ++bi) ntiles += nbj - (bi >> 1);
+
+  auto enc = encode_fn();
+  EXL3_REQUIRE(enc != nullptr, "cuTensorMapEncodeTiled is unavailable from the driver");
+  alignas(64) CUtensorMap map;
+  const cuuint64_t gdim[2] = {(cuuint64_t)d, (cuuint64_t)T};
+  const cuuint64_t gstride[1] = {(cuuint64_t)d * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kBK};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult cr =
+      enc(&map, dtype ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+          const_cast<void*>(X), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  EXL3_REQUIRE(cr == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)cr);
+
   static uint32_t attr_done[2] = {0u, 0u};  // per dtype, one bit per device
   int dev = 0;
   EXL3_CUDA(cudaGetDevice(&dev));
   const uint32_t bit = dev < 32 ? (1u << dev) : 0u;
   if (dtype == 0) {
     if (!(attr_done[0] & bit)) {
-      EXL3_CUDA(cudaFuncSetAttribute(hessian_tc_kernel<__half, 0>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHSmem));
+      EXL3_CUDA(cudaFuncSetAttribute(hessian_tma_kernel<0>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
       attr_done[0] |= bit;
     }
-    hessian_tc_kernel<__half, 0><<<(unsigned)ntiles, kHThreads, kHSmem, (cudaStream_t)stream>>>(
-        static_cast<const __half*>(X), T, d, H, nt, err_flag);
+    hessian_tma_kernel<0><<<(unsigned)ntiles, kThreads, kSmemBytes, (cudaStream_t)stream>>>(
+        map, T, d, H, nbj, err_flag);
   } else {
     if (!(attr_done[1] & bit)) {
-      EXL3_CUDA(cudaFuncSetAttribute(hessian_tc_kernel<__nv_bfloat16, 1>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kHSmem));
+      EXL3_CUDA(cudaFuncSetAttribute(hessian_tma_kernel<1>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
       attr_done[1] |= bit;
     }
-    hessian_tc_kernel<__nv_bfloat16, 1><<<(unsigned)ntiles, kHThreads, kHSmem,
-                                          (cudaStream_t)stream>>>(
-        static_cast<const __nv_bfloat16*>(X), T, d, H, nt, err_flag);
+    hessian_tma_kernel<1><<<(unsigned)ntiles, kThreads, kSmemBytes, (cudaStream_t)stream>>>(
+        map, T, d, H, nbj, err_flag);
   }
   EXL3_LAUNCHED();
   return EXL3_OK;

@@ -106,6 +106,27 @@ def test_hessian_accumulate_random(d, T, dtype):
     assert torch.equal(H, H.T)
 
 
+def test_hessian_long_accumulation_stays_within_tolerance():
+    """262,144 tokens in one call (32 accumulator segments): the drained
+    tensor-core chains keep the sum within 1e-4 of an fp32 GEMM."""
+    g = torch.Generator(device=DEV).manual_seed(11)
+    x = torch.randn(262144, 256, generator=g, device=DEV, dtype=torch.bfloat16)
+    x[:, 7] *= 16.0
+    H = torch.zeros(256, 256, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    from exl3_intel_arc_quantizer_b200._ext import ext
+
+    ext().hessian_accumulate_(H, x, err)
+    xf = x.float()
+    ref = xf.T @ xf
+    assert int(err.item()) == 0
+    assert _max_rel(H, ref) <= 1e-4
+    assert torch.equal(H, H.T)
+    H2 = torch.zeros(256, 256, device=DEV)
+    ext().hessian_accumulate_(H2, x, err)
+    assert torch.equal(H, H2)          # deterministic
+
+
 def test_collector_groups_share_hessians():
     from exl3_intel_arc_quantizer_b200.calibration import TransformerDecoderLayer, make_rotary_embeddings
 
