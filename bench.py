@@ -404,7 +404,12 @@ def run_b200(args):
             e1.record()
             e1.synchronize()
             ms4.append(e0.elapsed_time(e1))
-        k4 = world * n * len(ms4) / (sum(ms4) / 1e3)
+        t4 = sum(ms4)
+        if world > 1:
+            t = torch.tensor([t4], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t4 = float(t.item())
+        k4 = world * n * len(ms4) / (t4 / 1e3)
         enc4.arena.release()
 
     # e2e through the op binding with pinned host buffers
@@ -468,7 +473,7 @@ def run_b200(args):
                 "compare)",
         "kernel": "exl3::acs_pair_kernel (pass 1 + pass 2)" if K >= 2 else
                   "exl3::acs_kernel (pass 1 + pass 2)",
-        "acs_share_of_step": acs_ms.value / max(1e-9, total_ms / max(1, world)),
+        "acs_share_of_step": acs_ms.value / max(1e-9, sum(step_ms)),
         "traffic": traffic,
         "traffic_unit": "bytes per ACS launch (ncu dram read+write, 296-tile capture scaled "
                         "to the chunk)",
