@@ -114,18 +114,34 @@ def ldlq_column_sharded(weight: torch.Tensor, L: torch.Tensor, encode_tiles: Til
     if n % align:
         raise ValueError(f"columns ({n}) must be a multiple of {align} to shard")
     c0, c1 = shard_range(n, ws, rank, align)
-    sizes = [shard_range(n, ws, r, align) for r in range(ws)]
-    col_sizes = [e - s for s, e in sizes]
+    wq = enc = None
     if c1 > c0:
         local = ldlq(weight[:, c0:c1].contiguous(), L, encode_tiles, buf_size_k=buf_size_k)
         wq, enc = local.weight_q, local.encoded
     else:  # more ranks than column blocks: this rank contributes nothing
         wq = torch.empty((k, 0), dtype=weight.dtype, device=weight.device)
         enc = torch.empty((k // 16, 0, 256), dtype=torch.int16, device=weight.device)
-    weight_q = _all_gather_cat(wq, 1, col_sizes, group)
-    encoded = _all_gather_cat(enc, 1, [s // 16 for s in col_sizes], group)
+    weight_q, encoded = gather_column_slices(wq, enc, k, n, group, align)
     return LDLQResult(weight_q=weight_q, encoded=encoded, tiles_k=k // 16, tiles_n=n // 16,
                       buf_size_k=buf_size_k)
+
+
+def gather_column_slices(weight_q: Optional[torch.Tensor], encoded: Optional[torch.Tensor],
+                         k: int, n: int, group=None, align: int = 128
+                         ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """All-gather one module's LDLQ outputs from its column slices
+    (``shard_range(n, world, rank, align)`` per rank; ``None`` for a rank
+    with no slice) into the full ``weight_q`` (k, n) and ``encoded``
+    (k/16, n/16, 256) on every rank."""
+    ws, rank = dist.get_world_size(group), dist.get_rank(group)
+    sizes = [e - s for s, e in (shard_range(n, ws, r, align) for r in range(ws))]
+    dev = weight_q.device if weight_q is not None else torch.device(
+        "cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+    if weight_q is None:
+        weight_q = torch.empty((k, 0), dtype=torch.float32, device=dev)
+        encoded = torch.empty((k // 16, 0, 256), dtype=torch.int16, device=dev)
+    return (_all_gather_cat(weight_q, 1, sizes, group),
+            _all_gather_cat(encoded, 1, [s // 16 for s in sizes], group))
 
 
 def assign_modules(shapes: Dict[str, Tuple[int, int]], world_size: int) -> Dict[str, int]:

@@ -25,6 +25,7 @@ from .ldlq import (
     TileEncoder,
     block_ldl,
     ldlq,
+    ldlq_batched,
     make_xpu_tile_encoder,
 )
 from .regularize import RegularizeResult, regularize
@@ -90,35 +91,70 @@ def compute_proxy_loss(W: torch.Tensor, W_hat: torch.Tensor, H: torch.Tensor) ->
     return proxy, proxy / energy
 
 
-def quantize_linear_module(name: str, weight: torch.Tensor, H: torch.Tensor, K: int = 2,
-                           cb: int = CB_MUL1, tile_encoder: Optional[TileEncoder] = None,
-                           skip_g_scale: bool = True, buf_size_k: int = DEFAULT_BUF_SIZE_K,
-                           block_size: int = DEFAULT_BLOCK_SIZE) -> QuantizedModuleResult:
-    t0 = time.time()
+def _orient(weight: torch.Tensor, kdim: int) -> torch.Tensor:
+    """(k, n) fp32 copy: the quantized orientation has the Hessian's
+    dimension first (layer_quant.py:130-160)."""
     if weight.dim() != 2:
         raise ValueError(f"weight must be 2D, got shape {tuple(weight.shape)}")
-    kdim = H.shape[0]
     if weight.shape[1] == kdim:
-        W = weight.T.clone().to(torch.float32).contiguous()
-    elif weight.shape[0] == kdim:
-        W = weight.clone().to(torch.float32).contiguous()
-    else:
-        raise ValueError(f"Weight shape {tuple(weight.shape)} does not match Hessian dim {kdim}")
-    k, n = W.shape
-    device = W.device
-    su = torch.ones((k, 1), dtype=torch.float32, device=device)
-    sv = torch.ones((1, n), dtype=torch.float32, device=device)
+        return weight.T.clone().to(torch.float32).contiguous()
+    if weight.shape[0] == kdim:
+        return weight.clone().to(torch.float32).contiguous()
+    raise ValueError(f"Weight shape {tuple(weight.shape)} does not match Hessian dim {kdim}")
 
-    if tile_encoder is None:
-        if device.type != "cuda":
-            raise RuntimeError("quantize_linear_module needs CUDA tensors (no CPU encoder path)")
-        tile_encoder = make_xpu_tile_encoder(K=K, device_index=device.index or 0)
+
+def _check_encoder_k(tile_encoder, K: int) -> None:
     enc_k = getattr(tile_encoder, "K", None)
     if enc_k is not None and enc_k != K:
         raise ValueError(
             f"Tile encoder K={enc_k} does not match the requested K={K}. The trellis container "
             f"would be packed at {K} bpw while the encoder emitted {enc_k} bpw states. Build the "
             f"encoder with K={K}.")
+
+
+def _default_encoder(device: torch.device, K: int):
+    if device.type != "cuda":
+        raise RuntimeError("quantize_linear_module needs CUDA tensors (no CPU encoder path)")
+    return make_xpu_tile_encoder(K=K, device_index=device.index or 0)
+
+
+def _ldl_of(Hd: torch.Tensor, block_size: int) -> Tuple[BlockLDLResult, float]:
+    H_work = Hd.clone().contiguous()
+    blockwise_preapply_had_l_(H_work, HAD_DIM)
+    blockwise_preapply_had_r_(H_work, HAD_DIM)
+    ldl = block_ldl(H_work, block_size=block_size)
+    return ldl, compute_factorization_residual(H_work, ldl.cholesky)
+
+
+def _finish(name: str, K: int, cb: int, W: torch.Tensor, Hd: torch.Tensor,
+            reg: RegularizeResult, ldl: BlockLDLResult, fact_res: float, weight_q: torch.Tensor,
+            encoded: torch.Tensor, t0: float) -> QuantizedModuleResult:
+    k, n = W.shape
+    w_hat = weight_from_quantized(weight_q, reg.su, reg.sv)
+    diff = W - w_hat
+    mse = float(diff.pow(2).mean().item())
+    rel = float(torch.linalg.norm(diff).item() / max(1e-12, torch.linalg.norm(W).item()))
+    tile_dist = float((reg.weight - weight_q).pow(2).mean().item())
+    proxy, nproxy = compute_proxy_loss(W, w_hat, Hd)
+    metrics = ModuleMetrics(mse, rel, tile_dist, proxy, nproxy, fact_res, ldl.retries,
+                            reg.g_scale, time.time() - t0)
+    return QuantizedModuleResult(name, K, cb, (k, n), W, w_hat, encoded, reg.su, reg.sv,
+                                 metrics, reg, ldl)
+
+
+def quantize_linear_module(name: str, weight: torch.Tensor, H: torch.Tensor, K: int = 2,
+                           cb: int = CB_MUL1, tile_encoder: Optional[TileEncoder] = None,
+                           skip_g_scale: bool = True, buf_size_k: int = DEFAULT_BUF_SIZE_K,
+                           block_size: int = DEFAULT_BLOCK_SIZE) -> QuantizedModuleResult:
+    t0 = time.time()
+    W = _orient(weight, H.shape[0])
+    k, n = W.shape
+    device = W.device
+    su = torch.ones((k, 1), dtype=torch.float32, device=device)
+    sv = torch.ones((1, n), dtype=torch.float32, device=device)
+    if tile_encoder is None:
+        tile_encoder = _default_encoder(device, K)
+    _check_encoder_k(tile_encoder, K)
     g_scale_fn = None
     if not skip_g_scale:
         from .gss import g_scale_fn_from_encoder
@@ -128,23 +164,104 @@ def quantize_linear_module(name: str, weight: torch.Tensor, H: torch.Tensor, K: 
     Hd = H.to(device=device, dtype=torch.float32)
     reg = regularize(W, su, sv, H_diag=Hd.diagonal(), skip_g_scale=skip_g_scale,
                      g_scale_fn=g_scale_fn, had_dim=HAD_DIM)
-    H_work = Hd.clone().contiguous()
-    blockwise_preapply_had_l_(H_work, HAD_DIM)
-    blockwise_preapply_had_r_(H_work, HAD_DIM)
-    ldl = block_ldl(H_work, block_size=block_size)
-    fact_res = compute_factorization_residual(H_work, ldl.cholesky)
+    ldl, fact_res = _ldl_of(Hd, block_size)
     res = ldlq(reg.weight, ldl.transformed, tile_encoder, buf_size_k=buf_size_k)
-    w_hat = weight_from_quantized(res.weight_q, reg.su, reg.sv)
+    return _finish(name, K, cb, W, Hd, reg, ldl, fact_res, res.weight_q, res.encoded, t0)
 
-    diff = W - w_hat
-    mse = float(diff.pow(2).mean().item())
-    rel = float(torch.linalg.norm(diff).item() / max(1e-12, torch.linalg.norm(W).item()))
-    tile_dist = float((reg.weight - res.weight_q).pow(2).mean().item())
-    proxy, nproxy = compute_proxy_loss(W, w_hat, Hd)
-    metrics = ModuleMetrics(mse, rel, tile_dist, proxy, nproxy, fact_res, ldl.retries,
-                            reg.g_scale, time.time() - t0)
-    return QuantizedModuleResult(name, K, cb, (k, n), W, w_hat, res.encoded, reg.su, reg.sv,
-                                 metrics, reg, ldl)
+
+def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: int = 2,
+                     cb: int = CB_MUL1, tile_encoder: Optional[TileEncoder] = None,
+                     skip_g_scale: bool = True, buf_size_k: int = DEFAULT_BUF_SIZE_K,
+                     block_size: int = DEFAULT_BLOCK_SIZE,
+                     group=None) -> Dict[str, QuantizedModuleResult]:
+    """Quantize several ``name -> (weight, H)`` modules together, each with
+    exactly the arithmetic of :func:`quantize_linear_module`:
+
+    * the global-scale searches of all modules run as one batched search
+      (every candidate tile of every module in shared encoder launches);
+    * one block-LDL per distinct Hessian (q/k/v share one, gate/up share one);
+    * one interleaved LDLQ: each step encodes the current 16-row block of
+      every module in a single launch (``ldlq.ldlq_batched``).
+
+    With a process ``group`` (``torch.distributed``), every module's
+    128-aligned column slices are dealt over the ranks, each rank runs the
+    interleaved LDLQ on its slices, and one all-gather per module rebuilds
+    the full result on every rank (column slices never interact in LDLQ).
+    """
+    t0 = time.time()
+    if not modules:
+        return {}
+    names = list(modules)
+    device = modules[names[0]][0].device
+    if tile_encoder is None:
+        tile_encoder = _default_encoder(device, K)
+    _check_encoder_k(tile_encoder, K)
+
+    Ws, Hds, regs = {}, {}, {}
+    for nm in names:
+        weight, H = modules[nm]
+        W = _orient(weight, H.shape[0])
+        k, n = W.shape
+        Ws[nm] = W
+        Hds[nm] = H.to(device=W.device, dtype=torch.float32)
+        su = torch.ones((k, 1), dtype=torch.float32, device=W.device)
+        sv = torch.ones((1, n), dtype=torch.float32, device=W.device)
+        regs[nm] = regularize(W, su, sv, H_diag=Hds[nm].diagonal(), skip_g_scale=True,
+                              had_dim=HAD_DIM)
+    if not skip_g_scale:
+        from .gss import g_scale_search_batch, sample_scale_tiles
+
+        found = g_scale_search_batch([sample_scale_tiles(regs[nm].weight) for nm in names],
+                                     tile_encoder)
+        for nm, (g, _mse) in zip(names, found):
+            g = float(g)
+            if not g > 0.0:
+                raise ValueError(f"global-scale search returned a non-positive scale: {g}")
+            regs[nm].weight.mul_(g)
+            regs[nm].su.div_(g)
+            regs[nm].g_scale = g
+
+    # one block-LDL per distinct Hessian
+    ldls: List[Tuple[torch.Tensor, BlockLDLResult, float]] = []
+    ldl_of: Dict[str, int] = {}
+    for nm in names:
+        Hd = Hds[nm]
+        hit = next((i for i, (h, _, _) in enumerate(ldls)
+                    if h.shape == Hd.shape and (h.data_ptr() == Hd.data_ptr() or torch.equal(h, Hd))),
+                   None)
+        if hit is None:
+            ldl, fr = _ldl_of(Hd, block_size)
+            ldls.append((Hd, ldl, fr))
+            hit = len(ldls) - 1
+        ldl_of[nm] = hit
+
+    if group is None:
+        jobs = [(regs[nm].weight, ldls[ldl_of[nm]][1].transformed) for nm in names]
+        outs = ldlq_batched(jobs, tile_encoder, buf_size_k)
+        wq = {nm: o.weight_q for nm, o in zip(names, outs)}
+        enc = {nm: o.encoded for nm, o in zip(names, outs)}
+    else:
+        from .distributed import gather_column_slices, shard_range
+
+        import torch.distributed as dist
+
+        ws, rank = dist.get_world_size(group), dist.get_rank(group)
+        local = [nm for nm in names
+                 if (lambda r: r[1] > r[0])(shard_range(Ws[nm].shape[1], ws, rank, 128))]
+        jobs = []
+        for nm in local:
+            c0, c1 = shard_range(Ws[nm].shape[1], ws, rank, 128)
+            jobs.append((regs[nm].weight[:, c0:c1].contiguous(), ldls[ldl_of[nm]][1].transformed))
+        outs = dict(zip(local, ldlq_batched(jobs, tile_encoder, buf_size_k))) if jobs else {}
+        wq, enc = {}, {}
+        for nm in names:
+            k, n = Ws[nm].shape
+            o = outs.get(nm)
+            wq[nm], enc[nm] = gather_column_slices(
+                o.weight_q if o is not None else None, o.encoded if o is not None else None,
+                k, n, group)
+    return {nm: _finish(nm, K, cb, Ws[nm], Hds[nm], regs[nm], ldls[ldl_of[nm]][1],
+                        ldls[ldl_of[nm]][2], wq[nm], enc[nm], t0) for nm in names}
 
 
 def quantize_decoder_layer(layer: nn.Module, hessians: Dict[str, torch.Tensor], K: int = 2,

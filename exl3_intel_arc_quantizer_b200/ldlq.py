@@ -22,7 +22,7 @@ Same API and semantics as the reference ``exl3_quant/ldlq.py``
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Callable
+from typing import Sequence, Tuple, List, Callable
 
 import torch
 
@@ -108,8 +108,7 @@ def _as_int16_states(indices: torch.Tensor) -> torch.Tensor:
     return torch.where(v >= 0x8000, v - 0x10000, v).to(torch.int16)
 
 
-def ldlq(weight: torch.Tensor, L: torch.Tensor, encode_tiles: TileEncoder,
-         buf_size_k: int = DEFAULT_BUF_SIZE_K) -> LDLQResult:
+def _check_ldlq_args(weight: torch.Tensor, L: torch.Tensor, buf_size_k: int) -> int:
     if weight.dim() != 2:
         raise ValueError(f"weight must be 2-D, got shape {tuple(weight.shape)}")
     if weight.dtype != torch.float32:
@@ -133,8 +132,18 @@ def ldlq(weight: torch.Tensor, L: torch.Tensor, encode_tiles: TileEncoder,
     if k % buf != 0:
         raise ValueError(f"rows ({k}) must be divisible by buf_size_k ({buf}); "
                          "the bottom-up span walk assumes this")
+    return buf
 
+
+def _ldlq_steps(weight: torch.Tensor, L: torch.Tensor, buf: int):
+    """The LDLQ loop (ldlq.py:163-309) as a generator: yields each 16-row
+    block's tiles (tiles_n, 256) in encoder order and receives the encoder's
+    ``(recon, states)`` for them; returns the ``LDLQResult``. The op order is
+    the reference's: per span (bottom-up, ``buf`` rows) and 16-row block
+    (bottom-up), ``rows = W + L_slab^T (W - W_q)_below + prod_cache``, encode,
+    then the span's trailing ``prod_cache += L[span]^T (W - W_q)[span]``."""
     device = weight.device
+    k, n = weight.shape
     tiles_k, tiles_n = k // 16, n // 16
     perm = torch.as_tensor(tensor_core_perm(), dtype=torch.long, device=device)
     inv_perm = torch.as_tensor(tensor_core_perm_inv(), dtype=torch.long, device=device)
@@ -154,7 +163,7 @@ def ldlq(weight: torch.Tensor, L: torch.Tensor, encode_tiles: TileEncoder,
                 comp.addmm_(b_L[bj:, i + bi:i + bj].T, err_below, alpha=1.0, beta=1.0)
             rows = b_weight[bi:bj] + comp
             tiles = rows.reshape(16, tiles_n, 16).permute(1, 0, 2).reshape(tiles_n, 256)[:, perm]
-            q_w, q_i = encode_tiles(tiles)
+            q_w, q_i = yield tiles
             if q_w.shape != (tiles_n, 256) or q_i.shape != (tiles_n, 256):
                 raise ValueError("encode_tiles must return two (tiles_n, 256) tensors, got "
                                  f"{tuple(q_w.shape)} / {tuple(q_i.shape)}")
@@ -164,6 +173,48 @@ def ldlq(weight: torch.Tensor, L: torch.Tensor, encode_tiles: TileEncoder,
         prod_cache.addmm_(b_L.T, b_weight - b_weight_q, alpha=1.0, beta=1.0)
 
     return LDLQResult(weight_q, encoded, tiles_k, tiles_n, buf)
+
+
+def ldlq(weight: torch.Tensor, L: torch.Tensor, encode_tiles: TileEncoder,
+         buf_size_k: int = DEFAULT_BUF_SIZE_K) -> LDLQResult:
+    """LDLQ of one weight matrix (ldlq.py:163-309): one encoder call per
+    16-row block."""
+    return ldlq_batched([(weight, L)], encode_tiles, buf_size_k)[0]
+
+
+def ldlq_batched(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor]], encode_tiles: TileEncoder,
+                 buf_size_k: int = DEFAULT_BUF_SIZE_K) -> List[LDLQResult]:
+    """Several independent LDLQ loops advanced in lockstep: at every step the
+    current 16-row blocks of all unfinished jobs go to the encoder as ONE
+    batch. Each job's arithmetic is exactly its own ``ldlq`` (the encoder
+    treats every tile independently), so the results equal separate runs;
+    the GPU sees one large launch per step instead of one per module."""
+    gens, cur, results = [], [], [None] * len(jobs)
+    for weight, L in jobs:
+        buf = _check_ldlq_args(weight, L, buf_size_k)
+        gens.append(_ldlq_steps(weight, L, buf))
+    for idx, g in enumerate(gens):
+        cur.append(next(g))
+    active = list(range(len(gens)))
+    while active:
+        batch = [cur[a] for a in active]
+        sizes = [t.shape[0] for t in batch]
+        tiles = batch[0] if len(batch) == 1 else torch.cat(batch, dim=0)
+        q_w, q_i = encode_tiles(tiles)
+        if q_w.shape != tiles.shape or q_i.shape != tiles.shape:
+            raise ValueError("encode_tiles must return two (tiles_n, 256) tensors, got "
+                             f"{tuple(q_w.shape)} / {tuple(q_i.shape)}")
+        nxt = []
+        off = 0
+        for a, sz in zip(active, sizes):
+            try:
+                cur[a] = gens[a].send((q_w[off:off + sz], q_i[off:off + sz]))
+                nxt.append(a)
+            except StopIteration as stop:
+                results[a] = stop.value
+            off += sz
+        active = nxt
+    return results
 
 
 def make_xpu_tile_encoder(K: int = 2, device_index: int = 0, arena=None, sg_size: int = 32,
