@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-k4", action="store_true")
     ap.add_argument("--no-layer", action="store_true")
+    ap.add_argument("--decoder-layer-only", action="store_true",
+                    help="convert one config-4 decoder layer at K=2 and K=4 on all ranks and exit")
     ap.add_argument("--hessian-only", action="store_true",
                     help="time the Hessian accumulation on config 4 shapes and exit")
     ap.add_argument("--hessian-tokens", type=int, default=262144)
@@ -323,6 +325,67 @@ def run_hessian(device, tokens=262144, dims=(4096, 12288), steps=3, warmup=2):
             "peak_bf16_tflops_measured": peak, "groups": out}
 
 
+def run_decoder_layer(device, world, rank, K, seqs_total=128, seq_len=2048, hidden=4096,
+                      inter=12288, heads=32, kv_heads=8, batch_seqs=4):
+    """one decoder layer of a 9B-class GQA transformer
+    (hidden 4096, 32 q / 8 kv heads x 128, SwiGLU 12288), random-init bf16
+    weights (std 0.02, identical on every rank), calibration on 128 x 2048
+    synthetic N(0,1) tokens sharded over the ranks; all seven projections
+    converted (calibrate -> Hessian all-reduce -> quantize with column
+    sharding -> reload -> re-forward). Seconds are max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from exl3_intel_arc_quantizer_b200.calibration import TransformerDecoderLayer
+    from exl3_intel_arc_quantizer_b200.converter import convert_layer
+
+    group = dist.group.WORLD if world > 1 else None
+
+    def build(h, it, nh, nkv, seed):
+        torch.manual_seed(seed)
+        layer = TransformerDecoderLayer(h, it, nh, nkv)
+        with torch.no_grad():
+            for p in layer.parameters():
+                if p.dim() == 2:
+                    p.normal_(0.0, 0.02)
+        return layer.to(torch.bfloat16)
+
+    def make_hidden(nseq, s, h, seed):
+        g = torch.Generator(device=device).manual_seed(seed)
+        return [torch.randn(min(batch_seqs, nseq - i), s, h, generator=g, device=device,
+                            dtype=torch.float16) for i in range(0, nseq, batch_seqs)]
+
+    # warm-up on a small layer (extension load, cuBLAS/cuSOLVER handles)
+    convert_layer(build(512, 1024, 4, 2, 1), make_hidden(2, 128, 512, 5 + rank), K=K,
+                  device=device, group=group)
+    per_rank = seqs_total // world
+    hs = make_hidden(per_rank, seq_len, hidden, 1000 + rank)
+    layer = build(hidden, inter, heads, kv_heads, 7)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    res, nxt, tm = convert_layer(layer, hs, K=K, device=device, group=group)
+    torch.cuda.synchronize()
+    sec = time.perf_counter() - t0
+    phases = [tm.calibrate_s, tm.reduce_s, tm.quantize_s, tm.reload_reforward_s, sec]
+    if world > 1:
+        t = torch.tensor(phases, device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        phases = t.tolist()
+    rel = {m: r.metrics.relative_frobenius_error for m, r in res.items()}
+    del res, nxt, hs, layer
+    torch.cuda.empty_cache()
+    return {"workload": f"config 4: decoder layer h{hidden}/i{inter}/{heads}q{kv_heads}kv x128, "
+                        f"K={K}, {seqs_total}x{seq_len} calibration tokens over {world} GPU(s)",
+            "K": K, "seconds_per_layer": phases[4], "tiles": tm.tiles,
+            "tokens": seqs_total * seq_len,
+            "phases_s": {"calibrate": phases[0], "hessian_allreduce_finalize": phases[1],
+                         "quantize": phases[2], "reload_reforward": phases[3]},
+            "tiles_per_s": tm.tiles / phases[2],
+            "relative_frobenius_error": rel}
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -337,6 +400,14 @@ def run_b200(args):
     from exl3_intel_arc_quantizer_b200.xpu_quantizer import ScratchArena, XPUTrellisEncoder
 
     K, n = args.K, args.tiles
+    if args.decoder_layer_only:
+        out = {"decoder_layer": [run_decoder_layer(device, world, rank, k) for k in (2, 4)]}
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
     if args.hessian_only:
         if rank == 0:
             print(json.dumps({"hessian": run_hessian(device, tokens=args.hessian_tokens)}),
