@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-k4", action="store_true")
     ap.add_argument("--no-layer", action="store_true")
+    ap.add_argument("--no-decoder-layer", action="store_true")
     ap.add_argument("--decoder-layer-only", action="store_true",
                     help="convert one config-4 decoder layer at K=2 and K=4 on all ranks and exit")
     ap.add_argument("--hessian-only", action="store_true",
@@ -563,6 +564,11 @@ def run_b200(args):
     if rank == 0 and not args.no_layer:
         layer = run_layer(device)
         layer2 = run_layer(device, K=2, skip_g_scale=False)
+    if world > 1:
+        dist.barrier()
+    declayer = None
+    if not args.no_decoder_layer:
+        declayer = [run_decoder_layer(device, world, rank, k) for k in (2, 4)]
 
     if rank == 0:
         line = {
@@ -580,6 +586,7 @@ def run_b200(args):
             "k4_tiles_per_s": k4,
             "layer": layer,
             "layer_k2_gss": layer2,
+            "decoder_layer": declayer,
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
