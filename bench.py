@@ -550,12 +550,12 @@ def run_b200(args):
         "traffic_unit": "bytes per ACS launch (ncu dram read+write, 296-tile capture scaled "
                         "to the chunk)",
     }
-    from exl3_intel_arc_quantizer_b200.scratch_estimator import b200_backpointer_step_bytes
+    from exl3_intel_arc_quantizer_b200.scratch_estimator import b200_hbm_bytes_written_per_tile
 
-    bp_bytes_per_tile = 384 * b200_backpointer_step_bytes(K)   # 128 pass-1 + 256 pass-2 steps
-    roofline["backpointer_bytes_per_tile"] = bp_bytes_per_tile
-    roofline["hbm_backpointer_gbs"] = (tiles_timed * bp_bytes_per_tile
-                                       / (acs_ms.value / 1e3) / 1e9)
+    ck_bytes_per_tile = b200_hbm_bytes_written_per_tile(K)   # both passes' checkpoints
+    roofline["trellis_bytes_written_per_tile"] = ck_bytes_per_tile
+    roofline["hbm_trellis_write_gbs"] = (tiles_timed * ck_bytes_per_tile
+                                         / (acs_ms.value / 1e3) / 1e9)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

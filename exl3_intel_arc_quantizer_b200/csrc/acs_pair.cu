@@ -1,18 +1,30 @@
 // Tile-pair ACS encoder (K = 2..8): two tiles share one CTA, one per fp16
-// half2 lane.
+// half2 lane, with cost-vector checkpoints instead of per-step backpointers.
 //
 // Both tiles walk the same trellis, so a candidate's codebook value is one
 // scalar shared by the two lanes; everything per-tile (weight, accumulated
-// cost, branch choice) is a lane of one 32-bit register. Consequences:
+// cost) is a lane of one 32-bit register:
 //   * the cost vector is stored as {cost_A, cost_B} words in natural edge
 //     order: a predecessor cost is read as one word that already holds both
-//     lanes, and a result is written as one word -- no lane shuffles;
-//   * every barrier covers two tiles' work (half the barriers per tile) and
-//     each thread carries twice the independent dependency chains;
+//     lanes, and a result is written as one word;
 //   * threads take edges chunk-major (consecutive threads own consecutive
 //     chunks) so a warp's shared-memory stores are contiguous.
+//
+// Forward passes only compute minima (sub, fma on the fp16 FMA pipe, one
+// min on the ALU pipe per candidate): recording which branch won costs a
+// compare and a select per candidate on the ALU pipe, which bounded the
+// earlier tracked steps. Instead, the cost vector of every R-th step is also
+// copied to HBM as a checkpoint (R = 2 at K=2, every step above) by one bulk
+// copy from shared memory (ck_issue), which costs the warps nothing. The traceback walks the
+// path back from its end, recomputing from the nearest checkpoint only the
+// costs of the path's ancestors (Q^R loads and Q^R candidate evaluations per
+// R steps) with the same fp16 operations and the same first-minimum rule, so
+// the branches it finds are the ones a tracked forward pass would record.
+//
 // The arithmetic, tie-breaking and NaN behaviour are those of encoder.cu
-// (reference_encoder.py:130-324); only the data layout differs.
+// (reference_encoder.py:130-324): strict < over ascending k, a NaN at k=0
+// sticks, later NaNs never win; a tile pair with a NaN input runs
+// compare-and-select instead of min for its costs.
 #include "common.cuh"
 #include "encoder_shared.cuh"
 
@@ -31,24 +43,30 @@ struct PGeo {
   static constexpr int NCH = E / CE;                    // chunks per step
   static constexpr int NGC = SPLIT ? 1 : (((CE >> K) > 0) ? (CE >> K) : 1);
   static constexpr int KB = QT < 8 ? QT : 8;            // branches per load batch
-  static constexpr int EPW = SPLIT ? 1 : (K == 2 ? 8 : (K <= 4 ? 4 : 2));
-  static constexpr int NW = SPLIT ? 1 : (E + EPW - 1) / EPW;
-  static constexpr int BPS = SPLIT ? S * 4 : NW * kPairNT * 4;  // bytes / step / pair
+  static constexpr int R = (K == 2) ? 2 : 1;           // checkpoint stride
+  static constexpr int CKB = S * 4;                     // bytes per pair checkpoint
   static_assert(E * QT == 128, "codebook register budget: 128 values per thread");
 };
 
-int pair_bp_step_bytes(int K) {
-  switch (K) {
-    case 2: return PGeo<2>::BPS;
-    case 3: return PGeo<3>::BPS;
-    case 4: return PGeo<4>::BPS;
-    case 5: return PGeo<5>::BPS;
-    case 6: return PGeo<6>::BPS;
-    case 7: return PGeo<7>::BPS;
-    case 8: return PGeo<8>::BPS;
-    default: return 0;
-  }
+__host__ __device__ constexpr int ck_stride(int K) { return K == 2 ? 2 : 1; }
+
+// Checkpointed steps. Pass 1 (roll L/2): steps half-1, half-1+R, ... <= L-2,
+// the ones the end-state traceback over [half, L) needs. Pass 2 (roll 0):
+// steps R-1, 2R-1, ... <= L-2 (step -1 is the all-zero start).
+__host__ __device__ constexpr int ck_slots_pass1(int K, int L) {
+  return (L - L / 2 - 1) / ck_stride(K) + 1;
 }
+__host__ __device__ constexpr int ck_slots_pass2(int K, int L) { return (L - 1) / ck_stride(K); }
+
+int pair_ck_bytes_per_step_slot(int K) { return (65536 >> K) * 4; }
+
+size_t pair_ck_bytes(int K, int L) {
+  const int s1 = ck_slots_pass1(K, L), s2 = ck_slots_pass2(K, L);
+  const size_t b = (size_t)(s1 > s2 ? s1 : s2) * (size_t)pair_ck_bytes_per_step_slot(K);
+  return (b + 255) / 256 * 256;
+}
+
+size_t pair_tile_ws_bytes(int K, int L) { return pair_ck_bytes(K, L) / 2 + 8; }
 
 // Global edge of the thread's local edge le (chunk-major mapping).
 template <int K>
@@ -80,22 +98,13 @@ __device__ __forceinline__ void pair_init_codebook(uint32_t (&cbv)[64], int cb, 
   }
 }
 
-// acc + idx * 2^sh through the integer multiply-add (keeps the ALU pipe free).
-__device__ __forceinline__ uint32_t mad_shift(uint32_t idx, int sh, uint32_t acc) {
-  uint32_t r;
-  asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(idx), "r"(1u << sh), "r"(acc));
-  return r;
-}
-
 // One ACS step over both lanes.
 //   FIRST : step 0; pre2 = {pre_A, pre_B} wrap constraint (-1 = none)
-//   TRACK : record branch choices (COMPACT words) for the traceback
-//   EXACT : compare-and-select for the cost too (NaN-faithful)
-template <int K, bool FIRST, bool TRACK, bool EXACT>
+//   EXACT : compare-and-select for the cost (NaN-faithful) instead of min
+template <int K, bool FIRST, bool EXACT>
 __device__ __forceinline__ void pair_step(const uint32_t (&cbv)[64], uint32_t w2,
                                           const uint32_t* __restrict__ cin,
-                                          uint32_t* __restrict__ cout,
-                                          uint32_t* __restrict__ bp_step, int t, int preA,
+                                          uint32_t* __restrict__ cout, int t, int preA,
                                           int preB) {
   using G = PGeo<K>;
   if constexpr (!G::SPLIT) {
@@ -103,7 +112,7 @@ __device__ __forceinline__ void pair_step(const uint32_t (&cbv)[64], uint32_t w2
     for (int c = 0; c < G::NCH; ++c) {
       const int e0 = (c * kPairNT + t) * G::CE;
       const int g0 = e0 >> K;
-      uint32_t best[G::CE], idx[G::CE];
+      uint32_t best[G::CE];
 #pragma unroll
       for (int kb = 0; kb < G::QT; kb += G::KB) {
         uint32_t P[G::KB][G::NGC];
@@ -143,11 +152,8 @@ __device__ __forceinline__ void pair_step(const uint32_t (&cbv)[64], uint32_t w2
             }
             if (k == 0) {
               best[j] = cst;
-              idx[j] = 0;
-            } else if constexpr (TRACK || EXACT) {
-              const uint32_t msk = h2_lt_mask(cst, best[j]);
-              best[j] = EXACT ? bsel(msk, cst, best[j]) : h2_min(best[j], cst);
-              if constexpr (TRACK) idx[j] = bsel(msk, kconst(k), idx[j]);
+            } else if constexpr (EXACT) {
+              best[j] = bsel(h2_lt_mask(cst, best[j]), cst, best[j]);
             } else {
               best[j] = h2_min(best[j], cst);
             }
@@ -166,23 +172,12 @@ __device__ __forceinline__ void pair_step(const uint32_t (&cbv)[64], uint32_t w2
       } else {
         dst[0] = best[0];
       }
-      if constexpr (TRACK) {
-#pragma unroll
-        for (int a = 0; a < (G::CE + G::EPW - 1) / G::EPW; ++a) {
-          uint32_t acc = 0;
-#pragma unroll
-          for (int j = a * G::EPW; j < (a + 1) * G::EPW && j < G::CE; ++j)
-            acc = (j == a * G::EPW) ? idx[j] : mad_shift(idx[j], K * (j - a * G::EPW), acc);
-          const int w = (c * G::CE) / G::EPW + a;
-          bp_step[w * kPairNT + t] = acc;
-        }
-      }
     }
   } else {
     // K = 8: lanes t and t^1 split the 256 branches of edge t >> 1.
     const int e = t >> 1, r = t & 1;
     const int k0 = r * G::QT;
-    uint32_t best = kHInf2, idx = kconst(k0);
+    uint32_t best = kHInf2;
 #pragma unroll
     for (int kb = 0; kb < G::QT; kb += 8) {
       uint32_t P[8];
@@ -206,13 +201,12 @@ __device__ __forceinline__ void pair_step(const uint32_t (&cbv)[64], uint32_t w2
           }
         }
         if (kk == 0) {
+          // the lower range starts from its k = 0 candidate (a NaN there
+          // sticks); the upper range starts from +inf and skips NaNs
           const uint32_t msk = h2_lt_mask(cst, best) | (r == 0 ? 0xFFFFFFFFu : 0u);
           best = bsel(msk, cst, best);
-          if constexpr (TRACK) idx = bsel(msk, kconst(k), idx);
-        } else if constexpr (TRACK || EXACT) {
-          const uint32_t msk = h2_lt_mask(cst, best);
-          best = EXACT ? bsel(msk, cst, best) : h2_min(best, cst);
-          if constexpr (TRACK) idx = bsel(msk, kconst(k), idx);
+        } else if constexpr (EXACT) {
+          best = bsel(h2_lt_mask(cst, best), cst, best);
         } else {
           best = h2_min(best, cst);
         }
@@ -220,14 +214,8 @@ __device__ __forceinline__ void pair_step(const uint32_t (&cbv)[64], uint32_t w2
     }
     // lower branch range (r = 0) wins ties
     const uint32_t ob = __shfl_xor_sync(0xFFFFFFFFu, best, 1);
-    const uint32_t oi = __shfl_xor_sync(0xFFFFFFFFu, idx, 1);
     const uint32_t lo_c = r ? ob : best, hi_c = r ? best : ob;
-    const uint32_t lo_i = r ? oi : idx, hi_i = r ? idx : oi;
-    const uint32_t msk = h2_lt_mask(hi_c, lo_c);
-    if (r == 0) {
-      cout[e] = bsel(msk, hi_c, lo_c);
-      if constexpr (TRACK) bp_step[e] = bsel(msk, hi_i, lo_i);
-    }
+    if (r == 0) cout[e] = bsel(h2_lt_mask(hi_c, lo_c), hi_c, lo_c);
   }
 }
 
@@ -289,53 +277,79 @@ __device__ __forceinline__ void pair_argmin(const uint32_t* costs, uint32_t* red
   *outB = vb == 0xFFFFFFFFu ? 0 : (int)(vb & 0xFFFFu);
 }
 
-template <int K, bool EXACT>
-__device__ __forceinline__ void pair_pass1(const uint32_t (&cbv)[64], const uint32_t* wt,
-                                           uint32_t* c0, uint32_t* c1, uint8_t* bp, int L,
-                                           int t) {
-  using G = PGeo<K>;
-  const int half = L / 2;
-  pair_step<K, true, false, EXACT>(cbv, wt[half], nullptr, c0, nullptr, t, -1, -1);
-  __syncthreads();
-  for (int i = 1; i < half; ++i) {
-    const uint32_t* cin = (i & 1) ? c0 : c1;
-    uint32_t* cout = (i & 1) ? c1 : c0;
-    pair_step<K, false, false, EXACT>(cbv, wt[i + half], cin, cout, nullptr, t, -1, -1);
-    __syncthreads();
-  }
-  for (int i = half; i < L; ++i) {
-    const int ri = i - half;
-    const uint32_t* cin = (i & 1) ? c0 : c1;
-    uint32_t* cout = (i & 1) ? c1 : c0;
-    pair_step<K, false, true, EXACT>(cbv, wt[ri], cin, cout,
-                                     reinterpret_cast<uint32_t*>(bp + (size_t)ri * G::BPS), t,
-                                     -1, -1);
-    __syncthreads();
-  }
+// Checkpoints leave shared memory through the bulk-copy engine: after the
+// step's barrier one thread issues a single cp.async.bulk of the finished
+// cost vector (S x 4 bytes, 16-byte aligned) to its HBM slot; no warp spends
+// an instruction or an LSU slot on it. Writers order their shared-memory
+// stores for the async proxy first (ck_fence, before the barrier). The
+// buffer is rewritten two steps later, so the issuing thread waits until the
+// copy has finished reading it (ck_wait_read) before the next barrier.
+__device__ __forceinline__ void ck_fence() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void ck_issue(uint8_t* gdst, const uint32_t* ssrc, uint32_t bytes) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(ssrc));
+  asm volatile(
+      "cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n\t"
+      "cp.async.bulk.commit_group;" ::"l"(gdst), "r"(s), "r"(bytes)
+      : "memory");
+}
+__device__ __forceinline__ void ck_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void ck_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 template <int K, bool EXACT>
-__device__ __forceinline__ void pair_pass2(const uint32_t (&cbv)[64], const uint32_t* wt,
-                                           uint32_t* c0, uint32_t* c1, uint8_t* bp, int L,
-                                           int t, int preA, int preB) {
+__device__ __forceinline__ void pair_pass1(const uint32_t (&cbv)[64], const uint32_t* wt,
+                                           uint32_t* c0, uint32_t* c1, uint8_t* ckp, int L,
+                                           int t) {
   using G = PGeo<K>;
-  pair_step<K, true, true, EXACT>(cbv, wt[0], nullptr, c0, reinterpret_cast<uint32_t*>(bp), t,
-                                  preA, preB);
+  const int half = L / 2;
+  pair_step<K, true, EXACT>(cbv, wt[half], nullptr, c0, t, -1, -1);
   __syncthreads();
   for (int i = 1; i < L; ++i) {
     const uint32_t* cin = (i & 1) ? c0 : c1;
     uint32_t* cout = (i & 1) ? c1 : c0;
-    pair_step<K, false, true, EXACT>(cbv, wt[i], cin, cout,
-                                     reinterpret_cast<uint32_t*>(bp + (size_t)i * G::BPS), t,
-                                     -1, -1);
+    pair_step<K, false, EXACT>(cbv, wt[i < half ? i + half : i - half], cin, cout, t, -1, -1);
+    const int rel = i - (half - 1);
+    const bool ckpt = rel >= 0 && rel % G::R == 0 && i <= L - 2;
+    if (ckpt) ck_fence();
+    if (t == 0) ck_wait_read();  // the copy of step i-1 read the buffer step i+1 rewrites
     __syncthreads();
+    if (ckpt && t == 0) ck_issue(ckp + (size_t)(rel / G::R) * G::CKB, cout, G::CKB);
   }
+  if (t == 0) ck_wait_read();
+}
+
+template <int K, bool EXACT>
+__device__ __forceinline__ void pair_pass2(const uint32_t (&cbv)[64], const uint32_t* wt,
+                                           uint32_t* c0, uint32_t* c1, uint8_t* ckp, int L,
+                                           int t, int preA, int preB) {
+  using G = PGeo<K>;
+  pair_step<K, true, EXACT>(cbv, wt[0], nullptr, c0, t, preA, preB);
+  const bool ck0 = G::R == 1 && L >= 2;
+  if (ck0) ck_fence();
+  __syncthreads();
+  if (ck0 && t == 0) ck_issue(ckp, c0, G::CKB);
+  for (int i = 1; i < L; ++i) {
+    const uint32_t* cin = (i & 1) ? c0 : c1;
+    uint32_t* cout = (i & 1) ? c1 : c0;
+    pair_step<K, false, EXACT>(cbv, wt[i], cin, cout, t, -1, -1);
+    const bool ckpt = (i + 1) % G::R == 0 && i <= L - 2;
+    if (ckpt) ck_fence();
+    if (t == 0) ck_wait_read();
+    __syncthreads();
+    if (ckpt && t == 0) ck_issue(ckp + (size_t)((i + 1) / G::R - 1) * G::CKB, cout, G::CKB);
+  }
+  if (t == 0) ck_wait_read();
 }
 
 template <int K, int PASS>
 __global__ void __launch_bounds__(kPairNT, 1)
-acs_pair_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* __restrict__ bp,
-                size_t bp_pair_bytes, int32_t* __restrict__ best_edge,
+acs_pair_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* __restrict__ ck,
+                size_t ck_pair_bytes, int32_t* __restrict__ best_edge,
                 const int32_t* __restrict__ end_state, float* __restrict__ path_cost) {
   using G = PGeo<K>;
   extern __shared__ __align__(16) uint8_t smem[];
@@ -349,12 +363,12 @@ acs_pair_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* __r
   const int npairs = (n + 1) / 2;
   for (int tp = blockIdx.x; tp < npairs; tp += gridDim.x) {
     const int nan = pair_load(in, n, L, tp, wt, t);
-    uint8_t* pbp = bp + (size_t)tp * bp_pair_bytes;
+    uint8_t* pck = ck + (size_t)tp * ck_pair_bytes;
     const uint32_t* fin = ((L - 1) & 1) ? c1 : c0;
     const int ta = 2 * tp, tb = 2 * tp + 1;
     if constexpr (PASS == 1) {
-      if (nan) pair_pass1<K, true>(cbv, wt, c0, c1, pbp, L, t);
-      else     pair_pass1<K, false>(cbv, wt, c0, c1, pbp, L, t);
+      if (nan) pair_pass1<K, true>(cbv, wt, c0, c1, pck, L, t);
+      else     pair_pass1<K, false>(cbv, wt, c0, c1, pck, L, t);
       int ea, eb;
       pair_argmin<K>(fin, red, t, &ea, &eb);
       if (t == 0) {
@@ -364,8 +378,8 @@ acs_pair_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* __r
     } else {
       const int preA = end_state[ta];
       const int preB = (tb < n) ? end_state[tb] : preA;
-      if (nan) pair_pass2<K, true>(cbv, wt, c0, c1, pbp, L, t, preA, preB);
-      else     pair_pass2<K, false>(cbv, wt, c0, c1, pbp, L, t, preA, preB);
+      if (nan) pair_pass2<K, true>(cbv, wt, c0, c1, pck, L, t, preA, preB);
+      else     pair_pass2<K, false>(cbv, wt, c0, c1, pck, L, t, preA, preB);
       if (t == 0 && path_cost) {
         path_cost[ta] = half_bits_to_float((uint16_t)(fin[preA] & 0xFFFFu));
         if (tb < n) path_cost[tb] = half_bits_to_float((uint16_t)(fin[preB] >> 16));
@@ -373,62 +387,174 @@ acs_pair_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* __r
     }
     __syncthreads();
   }
+  if (t == 0) ck_wait_all();
 }
 
-// Branch recorded for (step, edge e, lane b) in the pair layout.
+// ---------------------------------------------------------------------------
+// Traceback from checkpoints (one warp per tile)
+// ---------------------------------------------------------------------------
+
+constexpr int kTbVals = 256;  // per-warp ancestor costs (at most Q + Q^2 + ... <= 256)
+
+__device__ __forceinline__ uint16_t h_sub(uint16_t a, uint16_t b) {
+  uint16_t r;
+  asm("sub.rn.f16 %0, %1, %2;" : "=h"(r) : "h"(a), "h"(b));
+  return r;
+}
+__device__ __forceinline__ uint16_t h_fma(uint16_t a, uint16_t b, uint16_t c) {
+  uint16_t r;
+  asm("fma.rn.f16 %0, %1, %2, %3;" : "=h"(r) : "h"(a), "h"(b), "h"(c));
+  return r;
+}
+
+// Ordering key of candidate k with cost bits v under the sequential rule
+// (strict < over ascending k; a NaN at k = 0 wins; later NaNs never win):
+// the smallest key is the candidate a forward pass keeps. Costs are >= +0,
+// so their bits order as unsigned integers.
+__device__ __forceinline__ uint32_t cand_key(int k, uint16_t v) {
+  const bool nan = (v & 0x7C00u) == 0x7C00u && (v & 0x03FFu) != 0u;
+  if (nan) return k == 0 ? 0u : 0xFFFFFFFFu;
+  return (((uint32_t)v + 1u) << 16) | (uint32_t)k;
+}
+
+// Cost of candidate k into edge x at step s. prev = predecessor's cost after
+// step s-1 (0 before step 0); at step 0 of a constrained pass, a candidate
+// whose predecessor is not `pre` costs +inf.
 template <int K>
-__device__ __forceinline__ int pair_bp_branch(const uint8_t* step_base, int e, int b) {
+__device__ __forceinline__ uint16_t cand_cost(int cb, int k, int x, uint16_t w, uint16_t prev,
+                                              bool first, int pre) {
   using G = PGeo<K>;
-  if constexpr (!G::SPLIT) {
-    const int c = e / (kPairNT * G::CE);
-    const int t = (e / G::CE) % kPairNT;
-    const int le = c * G::CE + e % G::CE;
-    const int w = le / G::EPW, pos = le % G::EPW;
-    const uint32_t word = reinterpret_cast<const uint32_t*>(step_base)[w * kPairNT + t];
-    return (int)((word >> (16 * b + K * pos)) & (G::Q - 1));
-  } else {
-    const uint32_t word = reinterpret_cast<const uint32_t*>(step_base)[e];
-    return (int)((word >> (16 * b)) & (G::Q - 1));
+  const uint16_t v = cb_state_bits(cb, ((uint32_t)k << G::Kr) | (uint32_t)x);
+  const uint16_t d = h_sub(v, w);
+  uint16_t c = h_fma(d, d, prev);
+  if (first && pre >= 0 && (((k << G::GB) | (x >> K)) != pre)) c = 0x7C00u;
+  return c;
+}
+
+// Walk the path back from `e_top` at step `i_top` down to step `i_stop`
+// (inclusive) for lane b of a pair. PASS 1: roll L/2, first checkpoint at
+// half-1, returns the edge before step i_stop (the end state). PASS 2: roll
+// 0, constrained start `pre`, writes each step's state to st[].
+template <int K, int PASS>
+__device__ int ck_walk(const uint8_t* __restrict__ pck, int b, int cb, const uint16_t* w,
+                       int L, int e_top, int pre, uint16_t* vals, uint16_t* st, int lane) {
+  using G = PGeo<K>;
+  const int half = L / 2;
+  const int i_stop = PASS == 1 ? half : 0;
+  int i = L - 1, e = e_top;
+  while (i >= i_stop) {
+    // nearest checkpoint c <= i - 1 (c = -1: the all-zero start of pass 2)
+    int c, slot;
+    if (PASS == 1) {
+      const int rel = ((i - 1) - (half - 1)) / G::R;
+      c = (half - 1) + rel * G::R;
+      slot = rel;
+    } else {
+      c = (i / G::R) * G::R - 1;
+      slot = (c + 1) / G::R - 1;
+    }
+    const int D = i - 1 - c;  // levels recomputed above the checkpoint
+    const int Lv = D + 1;     // level of the checkpoint (step i - Lv == c)
+    // level m holds the costs after step i - m at the Q^m ancestors of e at
+    // depth m: node j <-> edge (j << (Kr - m*K)) | (e >> (m*K)); levels are
+    // packed one after another (level m starts at Q + Q^2 + ... + Q^(m-1))
+    auto off = [](int m) { return ((1 << (m * K)) - (1 << K)) / ((1 << K) - 1); };
+    const int nL = 1 << (Lv * K);
+    const uint32_t* ckw =
+        c >= 0 ? reinterpret_cast<const uint32_t*>(pck + (size_t)slot * G::CKB) : nullptr;
+    for (int j = lane; j < nL; j += 32) {
+      uint16_t v = 0;
+      if (ckw) {
+        const int x = (j << (G::Kr - Lv * K)) | (e >> (Lv * K));
+        v = (uint16_t)((ckw[x] >> (16 * b)) & 0xFFFFu);
+      }
+      vals[off(Lv) + j] = v;
+    }
+    __syncwarp();
+    for (int m = Lv - 1; m >= 1; --m) {
+      const int s = i - m;
+      const uint16_t ws = w[PASS == 1 ? (s < half ? s + half : s - half) : s];
+      const int nm = 1 << (m * K);
+      for (int j = lane; j < nm; j += 32) {
+        const int x = (j << (G::Kr - m * K)) | (e >> (m * K));
+        uint32_t bk = 0xFFFFFFFFu;
+        uint16_t bv = 0;
+        for (int k = 0; k < G::Q; ++k) {
+          const uint16_t prev = vals[off(m + 1) + ((k << (m * K)) | j)];
+          const uint16_t cst = cand_cost<K>(cb, k, x, ws, prev, PASS == 2 && s == 0, pre);
+          const uint32_t key = cand_key(k, cst);
+          if (key < bk) {
+            bk = key;
+            bv = cst;
+          }
+        }
+        vals[off(m) + j] = bv;
+      }
+      __syncwarp();
+    }
+    // the path through this segment: steps i .. c+1 (not below i_stop)
+    int j = 0;
+    for (int tt = 0; tt <= D && i - tt >= i_stop; ++tt) {
+      const int s = i - tt;
+      const uint16_t ws = w[PASS == 1 ? (s < half ? s + half : s - half) : s];
+      uint32_t bk = 0xFFFFFFFFu;
+      for (int k = lane; k < G::Q; k += 32) {
+        const uint16_t prev = vals[off(tt + 1) + ((k << (tt * K)) | j)];
+        const uint32_t key = cand_key(k, cand_cost<K>(cb, k, e, ws, prev, PASS == 2 && s == 0, pre));
+        bk = key < bk ? key : bk;
+      }
+      bk = __reduce_min_sync(0xFFFFFFFFu, bk);
+      const int k = (bk == 0u || bk == 0xFFFFFFFFu) ? 0 : (int)(bk & 0xFFFFu);
+      if (PASS == 2 && lane == 0) st[s] = (uint16_t)((k << G::Kr) | e);
+      j |= k << (tt * K);
+      e = (k << G::GB) | (e >> K);
+    }
+    __syncwarp();
+    i = c;
   }
+  return e;
 }
 
 template <int K>
-__global__ void pair_tb1_kernel(const uint8_t* __restrict__ bp, size_t bp_pair_bytes, int n,
-                                int L, const int32_t* __restrict__ best_edge,
-                                int32_t* __restrict__ end_state) {
-  using G = PGeo<K>;
-  const int tile = blockIdx.x * blockDim.x + threadIdx.x;
+__device__ __forceinline__ void tb_load_weights(const float* __restrict__ in, int tile, int L,
+                                                uint16_t* w, int lane) {
+  for (int i = lane; i < L; i += 32)
+    w[i] = __half_as_ushort(__float2half_rn(in[(size_t)tile * L + i]));
+  __syncwarp();
+}
+
+template <int K>
+__global__ void __launch_bounds__(32 * kTbWarps)
+pair_tb1_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck, size_t ck_pair_bytes,
+                int n, int L, int cb, const int32_t* __restrict__ best_edge,
+                int32_t* __restrict__ end_state) {
+  __shared__ uint16_t vals[kTbWarps][kTbVals];
+  __shared__ uint16_t w[kTbWarps][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x * kTbWarps + warp;
   if (tile >= n) return;
-  const uint8_t* pbp = bp + (size_t)(tile >> 1) * bp_pair_bytes;
-  const int b = tile & 1;
-  int e = best_edge[tile];
-  for (int ri = L / 2 - 1; ri >= 0; --ri) {
-    const int k = pair_bp_branch<K>(pbp + (size_t)ri * G::BPS, e, b);
-    e = (k << G::GB) | (e >> K);
-  }
-  end_state[tile] = e;
+  tb_load_weights<K>(in, tile, L, w[warp], lane);
+  const int e = ck_walk<K, 1>(ck + (size_t)(tile >> 1) * ck_pair_bytes, tile & 1, cb, w[warp], L,
+                              best_edge[tile], -1, vals[warp], nullptr, lane);
+  if (lane == 0) end_state[tile] = e;
 }
 
 template <int K>
-__global__ void pair_tb2_kernel(const uint8_t* __restrict__ bp, size_t bp_pair_bytes, int n,
-                                int L, int cb, const int32_t* __restrict__ end_state,
-                                float* __restrict__ out_w, int16_t* __restrict__ out_idx,
-                                int16_t* __restrict__ out_packed) {
-  using G = PGeo<K>;
+__global__ void __launch_bounds__(32 * kTbWarps)
+pair_tb2_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck, size_t ck_pair_bytes,
+                int n, int L, int cb, const int32_t* __restrict__ end_state,
+                float* __restrict__ out_w, int16_t* __restrict__ out_idx,
+                int16_t* __restrict__ out_packed) {
+  __shared__ uint16_t vals[kTbWarps][kTbVals];
+  __shared__ uint16_t w[kTbWarps][256];
   __shared__ uint16_t st[kTbWarps][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x * kTbWarps + warp;
   if (tile >= n) return;
-  const uint8_t* pbp = bp + (size_t)(tile >> 1) * bp_pair_bytes;
-  const int b = tile & 1;
-  if (lane == 0) {
-    int e = end_state[tile];
-    for (int i = L - 1; i >= 0; --i) {
-      const int k = pair_bp_branch<K>(pbp + (size_t)i * G::BPS, e, b);
-      st[warp][i] = (uint16_t)((k << G::Kr) | e);
-      e = (k << G::GB) | (e >> K);
-    }
-  }
+  tb_load_weights<K>(in, tile, L, w[warp], lane);
+  const int pre = end_state[tile];
+  ck_walk<K, 2>(ck + (size_t)(tile >> 1) * ck_pair_bytes, tile & 1, cb, w[warp], L, pre, pre,
+                vals[warp], st[warp], lane);
   __syncwarp();
   for (int i = lane; i < L; i += 32) {
     const uint16_t s = st[warp][i];
@@ -456,14 +582,14 @@ int pair_encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t*
     if (dev < 32) attr_done |= (1 << dev);
   }
   const size_t per_tile = pair_tile_ws_bytes(K, L);
-  const size_t bp_pair = pair_bp_bytes(K, L);
+  const size_t ck_pair = pair_ck_bytes(K, L);
   int64_t cap = (int64_t)(ws_bytes / per_tile) & ~(int64_t)1;  // whole pairs
   EXL3_REQUIRE(cap >= 2, "workspace of %zu bytes is smaller than one tile pair (%zu bytes)",
                ws_bytes, 2 * per_tile);
   if (cap > n) cap = (n + 1) & ~(int64_t)1;
   if (cap > (1 << 30)) cap = 1 << 30;
-  uint8_t* bp = ws;
-  int32_t* best_edge = reinterpret_cast<int32_t*>(ws + (size_t)(cap / 2) * bp_pair);
+  uint8_t* ck = ws;
+  int32_t* best_edge = reinterpret_cast<int32_t*>(ws + (size_t)(cap / 2) * ck_pair);
   int32_t* end_state = best_edge + cap;
   const int sms = sm_count();
   for (int64_t start = 0; start < n; start += cap) {
@@ -471,40 +597,35 @@ int pair_encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t*
     const int pairs = (m + 1) / 2;
     const int grid = pairs < sms ? pairs : sms;
     const float* cin = in + start * L;
+    const int tb_grid = (m + kTbWarps - 1) / kTbWarps;
     {
       LaunchTimer lt(stream, 0);
       acs_pair_kernel<K, 1><<<grid, kPairNT, PSmem<K>::bytes, stream>>>(
-          cin, m, L, cb, bp, bp_pair, best_edge, nullptr, nullptr);
+          cin, m, L, cb, ck, ck_pair, best_edge, nullptr, nullptr);
     }
     EXL3_LAUNCHED();
     {
       LaunchTimer lt(stream, 1);
-      pair_tb1_kernel<K><<<(m + 127) / 128, 128, 0, stream>>>(bp, bp_pair, m, L, best_edge,
-                                                              end_state);
+      pair_tb1_kernel<K><<<tb_grid, 32 * kTbWarps, 0, stream>>>(cin, ck, ck_pair, m, L, cb,
+                                                                best_edge, end_state);
     }
     EXL3_LAUNCHED();
     {
       LaunchTimer lt(stream, 0);
       acs_pair_kernel<K, 2><<<grid, kPairNT, PSmem<K>::bytes, stream>>>(
-          cin, m, L, cb, bp, bp_pair, nullptr, end_state, out_cost ? out_cost + start : nullptr);
+          cin, m, L, cb, ck, ck_pair, nullptr, end_state, out_cost ? out_cost + start : nullptr);
     }
     EXL3_LAUNCHED();
     {
       LaunchTimer lt(stream, 1);
-      pair_tb2_kernel<K><<<(m + kTbWarps - 1) / kTbWarps, 32 * kTbWarps, 0, stream>>>(
-          bp, bp_pair, m, L, cb, end_state, out_w + start * L, out_idx + start * L,
+      pair_tb2_kernel<K><<<tb_grid, 32 * kTbWarps, 0, stream>>>(
+          cin, ck, ck_pair, m, L, cb, end_state, out_w + start * L, out_idx + start * L,
           out_packed ? out_packed + start * 16 * K : nullptr);
     }
     EXL3_LAUNCHED();
   }
   return EXL3_OK;
 }
-
-size_t pair_bp_bytes(int K, int L) {
-  return ((size_t)L * pair_bp_step_bytes(K) + 255) / 256 * 256;
-}
-
-size_t pair_tile_ws_bytes(int K, int L) { return pair_bp_bytes(K, L) / 2 + 8; }
 
 int pair_encode(int K, const float* in, float* out_w, int16_t* out_idx, int16_t* out_packed,
                 float* out_cost, int64_t n, int cb, int L, uint8_t* ws, size_t ws_bytes,

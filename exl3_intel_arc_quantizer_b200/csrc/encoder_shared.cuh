@@ -66,8 +66,7 @@ struct LaunchTimer {
 };
 
 // tile-pair encoder (acs_pair.cu)
-int pair_bp_step_bytes(int K);
-size_t pair_bp_bytes(int K, int L);       // backpointer bytes of one tile pair
+size_t pair_ck_bytes(int K, int L);       // cost checkpoints of one tile pair
 size_t pair_tile_ws_bytes(int K, int L);  // workspace per tile (half a pair + scalars)
 int pair_encode(int K, const float* in, float* out_w, int16_t* out_idx, int16_t* out_packed,
                 float* out_cost, int64_t n, int cb, int L, uint8_t* ws, size_t ws_bytes,

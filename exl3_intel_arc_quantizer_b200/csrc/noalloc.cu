@@ -8,7 +8,7 @@
 // array below instead of a caller workspace.
 //
 //   * The array is a file-scope __device__ object of kNoAllocScratchBytes
-//     (32 MiB + 4 KiB). Every GPU that loads this code holds it until the
+//     (64 MiB + 4 KiB). Every GPU that loads this code holds it until the
 //     process exits.
 //   * Host code cannot use the symbol as a device address. The first call on
 //     a device, with that device current, looks the address up with
@@ -19,14 +19,14 @@
 //     start at zero; calls that overlap on the GPU (different streams, or
 //     different host threads) race on the array and must be serialized.
 //   * A call needing more scratch than the array holds is rejected with
-//     EXL3_EINVAL: at most 32 tiles at K=2 and L=256 (more at larger K).
+//     EXL3_EINVAL: at most 16 tiles at K=2 and L=256 (more at larger K).
 #include <mutex>
 
 #include "common.cuh"
 
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = (32u << 20) + (4u << 10);
+constexpr size_t kNoAllocScratchBytes = (64u << 20) + (4u << 10);
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 std::mutex g_noalloc_mu;

@@ -7,8 +7,9 @@ reference's scratch layout — ``temp_costs (B, 2, S)`` fp16 plus
 split passes still use.
 
 The B200 encoder itself needs far less: the cost vectors live in shared
-memory and the backpointers are the chosen K-bit branch per edge and step
-(:func:`b200_workspace_bytes`), e.g. 1 MiB per tile at K=2 against 8 MiB.
+memory; K = 1 stores the chosen branch per edge and step, K >= 2 stores a
+cost-vector checkpoint every step or two (:func:`b200_workspace_bytes`),
+e.g. 4 MiB per tile at K=2 against the reference layout's 8 MiB per pass.
 """
 
 from __future__ import annotations
@@ -109,21 +110,42 @@ class ScratchEstimator:
 
 
 def b200_backpointer_step_bytes(k: int) -> int:
-    """Backpointer bytes per trellis step of one tile in the B200 encoder.
+    """Backpointer bytes per trellis step of one tile in the single-tile
+    (K = 1) B200 encoder (mirrors ``Geo<1>::BPS`` in csrc/encoder.cu)."""
+    if k != 1:
+        raise ValueError("only the K = 1 encoder stores backpointers; K >= 2 stores "
+                         "cost checkpoints (b200_checkpoint_bytes)")
+    return 2 * 512 * 4
 
-    K = 1 encodes one tile per CTA (mirrors ``Geo<1>::BPS`` in csrc/encoder.cu);
-    K >= 2 encodes tile pairs, one per fp16 lane, and this is half of the
-    pair's step (``PGeo<K>::BPS`` in csrc/acs_pair.cu)."""
-    if not 1 <= k <= 8:
-        raise ValueError(f"K must be in 1..8, got {k}")
+
+def b200_checkpoint_stride(k: int) -> int:
+    """Steps between cost checkpoints of the tile-pair encoder (K >= 2)."""
+    return 2 if k == 2 else 1
+
+
+def b200_checkpoint_slots(k: int, t: int = 256) -> Tuple[int, int]:
+    """Checkpointed steps of pass 1 and pass 2 (``ck_slots_pass1/2`` in
+    csrc/acs_pair.cu)."""
+    r = b200_checkpoint_stride(k)
+    return (t - t // 2 - 1) // r + 1, (t - 1) // r
+
+
+def b200_checkpoint_bytes(k: int, t: int = 256) -> int:
+    """Checkpoint workspace of one tile pair (``pair_ck_bytes``): the larger
+    pass's slots x (65536 >> K) edges x 4 bytes, 256-byte aligned."""
+    s1, s2 = b200_checkpoint_slots(k, t)
+    b = max(s1, s2) * (65536 >> k) * 4
+    return -(-b // 256) * 256
+
+
+def b200_hbm_bytes_written_per_tile(k: int, t: int = 256) -> int:
+    """Trellis bytes one tile writes to HBM over both passes: K = 1 its
+    backpointers (t/2 + t steps); K >= 2 half of every checkpoint of the
+    pair."""
     if k == 1:
-        return 2 * 512 * 4
-    if k == 8:
-        return 256 * 4 // 2
-    edges = (65536 >> k) // 512                     # edges per thread
-    per_word = 8 if k == 2 else (4 if k <= 4 else 2)
-    words = -(-edges // per_word)
-    return words * 512 * 4 // 2
+        return (t // 2 + t) * b200_backpointer_step_bytes(1)
+    s1, s2 = b200_checkpoint_slots(k, t)
+    return (s1 + s2) * (65536 >> k) * 4 // 2
 
 
 def b200_workspace_bytes(k: int, t: int = 256, b: int = 1) -> int:
@@ -132,6 +154,5 @@ def b200_workspace_bytes(k: int, t: int = 256, b: int = 1) -> int:
     if k == 1:
         per = -(-(t * b200_backpointer_step_bytes(k)) // 256) * 256 + 8
         return b * per
-    pair = -(-(t * 2 * b200_backpointer_step_bytes(k)) // 256) * 256
     b = b + (b & 1)
-    return b * (pair // 2 + 8)
+    return b * (b200_checkpoint_bytes(k, t) // 2 + 8)

@@ -125,8 +125,8 @@ int exl3_pack_trellis(const int16_t* states, int16_t* packed, int64_t n, int K,
  * runtime's pool, or a plain C/FFI host without a device allocator that
  * must not call cudaMalloc, which synchronizes the device). No counterpart
  * in the reference. Same arguments and outputs as exl3_quantize_tiles minus
- * the workspace; the scratch is a fixed 32 MiB + 4 KiB __device__ array held
- * by every GPU that loads the library, shared by all calls: at most 32 tiles
+ * the workspace; the scratch is a fixed 64 MiB + 4 KiB __device__ array held
+ * by every GPU that loads the library, shared by all calls: at most 16 tiles
  * per call at K=2, L=256 (more at larger K), larger calls return EXL3_EINVAL.
  * The first call on a device resolves the array's address (make it before
  * any stream capture); calls that overlap on the GPU race on the scratch.

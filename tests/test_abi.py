@@ -44,8 +44,9 @@ def test_workspace_size_formula():
     for K in range(1, 9):
         for L in (256, 160):
             assert lib.exl3_quantize_tiles_ws_bytes(7, K, L) == b200_workspace_bytes(K, L, 7)
-    # K=2: 1 MiB of backpointers per tile; tiles are encoded in pairs
-    assert lib.exl3_quantize_tiles_ws_bytes(2, 2, 256) == 2 * (256 * 4096 + 8)
+    # K=2: 127 pass-2 cost checkpoints of 16,384 {cost_A, cost_B} words per
+    # tile pair, half per tile; tiles are encoded in pairs
+    assert lib.exl3_quantize_tiles_ws_bytes(2, 2, 256) == 2 * (127 * 16384 * 4 // 2 + 8)
     assert lib.exl3_quantize_tiles_ws_bytes(1, 2, 256) == lib.exl3_quantize_tiles_ws_bytes(2, 2, 256)
     assert lib.exl3_quantize_tiles_ws_bytes(1, 9, 256) == 0
     assert lib.exl3_quantize_tiles_ws_bytes(1, 2, 128) == 0

@@ -57,7 +57,7 @@ def test_no_alloc_entry_point_matches_workspace_entry_point():
     dev = torch.device("cuda", 0)
     stream = P(torch.cuda.current_stream(dev).cuda_stream)
     K, cb = 2, 2
-    for call, n in enumerate((32, 19)):           # two calls in a row, 2nd one odd
+    for call, n in enumerate((16, 11)):           # two calls in a row, 2nd one odd
         g = torch.Generator().manual_seed(100 + call)
         x = (torch.randn((n, 256), generator=g)
              * torch.exp(0.5 * torch.randn((n, 1), generator=g))).to(dev)
@@ -77,7 +77,7 @@ def test_no_alloc_entry_point_rejects_oversized_calls():
     dev = torch.device("cuda", 0)
     stream = P(torch.cuda.current_stream(dev).cuda_stream)
     x = torch.zeros((1, 256), device=dev)
-    rc = no_alloc(_ptr(x), _ptr(x), _ptr(x), None, None, 33, 2, 2, 256, stream)
+    rc = no_alloc(_ptr(x), _ptr(x), _ptr(x), None, None, 17, 2, 2, 256, stream)
     assert rc == -22
     msg = lib.exl3_last_error().decode()
-    assert "at most 32 tiles per call at K=2" in msg, msg
+    assert "at most 16 tiles per call at K=2" in msg, msg
