@@ -34,7 +34,8 @@ sys.path.insert(0, str(REPO))
 METRIC = "encoder tiles/s at K=2/4 (1/2/4/8 B200); seconds per 4096x4096 layer"
 PUBLISHED_K2_TILES_PER_S = 1711.5     # Arc B580, K=2 mul1, 65,536 tiles
 ACS_PER_TILE = 2 * 256 * 65536        # candidate add-compare-selects per tile (both passes)
-FP16_OPS_PER_ACS = 3                  # sub, fma, compare per candidate
+FP16_OPS_PER_ACS = 2                  # sub + fma per candidate on the fp16 FMA pipe
+                                      # (the running min is an ALU-pipe op)
 
 
 def parse():
@@ -531,24 +532,25 @@ def run_b200(args):
     traffic = None
     tfile = REPO / "profiles" / f"encoder_k{K}_dram_per_launch.json"
     if tfile.exists():
-        per = json.loads(tfile.read_text()).get("dram_bytes_per_tile_per_pass")
-        if per is not None:
-            # one ACS launch = one pass over a chunk; scaled from the ncu
-            # capture's 296 tiles (backpointer writes grow with the tile count)
+        prof = json.loads(tfile.read_text())
+        per = prof.get("dram_bytes_per_tile_per_pass")
+        if per is not None and prof.get("layout") == "cost checkpoints, bulk copies":
+            # one ACS launch = one pass over a chunk; per-tile bytes from an
+            # ncu capture of smaller launches, scaled by the chunk's tiles
             traffic = per * min(args.chunk, n)
     roofline = {
-        "bound": "fp16_alu",
+        "bound": "fp16_fma_pipe",
         "achieved": achieved / 1e9, "peak": peak / 1e9, "unit": "Gop/s",
         "frac": achieved / peak if peak else None,
         "peak_source": "measured live: exl3_probe_fp16x2_rate (fma.rn.f16x2 at full occupancy)",
-        "work": f"{ACS_PER_TILE} candidate ACS/tile x {FP16_OPS_PER_ACS} fp16 ops (sub, fma, "
-                "compare)",
+        "work": f"{ACS_PER_TILE} candidate ACS/tile x {FP16_OPS_PER_ACS} fp16 ops on the FMA "
+                "pipe (sub, fma; the min is on the ALU pipe)",
         "kernel": "exl3::acs_pair_kernel (pass 1 + pass 2)" if K >= 2 else
                   "exl3::acs_kernel (pass 1 + pass 2)",
         "acs_share_of_step": acs_ms.value / max(1e-9, sum(step_ms)),
         "traffic": traffic,
-        "traffic_unit": "bytes per ACS launch (ncu dram read+write, 296-tile capture scaled "
-                        "to the chunk)",
+        "traffic_unit": "bytes per ACS launch (ncu dram read+write per tile of a smaller "
+                        "launch, scaled to the chunk)",
     }
     from exl3_intel_arc_quantizer_b200.scratch_estimator import b200_hbm_bytes_written_per_tile
 
