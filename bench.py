@@ -344,13 +344,15 @@ def run_decoder_layer(device, world, rank, K, seqs_total=128, seq_len=2048, hidd
     group = dist.group.WORLD if world > 1 else None
 
     def build(h, it, nh, nkv, seed):
+        # weights as a checkpoint would hold them (bf16), already on the GPU:
+        # loading is outside the timed region
         torch.manual_seed(seed)
         layer = TransformerDecoderLayer(h, it, nh, nkv)
         with torch.no_grad():
             for p in layer.parameters():
                 if p.dim() == 2:
                     p.normal_(0.0, 0.02)
-        return layer.to(torch.bfloat16)
+        return layer.to(device=device, dtype=torch.bfloat16)
 
     def make_hidden(nseq, s, h, seed):
         g = torch.Generator(device=device).manual_seed(seed)

@@ -15,6 +15,8 @@ Every vector comes from the reference's own CPU code path:
   * float    — hadamard / regularize / calibration.HessianCollector
   * storage  — exl3_quant.serialization (pack/unpack_module_trellis,
                build_layer_tensors, decode_weight_from_storage)
+  * gss      — exl3_quant.gss (sample_scale_tiles, g_scale_search_batch with
+               the reference encoder)
 
 Inputs are seeded synthetic data with the shapes and distributions of the
 reference's tests and of the benchmark configurations.
@@ -301,6 +303,34 @@ def gen_module(out):
     return {"k": k, "n": n, "K": 2, "buf": 64, "seed": 31}
 
 
+def gen_gss(pool, out):
+    """gss.py: tile sampling and the two-stage global-scale search with the
+    reference encoder (encode calls mapped over the process pool)."""
+    sys.path.insert(0, REF)
+    import torch
+    from exl3_quant import gss
+
+    class PoolEncoder:
+        K = 2
+
+        def __call__(self, tiles):
+            arr = np.ascontiguousarray(tiles.detach().cpu().numpy(), dtype=np.float32)
+            res = pool.map(_encode_job, [(2, 2, 256, t, False) for t in arr], chunksize=4)
+            rec = np.stack([r[2] for r in res]).view(np.float16).astype(np.float32)
+            idx = np.stack([r[0] for r in res]).view(np.int16)
+            return torch.from_numpy(rec), torch.from_numpy(idx)
+
+    g = torch.Generator().manual_seed(41)
+    w = torch.randn(128, 256, generator=g) * 0.9
+    w[:, 5] *= 4.0
+    samples = gss.sample_scale_tiles(w, 3)
+    scale, mse = gss.g_scale_search_batch([samples], PoolEncoder())[0]
+    np.savez_compressed(out / "gss_golden.npz", weight_r=w.numpy(), samples=samples.numpy(),
+                        result=np.array([scale, mse], dtype=np.float64))
+    return {"shape": [128, 256], "K": 2, "tiles": int(samples.shape[0]),
+            "scale": scale, "mse": mse}
+
+
 def gen_storage(out):
     """serialization.py: module packing, unpacking and weight decode.
 
@@ -357,7 +387,7 @@ def main():
     global REF
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
-    ap.add_argument("--only", default="", help="comma list: encoder,forward,format,float,ldlq,module,storage")
+    ap.add_argument("--only", default="", help="comma list: encoder,forward,format,float,ldlq,module,storage,gss")
     ap.add_argument("--procs", type=int, default=os.cpu_count() or 1)
     args = ap.parse_args()
     REF = str(Path(args.reference).resolve())
@@ -383,6 +413,8 @@ def main():
             manifest["module"] = gen_module(HERE)
         if not only or "storage" in only:
             manifest["storage"] = gen_storage(HERE)
+        if not only or "gss" in only:
+            manifest["gss"] = gen_gss(pool, HERE)
     files = {}
     for f in sorted(HERE.glob("*.npz")):
         files[f.name] = hashlib.sha256(f.read_bytes()).hexdigest()
