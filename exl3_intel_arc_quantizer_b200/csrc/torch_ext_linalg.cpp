@@ -3,6 +3,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <vector>
+
 #include "../../include/exl3k.h"
 
 namespace {
@@ -117,7 +119,42 @@ void decode_weight(at::Tensor trellis, at::Tensor su, at::Tensor sv, at::Tensor 
         "decode_weight");
 }
 
+// LDLQ for several matrices in lockstep; the workspace comes from the
+// caching allocator of the tensors' device.
+void ldlq_(std::vector<at::Tensor> W, std::vector<at::Tensor> L, std::vector<at::Tensor> Wq,
+           std::vector<at::Tensor> enc, int64_t K, int64_t cb, int64_t buf) {
+  const size_t nj = W.size();
+  TORCH_CHECK(nj >= 1 && L.size() == nj && Wq.size() == nj && enc.size() == nj,
+              "W, L, W_q and encoded must be lists of the same non-zero length");
+  std::vector<exl3_ldlq_job> jobs(nj);
+  for (size_t i = 0; i < nj; ++i) {
+    check_f32_cuda_2d(W[i], "W");
+    check_f32_cuda_2d(L[i], "L");
+    check_f32_cuda_2d(Wq[i], "W_q");
+    const int64_t k = W[i].size(0), n = W[i].size(1);
+    TORCH_CHECK(L[i].size(0) == k && L[i].size(1) == k, "L must be (", k, ", ", k, ")");
+    TORCH_CHECK(Wq[i].size(0) == k && Wq[i].size(1) == n, "W_q must be (", k, ", ", n, ")");
+    TORCH_CHECK(enc[i].is_cuda() && enc[i].is_contiguous() && enc[i].scalar_type() == at::kShort &&
+                    enc[i].numel() == k * n,
+                "encoded must be a contiguous int16 CUDA tensor of k*n elements");
+    for (const at::Tensor* t : {&L[i], &Wq[i], &enc[i]})
+      TORCH_CHECK(t->device() == W[0].device(), "all tensors must be on the same device");
+    jobs[i] = {W[i].data_ptr<float>(), L[i].data_ptr<float>(), Wq[i].data_ptr<float>(),
+               enc[i].data_ptr<int16_t>(), k, n};
+  }
+  c10::cuda::CUDAGuard g(W[0].device());
+  const size_t bytes = exl3_ldlq_ws_bytes(jobs.data(), (int)nj, (int)K, (int)buf);
+  TORCH_CHECK(bytes > 0, "ldlq: invalid arguments: ", exl3_last_error());
+  auto ws = at::empty({(int64_t)bytes}, W[0].options().dtype(at::kByte));
+  check(exl3_ldlq(jobs.data(), (int)nj, (int)K, (int)cb, (int)buf, ws.data_ptr(), bytes,
+                  cur_stream(W[0])),
+        "ldlq");
+}
+
 void register_linalg_ops(pybind11::module& m) {
+  m.def("ldlq_", &ldlq_, pybind11::arg("W"), pybind11::arg("L"), pybind11::arg("W_q"),
+        pybind11::arg("encoded"), pybind11::arg("K"), pybind11::arg("cb"), pybind11::arg("buf"),
+        "LDLQ of several matrices in lockstep with the B200 encoder");
   m.def("unpack_trellis", &unpack_trellis, pybind11::arg("trellis"), pybind11::arg("states"),
         pybind11::arg("K"), "Container words -> 16-bit states");
   m.def("decode_weight", &decode_weight, pybind11::arg("trellis"), pybind11::arg("su"),

@@ -26,6 +26,7 @@ from .ldlq import (
     block_ldl,
     ldlq,
     ldlq_batched,
+    ldlq_native,
     make_xpu_tile_encoder,
 )
 from .regularize import RegularizeResult, regularize
@@ -165,8 +166,17 @@ def quantize_linear_module(name: str, weight: torch.Tensor, H: torch.Tensor, K: 
     reg = regularize(W, su, sv, H_diag=Hd.diagonal(), skip_g_scale=skip_g_scale,
                      g_scale_fn=g_scale_fn, had_dim=HAD_DIM)
     ldl, fact_res = _ldl_of(Hd, block_size)
-    res = ldlq(reg.weight, ldl.transformed, tile_encoder, buf_size_k=buf_size_k)
+    res = _run_ldlq([(reg.weight, ldl.transformed)], tile_encoder, K, buf_size_k)[0]
     return _finish(name, K, cb, W, Hd, reg, ldl, fact_res, res.weight_q, res.encoded, t0)
+
+
+def _run_ldlq(jobs, tile_encoder, K: int, buf_size_k: int):
+    """The device loop for the B200 encoder on CUDA tensors, the callback loop
+    (the reference's op sequence) for any other encoder."""
+    if (getattr(tile_encoder, "native_ldlq", False) and jobs
+            and all(w.is_cuda for w, _ in jobs)):
+        return ldlq_native(jobs, K, getattr(tile_encoder, "cb", CB_MUL1), buf_size_k)
+    return ldlq_batched(jobs, tile_encoder, buf_size_k)
 
 
 def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: int = 2,
@@ -237,7 +247,7 @@ def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: i
 
     if group is None:
         jobs = [(regs[nm].weight, ldls[ldl_of[nm]][1].transformed) for nm in names]
-        outs = ldlq_batched(jobs, tile_encoder, buf_size_k)
+        outs = _run_ldlq(jobs, tile_encoder, K, buf_size_k)
         wq = {nm: o.weight_q for nm, o in zip(names, outs)}
         enc = {nm: o.encoded for nm, o in zip(names, outs)}
     else:
@@ -252,7 +262,7 @@ def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: i
         for nm in local:
             c0, c1 = shard_range(Ws[nm].shape[1], ws, rank, 128)
             jobs.append((regs[nm].weight[:, c0:c1].contiguous(), ldls[ldl_of[nm]][1].transformed))
-        outs = dict(zip(local, ldlq_batched(jobs, tile_encoder, buf_size_k))) if jobs else {}
+        outs = dict(zip(local, _run_ldlq(jobs, tile_encoder, K, buf_size_k))) if jobs else {}
         wq, enc = {}, {}
         for nm in names:
             k, n = Ws[nm].shape

@@ -217,6 +217,32 @@ def ldlq_batched(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor]], encode_tiles
     return results
 
 
+def ldlq_native(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor]], K: int, cb: int = 2,
+                buf_size_k: int = DEFAULT_BUF_SIZE_K) -> List[LDLQResult]:
+    """The LDLQ loop of every ``(weight, L)`` job on the GPU (``exl3_ldlq``):
+    the same spans, blocks and feedback as :func:`ldlq` with the B200 encoder,
+    without a host round trip per block; all jobs advance in lockstep with one
+    encoder launch per step. The compensation and trailing products are the
+    library's own fp32 kernels (fixed summation order), so results are close
+    to, not bit-identical with, the cuBLAS products of :func:`ldlq`."""
+    from ._ext import ext, require_cuda
+
+    if not jobs:
+        return []
+    Ws, Ls, Wqs, encs = [], [], [], []
+    for weight, L in jobs:
+        buf = _check_ldlq_args(weight, L, buf_size_k)
+        require_cuda(weight.device)
+        k, n = weight.shape
+        Ws.append(weight.contiguous())
+        Ls.append(L.contiguous())
+        Wqs.append(torch.empty_like(Ws[-1]))
+        encs.append(torch.empty((k // 16, n // 16, 256), dtype=torch.int16, device=weight.device))
+    ext().ldlq_(Ws, Ls, Wqs, encs, int(K), int(cb), int(buf))
+    return [LDLQResult(wq, e, w.shape[0] // 16, w.shape[1] // 16, int(buf_size_k))
+            for w, wq, e in zip(Ws, Wqs, encs)]
+
+
 def make_xpu_tile_encoder(K: int = 2, device_index: int = 0, arena=None, sg_size: int = 32,
                           force_global_costs: bool = False,
                           traceback_mode: str = "gpu_resident") -> TileEncoder:
@@ -243,6 +269,7 @@ def make_xpu_tile_encoder(K: int = 2, device_index: int = 0, arena=None, sg_size
     encode.K = K
     encode.cb = CB_MUL1
     encode.encoder = enc
+    encode.native_ldlq = True   # quantize drivers may run the loop natively (ldlq_native)
     return encode
 
 

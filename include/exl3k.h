@@ -137,6 +137,33 @@ int exl3_quantize_tiles_noalloc(const float* in, float* out_w, int16_t* out_idx,
                                 int cb, int L, exl3_stream_t stream);
 
 /* ------------------------------------------------------------------ */
+/* LDLQ block-feedback loop                                            */
+/* ------------------------------------------------------------------ */
+
+/* One weight matrix for exl3_ldlq. All pointers are device pointers on the
+ * current device, row-major fp32 unless stated. */
+typedef struct exl3_ldlq_job {
+  const float* W;     /* (k, n) regularized weight (transformed basis) */
+  const float* L;     /* (k, k) block-LDL factor (unit diagonal blocks) */
+  float* W_q;         /* out (k, n): quantized weight in the same basis */
+  int16_t* encoded;   /* out (k/16, n/16, 256): trellis states, encoder order */
+  int64_t k, n;       /* k % buf == 0, n % 128 == 0 */
+} exl3_ldlq_job;
+
+/*
+ * The LDLQ loop (spans of `buf` rows bottom-up, 16-row blocks bottom-up,
+ * compensation through L, trailing update after each span) for 1..32
+ * independent matrices advanced in lockstep: every step encodes the current
+ * 16-row block of all unfinished matrices in one encoder launch. Replaces
+ * ldlq (exl3_quant/ldlq.py:163-309) with the B200 encoder as its tile
+ * encoder (make_xpu_tile_encoder, ldlq.py:344-387). exl3_ldlq_ws_bytes
+ * returns the workspace size (0 on invalid arguments).
+ */
+size_t exl3_ldlq_ws_bytes(const exl3_ldlq_job* jobs, int njobs, int K, int buf);
+int exl3_ldlq(const exl3_ldlq_job* jobs, int njobs, int K, int cb, int buf, void* ws,
+              size_t ws_bytes, exl3_stream_t stream);
+
+/* ------------------------------------------------------------------ */
 /* Storage side: container unpack and weight decode                    */
 /* ------------------------------------------------------------------ */
 

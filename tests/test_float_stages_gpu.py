@@ -191,3 +191,38 @@ def test_quantize_linear_module_close_to_reference(manifest):
     assert rel <= 1e-2
     assert abs(m.relative_frobenius_error - ref_m[1]) <= 0.02 * ref_m[1]
     assert abs(m.proxy_loss - ref_m[3]) <= 0.02 * abs(ref_m[3])
+
+
+def test_ldlq_native_loop(ldlq_golden):
+    """exl3_ldlq: identity L -> exactly the callback loop; golden cases ->
+    close to the reference (its compensation products round differently
+    from cuBLAS's); several jobs in lockstep == each job alone, bit for bit."""
+    from exl3_intel_arc_quantizer_b200.ldlq import ldlq_native
+
+    enc = make_xpu_tile_encoder(K=2)
+    g = torch.Generator(device="cpu").manual_seed(3)
+    w = torch.randn(128, 256, generator=g).to(DEV)
+    eye = torch.eye(128, device=DEV)
+    a = ldlq(w, eye, enc, buf_size_k=64)
+    b = ldlq_native([(w, eye)], K=2, buf_size_k=64)[0]
+    assert torch.equal(a.weight_q, b.weight_q) and torch.equal(a.encoded, b.encoded)
+    for name in ("k2_32x128", "k4_64x128"):
+        K, k, n, buf, seed = (int(v) for v in ldlq_golden[f"{name}/params"])
+        wg = torch.from_numpy(ldlq_golden[f"{name}/weight"]).to(DEV)
+        Lg = torch.from_numpy(ldlq_golden[f"{name}/L"]).to(DEV)
+        r = ldlq_native([(wg, Lg)], K=K, buf_size_k=buf)[0]
+        ref_q = torch.from_numpy(ldlq_golden[f"{name}/weight_q"])
+        rel = float(torch.linalg.norm(r.weight_q.cpu() - ref_q) / torch.linalg.norm(ref_q))
+        same = float((r.encoded.cpu() == torch.from_numpy(ldlq_golden[f"{name}/encoded"]))
+                     .all(dim=-1).float().mean())
+        print(f"native ldlq {name}: rel frob {rel:.3e}, identical tiles {same:.3f}")
+        assert rel <= 1e-2 and same >= 0.9
+    A = torch.randn(256, 32, generator=g).to(DEV)
+    L1 = block_ldl(A @ A.T / 32 + 0.1 * torch.eye(256, device=DEV)).transformed
+    w1 = torch.randn(256, 384, generator=g).to(DEV)
+    w2 = torch.randn(128, 128, generator=g).to(DEV)
+    L2 = block_ldl(w2 @ w2.T / 128 + torch.eye(128, device=DEV)).transformed
+    both = ldlq_native([(w1, L1), (w2, L2)], K=2)
+    for (wx, Lx), r in zip(((w1, L1), (w2, L2)), both):
+        one = ldlq_native([(wx, Lx)], K=2)[0]
+        assert torch.equal(one.weight_q, r.weight_q) and torch.equal(one.encoded, r.encoded)
