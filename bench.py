@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--no-k4", action="store_true")
     ap.add_argument("--no-layer", action="store_true")
     ap.add_argument("--no-decoder-layer", action="store_true")
+    ap.add_argument("--model-only", action="store_true",
+                    help="convert the config-5 model (32 decoder layers, K=4) on all ranks and exit")
+    ap.add_argument("--model-layers", type=int, default=32)
     ap.add_argument("--decoder-layer-only", action="store_true",
                     help="convert one config-4 decoder layer at K=2 and K=4 on all ranks and exit")
     ap.add_argument("--hessian-only", action="store_true",
@@ -390,6 +393,56 @@ def run_decoder_layer(device, world, rank, K, seqs_total=128, seq_len=2048, hidd
             "relative_frobenius_error": rel}
 
 
+def run_model(device, world, rank, K=4, nlayers=32, seqs_total=128, seq_len=2048, hidden=4096,
+              inter=12288, heads=32, kv_heads=8, batch_seqs=4):
+    """a 32-layer model of the config-4 decoder shape
+    converted layer by layer (calibrate on the current hidden states,
+    Hessian all-reduce, quantize with column sharding, reload, re-forward),
+    calibration tokens sharded over the ranks. Random-init bf16 weights
+    (std 0.02, identical on every rank), synthetic N(0,1) hidden states in
+    place of the (unquantized) embedding output. Seconds are max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from exl3_intel_arc_quantizer_b200.calibration import TransformerDecoderLayer
+    from exl3_intel_arc_quantizer_b200.converter import convert_layers
+
+    group = dist.group.WORLD if world > 1 else None
+    layers = []
+    for li in range(nlayers):
+        torch.manual_seed(1000 + li)
+        with torch.device(device):
+            layer = TransformerDecoderLayer(hidden, inter, heads, kv_heads)
+        with torch.no_grad():
+            for p in layer.parameters():
+                if p.dim() == 2:
+                    p.normal_(0.0, 0.02)
+        layers.append(layer.to(torch.bfloat16))
+    per_rank = seqs_total // world
+    g = torch.Generator(device=device).manual_seed(7 + rank)
+    hs = [torch.randn(min(batch_seqs, per_rank - i), seq_len, hidden, generator=g, device=device,
+                      dtype=torch.float16) for i in range(0, per_rank, batch_seqs)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    results, timings = convert_layers(layers, hs, K=K, device=device, group=group)
+    torch.cuda.synchronize()
+    sec = time.perf_counter() - t0
+    tiles = sum(t.tiles for t in timings)
+    if world > 1:
+        t = torch.tensor([sec], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        sec = float(t.item())
+    rel = [sum(r.metrics.relative_frobenius_error for r in res.values()) / len(res)
+           for res in results]
+    return {"workload": f"config 5: {nlayers} decoder layers h{hidden}/i{inter}/{heads}q{kv_heads}kv, "
+                        f"K={K}, {seqs_total}x{seq_len} calibration tokens over {world} GPU(s)",
+            "K": K, "layers": nlayers, "seconds": sec, "seconds_per_layer": sec / nlayers,
+            "tiles": tiles, "tiles_per_s_per_gpu": tiles / sec / world,
+            "mean_relative_frobenius_error_first_last": [rel[0], rel[-1]]}
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -404,6 +457,14 @@ def run_b200(args):
     from exl3_intel_arc_quantizer_b200.xpu_quantizer import ScratchArena, XPUTrellisEncoder
 
     K, n = args.K, args.tiles
+    if args.model_only:
+        out = {"model": run_model(device, world, rank, K=4, nlayers=args.model_layers)}
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
     if args.decoder_layer_only:
         out = {"decoder_layer": [run_decoder_layer(device, world, rank, k) for k in (2, 4)]}
         if rank == 0:

@@ -103,3 +103,61 @@ def test_product_has_no_cpu_encoder_path():
 
     with pytest.raises(RuntimeError, match="no CUDA device"):
         XPUTrellisEncoder(K=2).encode_tile(np.zeros(256, np.float32))
+
+
+class _LdlqJob(ctypes.Structure):
+    _fields_ = [("W", ctypes.c_void_p), ("L", ctypes.c_void_p), ("W_q", ctypes.c_void_p),
+                ("encoded", ctypes.c_void_p), ("k", ctypes.c_int64), ("n", ctypes.c_int64)]
+
+
+def test_float_and_storage_entry_points_validate_arguments():
+    """Argument checks of the LDLQ, storage, Hadamard and Hessian entry
+    points: status codes and messages, no device work (no GPU needed)."""
+    lib = _ext.lib()
+    P = ctypes.c_void_p
+    d = P(256)
+    lib.exl3_ldlq_ws_bytes.restype = ctypes.c_size_t
+    lib.exl3_ldlq_ws_bytes.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    lib.exl3_ldlq.restype = ctypes.c_int
+    lib.exl3_ldlq.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, P,
+                              ctypes.c_size_t, P]
+    good = (_LdlqJob * 1)(_LdlqJob(256, 256, 256, 256, 256, 512))
+    assert lib.exl3_ldlq_ws_bytes(good, 1, 2, 128) > 256 * 512 * 4
+    for job, msg in (((256, 256, 256, 256, 200, 512), b"multiple of buf"),
+                     ((256, 256, 256, 256, 256, 100), b"multiple of 128"),
+                     ((None, 256, 256, 256, 256, 512), b"NULL pointer")):
+        bad = (_LdlqJob * 1)(_LdlqJob(*job))
+        assert lib.exl3_ldlq(bad, 1, 2, 2, 128, d, 1 << 30, None) == EINVAL
+        assert msg in lib.exl3_last_error(), lib.exl3_last_error()
+        assert lib.exl3_ldlq_ws_bytes(bad, 1, 2, 128) == 0
+    assert lib.exl3_ldlq(good, 1, 2, 2, 24, d, 1 << 30, None) == EINVAL
+    assert lib.exl3_ldlq(good, 0, 2, 2, 128, d, 1 << 30, None) == EINVAL
+    assert lib.exl3_ldlq(good, 1, 9, 2, 128, d, 1 << 30, None) == EINVAL
+    assert lib.exl3_ldlq(good, 1, 2, 2, 128, d, 16, None) == EINVAL
+    assert b"smaller than" in lib.exl3_last_error()
+
+    f = lib.exl3_decode_weight
+    f.restype = ctypes.c_int
+    f.argtypes = [P, P, P, ctypes.c_int, P, P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                  ctypes.c_int, P]
+    assert f(d, d, d, 0, d, None, 4, 8, 2, 2, None) == EINVAL          # k = 64 not a 128-multiple
+    assert b"multiples of 128" in lib.exl3_last_error()
+    assert f(d, d, d, 2, d, None, 8, 8, 2, 2, None) == EINVAL          # scale dtype
+    assert f(d, d, d, 0, d, None, 8, 8, 9, 2, None) == EINVAL          # K
+    assert f(d, d, d, 0, d, None, 8, 8, 2, 3, None) == EINVAL          # codebook
+    g = lib.exl3_unpack_trellis
+    g.restype = ctypes.c_int
+    g.argtypes = [P, P, ctypes.c_int64, ctypes.c_int, P]
+    assert g(d, d, 4, 0, None) == EINVAL
+    assert g(d, d, 0, 2, None) == 0                                     # empty is a no-op
+    h = lib.exl3_hessian_accumulate
+    h.restype = ctypes.c_int
+    h.argtypes = [P, P, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, P, P]
+    assert h(d, d, 1, 16, 100, d, None) == EINVAL                       # d % 8
+    assert h(d, d, 2, 16, 128, d, None) == EINVAL                       # dtype
+    assert h(d, P(8), 1, 16, 128, d, None) == EINVAL                    # X alignment
+    assert h(d, d, 1, 0, 128, d, None) == 0                             # no tokens: no-op
+    r = lib.exl3_had128_right
+    r.restype = ctypes.c_int
+    r.argtypes = [P, ctypes.c_int64, ctypes.c_int64, P]
+    assert r(d, 4, 100, None) == EINVAL
