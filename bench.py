@@ -52,6 +52,7 @@ def parse():
     ap.add_argument("--no-k4", action="store_true")
     ap.add_argument("--no-layer", action="store_true")
     ap.add_argument("--no-decoder-layer", action="store_true")
+    ap.add_argument("--no-k-sweep", action="store_true")
     ap.add_argument("--model-only", action="store_true",
                     help="convert the config-5 model (32 decoder layers, K=4) on all ranks and exit")
     ap.add_argument("--model-layers", type=int, default=32)
@@ -524,29 +525,38 @@ def run_b200(args):
         dist.barrier()
     value = world * n * args.steps / (total_ms / 1e3)
 
-    # secondary: K=4 throughput (same workload, same timing rules)
-    k4 = None
-    if not args.no_k4 and K != 4:
-        enc4 = XPUTrellisEncoder(K=4, cb=2, device_index=local,
-                                 arena=ScratchArena(device_index=local, default_cap_b=args.chunk))
+    # secondary: the config-2 K sweep (same workload, same timing rules);
+    # K=4 is also reported on its own
+    def encoder_rate(Kx, reps):
+        ex = XPUTrellisEncoder(K=Kx, cb=2, device_index=local,
+                               arena=ScratchArena(device_index=local, default_cap_b=args.chunk))
         for _ in range(2):
-            enc4.encode_device(x)
-        ms4 = []
-        for _ in range(max(2, args.steps // 2)):
+            ex.encode_device(x)
+        ms = []
+        for _ in range(reps):
             flush.zero_()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            enc4.encode_device(x)
+            ex.encode_device(x)
             e1.record()
             e1.synchronize()
-            ms4.append(e0.elapsed_time(e1))
-        t4 = sum(ms4)
+            ms.append(e0.elapsed_time(e1))
+        tx = sum(ms)
         if world > 1:
-            t = torch.tensor([t4], device=device, dtype=torch.float64)
+            t = torch.tensor([tx], device=device, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            t4 = float(t.item())
-        k4 = world * n * len(ms4) / (t4 / 1e3)
-        enc4.arena.release()
+            tx = float(t.item())
+        ex.arena.release()
+        return world * n * len(ms) / (tx / 1e3)
+
+    k4 = None
+    if not args.no_k4 and K != 4:
+        k4 = encoder_rate(4, max(2, args.steps // 2))
+    ksweep = None
+    if not args.no_k_sweep:
+        ksweep = {str(kx): (value if kx == K else (k4 if (kx == 4 and k4) else
+                                                    encoder_rate(kx, 2)))
+                  for kx in (1, 2, 3, 4, 5, 6, 8)}
 
     # e2e through the op binding with pinned host buffers
     e2e = None
@@ -649,6 +659,7 @@ def run_b200(args):
                        "l2": "flushed between timed steps (512 MiB write)",
                        "parallelism": f"tiles sharded, {world} rank(s), no collective"},
             "k4_tiles_per_s": k4,
+            "k_sweep_tiles_per_s": ksweep,
             "layer": layer,
             "layer_k2_gss": layer2,
             "decoder_layer": declayer,

@@ -145,22 +145,38 @@ __device__ __forceinline__ void red_add4(float* p, float a, float b, float c, fl
 }
 
 // i-block bi (128 rows) pairs with the j-blocks bj >= bi/2 (256 columns):
-// the ones that reach column >= row somewhere
-__device__ __forceinline__ void tile_of(int idx, int nbj, int& bi, int& bj) {
-  bi = 0;
+// the ones that reach column >= row somewhere. Launch order walks groups of
+// 8 consecutive i-blocks column by column (bi fastest), so the CTAs resident
+// at one time share few A and B slabs of X in L2.
+constexpr int kRasterGroup = 8;
+
+__device__ __forceinline__ void tile_of(int idx, int nbi, int nbj, int& bi, int& bj) {
+  int g0 = 0;
   for (;;) {
-    const int cnt = nbj - (bi >> 1);
+    const int g1 = min(g0 + kRasterGroup, nbi);
+    int cnt = 0;
+    for (int b = g0; b < g1; ++b) cnt += nbj - (b >> 1);
     if (idx < cnt) break;
     idx -= cnt;
-    ++bi;
+    g0 = g1;
   }
-  bj = (bi >> 1) + idx;
+  const int glast = min(g0 + kRasterGroup, nbi) - 1;
+  for (int j = g0 >> 1;; ++j) {
+    const int hi = min(glast, 2 * j + 1);  // bj >= bi/2  <=>  bi <= 2*bj + 1
+    const int cnt = hi - g0 + 1;
+    if (idx < cnt) {
+      bi = g0 + idx;
+      bj = j;
+      return;
+    }
+    idx -= cnt;
+  }
 }
 
 template <int BF16>
 __global__ void __launch_bounds__(kThreads, 1)
 hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, int64_t d,
-                   float* __restrict__ H, int nbj, int* __restrict__ err_flag) {
+                   float* __restrict__ H, int nbi, int nbj, int* __restrict__ err_flag) {
   extern __shared__ uint8_t dsm_raw[];
   // 1024-byte alignment for the swizzled operand tiles
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -174,7 +190,7 @@ hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, i
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int bi, bj;
-  tile_of(blockIdx.x, nbj, bi, bj);
+  tile_of(blockIdx.x, nbi, nbj, bi, bj);
   const int i0 = bi * kBM, j0 = bj * kBN;
   const int nchunks = (int)((T_tokens + kBK - 1) / kBK);
   const int nseg = (nchunks + kSegChunks - 1) / kSegChunks;
@@ -407,7 +423,7 @@ extern "C" int exl3_hessian_accumulate(float* H, const void* X, int dtype, int64
       attr_done[0] |= bit;
     }
     hessian_tma_kernel<0><<<(unsigned)ntiles, kThreads, kSmemBytes, (cudaStream_t)stream>>>(
-        map, T, d, H, nbj, err_flag);
+        map, T, d, H, nbi, nbj, err_flag);
   } else {
     if (!(attr_done[1] & bit)) {
       EXL3_CUDA(cudaFuncSetAttribute(hessian_tma_kernel<1>,
@@ -415,7 +431,7 @@ extern "C" int exl3_hessian_accumulate(float* H, const void* X, int dtype, int64
       attr_done[1] |= bit;
     }
     hessian_tma_kernel<1><<<(unsigned)ntiles, kThreads, kSmemBytes, (cudaStream_t)stream>>>(
-        map, T, d, H, nbj, err_flag);
+        map, T, d, H, nbi, nbj, err_flag);
   }
   EXL3_LAUNCHED();
   return EXL3_OK;
