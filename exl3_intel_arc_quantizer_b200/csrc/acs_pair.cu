@@ -431,14 +431,27 @@ __device__ __forceinline__ uint16_t cand_cost(int cb, int k, int x, uint16_t w, 
   return c;
 }
 
+// Checkpoint geometry of the traceback: pair checkpoints hold {cost_A,
+// cost_B} words (stride PGeo<K>::R); the single-tile K=1 encoder's hold one
+// fp16 cost per edge every kSingleR steps.
+constexpr int kSingleR = 4;
+
+template <int K, bool SINGLE>
+struct WGeo {
+  static constexpr int R = SINGLE ? kSingleR : PGeo<K>::R;
+  static constexpr int CKB = SINGLE ? PGeo<K>::S * 2 : PGeo<K>::CKB;
+};
+
 // Walk the path back from `e_top` at step `i_top` down to step `i_stop`
-// (inclusive) for lane b of a pair. PASS 1: roll L/2, first checkpoint at
-// half-1, returns the edge before step i_stop (the end state). PASS 2: roll
-// 0, constrained start `pre`, writes each step's state to st[].
-template <int K, int PASS>
+// (inclusive) for lane b of a pair (or the one tile of a single-tile
+// checkpoint set). PASS 1: roll L/2, first checkpoint at half-1, returns the
+// edge before step i_stop (the end state). PASS 2: roll 0, constrained start
+// `pre`, writes each step's state to st[].
+template <int K, int PASS, bool SINGLE = false>
 __device__ int ck_walk(const uint8_t* __restrict__ pck, int b, int cb, const uint16_t* w,
                        int L, int e_top, int pre, uint16_t* vals, uint16_t* st, int lane) {
   using G = PGeo<K>;
+  using W = WGeo<K, SINGLE>;
   const int half = L / 2;
   const int i_stop = PASS == 1 ? half : 0;
   int i = L - 1, e = e_top;
@@ -446,12 +459,12 @@ __device__ int ck_walk(const uint8_t* __restrict__ pck, int b, int cb, const uin
     // nearest checkpoint c <= i - 1 (c = -1: the all-zero start of pass 2)
     int c, slot;
     if (PASS == 1) {
-      const int rel = ((i - 1) - (half - 1)) / G::R;
-      c = (half - 1) + rel * G::R;
+      const int rel = ((i - 1) - (half - 1)) / W::R;
+      c = (half - 1) + rel * W::R;
       slot = rel;
     } else {
-      c = (i / G::R) * G::R - 1;
-      slot = (c + 1) / G::R - 1;
+      c = (i / W::R) * W::R - 1;
+      slot = (c + 1) / W::R - 1;
     }
     const int D = i - 1 - c;  // levels recomputed above the checkpoint
     const int Lv = D + 1;     // level of the checkpoint (step i - Lv == c)
@@ -460,13 +473,15 @@ __device__ int ck_walk(const uint8_t* __restrict__ pck, int b, int cb, const uin
     // packed one after another (level m starts at Q + Q^2 + ... + Q^(m-1))
     auto off = [](int m) { return ((1 << (m * K)) - (1 << K)) / ((1 << K) - 1); };
     const int nL = 1 << (Lv * K);
-    const uint32_t* ckw =
-        c >= 0 ? reinterpret_cast<const uint32_t*>(pck + (size_t)slot * G::CKB) : nullptr;
+    const uint8_t* ckb = c >= 0 ? pck + (size_t)slot * W::CKB : nullptr;
     for (int j = lane; j < nL; j += 32) {
       uint16_t v = 0;
-      if (ckw) {
+      if (ckb) {
         const int x = (j << (G::Kr - Lv * K)) | (e >> (Lv * K));
-        v = (uint16_t)((ckw[x] >> (16 * b)) & 0xFFFFu);
+        if (SINGLE)
+          v = reinterpret_cast<const uint16_t*>(ckb)[x];
+        else
+          v = (uint16_t)((reinterpret_cast<const uint32_t*>(ckb)[x] >> (16 * b)) & 0xFFFFu);
       }
       vals[off(Lv) + j] = v;
     }
@@ -621,6 +636,305 @@ int pair_encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t*
       pair_tb2_kernel<K><<<tb_grid, 32 * kTbWarps, 0, stream>>>(
           cin, ck, ck_pair, m, L, cb, end_state, out_w + start * L, out_idx + start * L,
           out_packed ? out_packed + start * 16 * K : nullptr);
+    }
+    EXL3_LAUNCHED();
+  }
+  return EXL3_OK;
+}
+
+
+// ---------------------------------------------------------------------------
+// K = 1: one tile per CTA. A tile pair's two 32,768-word cost vectors would
+// take 256 KiB, above a CTA's shared memory; one tile's fp16 vectors take
+// 128 KiB. The fp16 lanes hold the two edges 2g and 2g+1 that share both
+// predecessors g and g + 2^14, so a step is the pair kernel's step with
+// edges instead of tiles in the lanes: per edge pair two sub + two fma on
+// the FMA pipe and one min on the ALU pipe, min-only, cost checkpoints every
+// kSingleR steps by bulk copy, the same recomputing traceback.
+// ---------------------------------------------------------------------------
+struct SGeo {
+  static constexpr int S = 32768;               // edges
+  static constexpr int NP = S / 2 / kPairNT;    // 32 edge pairs per thread
+  static constexpr int CP = 8;                  // pairs per chunk
+  static constexpr int NCH = NP / CP;           // 4 chunks per step
+  static constexpr int R = kSingleR;
+  static constexpr int CKB = S * 2;             // fp16 per edge
+};
+
+__host__ __device__ constexpr int single_slots_pass1(int L) { return (L - L / 2 - 1) / kSingleR + 1; }
+__host__ __device__ constexpr int single_slots_pass2(int L) { return (L - 1) / kSingleR; }
+
+size_t single_ck_bytes(int L) {
+  const int s1 = single_slots_pass1(L), s2 = single_slots_pass2(L);
+  const size_t b = (size_t)(s1 > s2 ? s1 : s2) * SGeo::CKB;
+  return (b + 255) / 256 * 256;
+}
+
+size_t single_tile_ws_bytes(int L) { return single_ck_bytes(L) + 8; }
+
+// edge pair g = (c * 512 + t) * CP + j: cbv[(c * CP + j) * 2 + k] holds the
+// codebook values of states (k << 15) | 2g and (k << 15) | (2g + 1)
+__device__ __forceinline__ void single_init_codebook(uint32_t (&cbv)[64], int cb, int t) {
+#pragma unroll
+  for (int c = 0; c < SGeo::NCH; ++c)
+#pragma unroll
+    for (int j = 0; j < SGeo::CP; ++j) {
+      const uint32_t g = (uint32_t)((c * kPairNT + t) * SGeo::CP + j);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const uint32_t s0 = ((uint32_t)k << 15) | (2 * g);
+        cbv[(c * SGeo::CP + j) * 2 + k] =
+            (uint32_t)cb_state_bits(cb, s0) | ((uint32_t)cb_state_bits(cb, s0 + 1) << 16);
+      }
+    }
+}
+
+// cin: fp16 per edge; cout: {cost(2g), cost(2g+1)} words per edge pair (the
+// same bytes read as fp16 per edge); w2 = {w, w}
+template <bool FIRST, bool EXACT>
+__device__ __forceinline__ void single_step(const uint32_t (&cbv)[64], uint32_t w2,
+                                            const uint16_t* __restrict__ cin,
+                                            uint32_t* __restrict__ cout, int t, int pre) {
+#pragma unroll
+  for (int c = 0; c < SGeo::NCH; ++c) {
+    const int g0 = (c * kPairNT + t) * SGeo::CP;
+    uint32_t p0[4], p1[4];
+    if constexpr (!FIRST) {
+      const uint4 a = *reinterpret_cast<const uint4*>(cin + g0);
+      const uint4 b = *reinterpret_cast<const uint4*>(cin + (1 << 14) + g0);
+      p0[0] = a.x; p0[1] = a.y; p0[2] = a.z; p0[3] = a.w;
+      p1[0] = b.x; p1[1] = b.y; p1[2] = b.z; p1[3] = b.w;
+    }
+    uint32_t best[SGeo::CP];
+#pragma unroll
+    for (int j = 0; j < SGeo::CP; ++j) {
+      uint32_t c0, c1;
+      {
+        const uint32_t d0 = h2_sub(cbv[(c * SGeo::CP + j) * 2], w2);
+        const uint32_t d1 = h2_sub(cbv[(c * SGeo::CP + j) * 2 + 1], w2);
+        uint32_t q0 = 0u, q1 = 0u;
+        if constexpr (!FIRST) {
+          q0 = (j & 1) ? h2_hi2(p0[j >> 1]) : h2_lo2(p0[j >> 1]);
+          q1 = (j & 1) ? h2_hi2(p1[j >> 1]) : h2_lo2(p1[j >> 1]);
+        }
+        c0 = h2_fma(d0, d0, q0);
+        c1 = h2_fma(d1, d1, q1);
+      }
+      if constexpr (FIRST) {
+        if (pre >= 0) {
+          const int g = g0 + j;
+          c0 = (g == pre) ? c0 : kHInf2;                 // pred (0 << 14) | g
+          c1 = (((1 << 14) | g) == pre) ? c1 : kHInf2;   // pred (1 << 14) | g
+        }
+      }
+      best[j] = EXACT ? bsel(h2_lt_mask(c1, c0), c1, c0) : h2_min(c0, c1);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(cout + g0);
+    dst[0] = make_uint4(best[0], best[1], best[2], best[3]);
+    dst[1] = make_uint4(best[4], best[5], best[6], best[7]);
+  }
+}
+
+template <bool EXACT>
+__device__ __forceinline__ void single_pass1(const uint32_t (&cbv)[64], const uint32_t* wt,
+                                             uint16_t* c0, uint16_t* c1, uint8_t* ckp, int L,
+                                             int t) {
+  const int half = L / 2;
+  single_step<true, EXACT>(cbv, wt[half], nullptr, reinterpret_cast<uint32_t*>(c0), t, -1);
+  __syncthreads();
+  for (int i = 1; i < L; ++i) {
+    const uint16_t* cin = (i & 1) ? c0 : c1;
+    uint16_t* cout = (i & 1) ? c1 : c0;
+    single_step<false, EXACT>(cbv, wt[i < half ? i + half : i - half], cin,
+                              reinterpret_cast<uint32_t*>(cout), t, -1);
+    const int rel = i - (half - 1);
+    const bool ckpt = rel >= 0 && rel % SGeo::R == 0 && i <= L - 2;
+    if (ckpt) ck_fence();
+    if (t == 0) ck_wait_read();
+    __syncthreads();
+    if (ckpt && t == 0)
+      ck_issue(ckp + (size_t)(rel / SGeo::R) * SGeo::CKB, reinterpret_cast<uint32_t*>(cout),
+               SGeo::CKB);
+  }
+  if (t == 0) ck_wait_read();
+}
+
+template <bool EXACT>
+__device__ __forceinline__ void single_pass2(const uint32_t (&cbv)[64], const uint32_t* wt,
+                                             uint16_t* c0, uint16_t* c1, uint8_t* ckp, int L,
+                                             int t, int pre) {
+  single_step<true, EXACT>(cbv, wt[0], nullptr, reinterpret_cast<uint32_t*>(c0), t, pre);
+  __syncthreads();
+  for (int i = 1; i < L; ++i) {
+    const uint16_t* cin = (i & 1) ? c0 : c1;
+    uint16_t* cout = (i & 1) ? c1 : c0;
+    single_step<false, EXACT>(cbv, wt[i], cin, reinterpret_cast<uint32_t*>(cout), t, -1);
+    const bool ckpt = (i + 1) % SGeo::R == 0 && i <= L - 2;
+    if (ckpt) ck_fence();
+    if (t == 0) ck_wait_read();
+    __syncthreads();
+    if (ckpt && t == 0)
+      ck_issue(ckp + (size_t)((i + 1) / SGeo::R - 1) * SGeo::CKB,
+               reinterpret_cast<uint32_t*>(cout), SGeo::CKB);
+  }
+  if (t == 0) ck_wait_read();
+}
+
+// minimum cost, lowest edge on ties, non-finite skipped, none finite -> 0
+__device__ __forceinline__ int single_argmin(const uint16_t* costs, uint32_t* red, int t) {
+  uint32_t key = 0xFFFFFFFFu;
+  for (int e = t; e < SGeo::S; e += kPairNT) {
+    const uint32_t b = costs[e];
+    if ((b & 0x7C00u) != 0x7C00u) key = min(key, (b << 16) | (uint32_t)e);
+  }
+  key = __reduce_min_sync(0xFFFFFFFFu, key);
+  if ((t & 31) == 0) red[t >> 5] = key;
+  __syncthreads();
+  if (t < 32) {
+    uint32_t v = (t < kPairNT / 32) ? red[t] : 0xFFFFFFFFu;
+    v = __reduce_min_sync(0xFFFFFFFFu, v);
+    if (t == 0) red[0] = v;
+  }
+  __syncthreads();
+  const uint32_t v = red[0];
+  __syncthreads();
+  return v == 0xFFFFFFFFu ? 0 : (int)(v & 0xFFFFu);
+}
+
+constexpr size_t kSingleSmem = 2ull * SGeo::S * sizeof(uint16_t) + 256 * sizeof(uint32_t);
+
+template <int PASS>
+__global__ void __launch_bounds__(kPairNT, 1)
+acs_single_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* __restrict__ ck,
+                  size_t ck_tile_bytes, int32_t* __restrict__ best_edge,
+                  const int32_t* __restrict__ end_state, float* __restrict__ path_cost) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint16_t* c0 = reinterpret_cast<uint16_t*>(smem);
+  uint16_t* c1 = c0 + SGeo::S;
+  uint32_t* wt = reinterpret_cast<uint32_t*>(smem + 2ull * SGeo::S * sizeof(uint16_t));
+  __shared__ uint32_t red[kPairNT / 32];
+  const int t = threadIdx.x;
+  uint32_t cbv[64];
+  single_init_codebook(cbv, cb, t);
+  for (int tile = blockIdx.x; tile < n; tile += gridDim.x) {
+    int nan = 0;
+    for (int i = t; i < L; i += kPairNT) {
+      const __half h = __float2half_rn(in[(size_t)tile * L + i]);
+      const uint32_t b = __half_as_ushort(h);
+      nan |= __hisnan(h) ? 1 : 0;
+      wt[i] = b | (b << 16);
+    }
+    nan = __syncthreads_or(nan);
+    uint8_t* tck = ck + (size_t)tile * ck_tile_bytes;
+    const uint16_t* fin = ((L - 1) & 1) ? c1 : c0;
+    if constexpr (PASS == 1) {
+      if (nan) single_pass1<true>(cbv, wt, c0, c1, tck, L, t);
+      else     single_pass1<false>(cbv, wt, c0, c1, tck, L, t);
+      const int be = single_argmin(fin, red, t);
+      if (t == 0) best_edge[tile] = be;
+    } else {
+      const int pre = end_state[tile];
+      if (nan) single_pass2<true>(cbv, wt, c0, c1, tck, L, t, pre);
+      else     single_pass2<false>(cbv, wt, c0, c1, tck, L, t, pre);
+      if (t == 0 && path_cost) path_cost[tile] = half_bits_to_float(fin[pre]);
+    }
+    __syncthreads();
+  }
+  if (t == 0) ck_wait_all();
+}
+
+__global__ void __launch_bounds__(32 * kTbWarps)
+single_tb1_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck,
+                  size_t ck_tile_bytes, int n, int L, int cb,
+                  const int32_t* __restrict__ best_edge, int32_t* __restrict__ end_state) {
+  __shared__ uint16_t vals[kTbWarps][kTbVals];
+  __shared__ uint16_t w[kTbWarps][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x * kTbWarps + warp;
+  if (tile >= n) return;
+  tb_load_weights<1>(in, tile, L, w[warp], lane);
+  const int e = ck_walk<1, 1, true>(ck + (size_t)tile * ck_tile_bytes, 0, cb, w[warp], L,
+                                    best_edge[tile], -1, vals[warp], nullptr, lane);
+  if (lane == 0) end_state[tile] = e;
+}
+
+__global__ void __launch_bounds__(32 * kTbWarps)
+single_tb2_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck,
+                  size_t ck_tile_bytes, int n, int L, int cb,
+                  const int32_t* __restrict__ end_state, float* __restrict__ out_w,
+                  int16_t* __restrict__ out_idx, int16_t* __restrict__ out_packed) {
+  __shared__ uint16_t vals[kTbWarps][kTbVals];
+  __shared__ uint16_t w[kTbWarps][256];
+  __shared__ uint16_t st[kTbWarps][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x * kTbWarps + warp;
+  if (tile >= n) return;
+  tb_load_weights<1>(in, tile, L, w[warp], lane);
+  const int pre = end_state[tile];
+  ck_walk<1, 2, true>(ck + (size_t)tile * ck_tile_bytes, 0, cb, w[warp], L, pre, pre,
+                      vals[warp], st[warp], lane);
+  __syncwarp();
+  for (int i = lane; i < L; i += 32) {
+    const uint16_t s = st[warp][i];
+    out_idx[(size_t)tile * L + i] = (int16_t)s;
+    out_w[(size_t)tile * L + i] = half_bits_to_float(cb_state_bits(cb, s));
+  }
+  if (out_packed && L == 256 && lane < 16)
+    pack_span(st[warp], 1, lane, out_packed + (size_t)tile * 16);
+}
+
+int single_encode(const float* in, float* out_w, int16_t* out_idx, int16_t* out_packed,
+                  float* out_cost, int64_t n, int cb, int L, uint8_t* ws, size_t ws_bytes,
+                  cudaStream_t stream) {
+  static int attr_done = 0;  // one bit per device
+  int dev = 0;
+  EXL3_CUDA(cudaGetDevice(&dev));
+  if (!(dev < 32 && (attr_done & (1 << dev)))) {
+    EXL3_CUDA(cudaFuncSetAttribute(acs_single_kernel<1>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSingleSmem));
+    EXL3_CUDA(cudaFuncSetAttribute(acs_single_kernel<2>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSingleSmem));
+    if (dev < 32) attr_done |= (1 << dev);
+  }
+  const size_t per_tile = single_tile_ws_bytes(L);
+  const size_t ck_tile = single_ck_bytes(L);
+  int64_t cap = (int64_t)(ws_bytes / per_tile);
+  EXL3_REQUIRE(cap >= 1, "workspace of %zu bytes is smaller than one tile (%zu bytes)", ws_bytes,
+               per_tile);
+  if (cap > n) cap = n;
+  if (cap > (1 << 30)) cap = 1 << 30;
+  uint8_t* ck = ws;
+  int32_t* best_edge = reinterpret_cast<int32_t*>(ws + (size_t)cap * ck_tile);
+  int32_t* end_state = best_edge + cap;
+  const int sms = sm_count();
+  for (int64_t start = 0; start < n; start += cap) {
+    const int m = (int)((n - start) < cap ? (n - start) : cap);
+    const int grid = m < sms ? m : sms;
+    const int tb_grid = (m + kTbWarps - 1) / kTbWarps;
+    const float* cin = in + start * L;
+    {
+      LaunchTimer lt(stream, 0);
+      acs_single_kernel<1><<<grid, kPairNT, kSingleSmem, stream>>>(cin, m, L, cb, ck, ck_tile,
+                                                                   best_edge, nullptr, nullptr);
+    }
+    EXL3_LAUNCHED();
+    {
+      LaunchTimer lt(stream, 1);
+      single_tb1_kernel<<<tb_grid, 32 * kTbWarps, 0, stream>>>(cin, ck, ck_tile, m, L, cb,
+                                                               best_edge, end_state);
+    }
+    EXL3_LAUNCHED();
+    {
+      LaunchTimer lt(stream, 0);
+      acs_single_kernel<2><<<grid, kPairNT, kSingleSmem, stream>>>(
+          cin, m, L, cb, ck, ck_tile, nullptr, end_state, out_cost ? out_cost + start : nullptr);
+    }
+    EXL3_LAUNCHED();
+    {
+      LaunchTimer lt(stream, 1);
+      single_tb2_kernel<<<tb_grid, 32 * kTbWarps, 0, stream>>>(
+          cin, ck, ck_tile, m, L, cb, end_state, out_w + start * L, out_idx + start * L,
+          out_packed ? out_packed + start * 16 : nullptr);
     }
     EXL3_LAUNCHED();
   }

@@ -12,22 +12,20 @@
 //     traceback to ring index 0 = end_state; (roll = 0, step 0 masked to
 //     pred == end_state) -> traceback emitting states.
 //
-// B200 design (not a port):
-//   * one tile per CTA iteration, 512 threads, persistent CTAs (one per SM);
-//   * all 65536 codebook values of the tile's trellis live in registers
-//     (64 packed half2 per thread) for the whole kernel, so the inner loop
-//     never decodes the codebook;
-//   * each thread owns adjacent edge pairs (one half2 lane each): both lanes
-//     share every predecessor, so one broadcast cost feeds a packed
-//     sub / fma / compare / select sequence;
-//   * the fp16 cost vector ping-pongs in shared memory (one barrier per step);
-//   * backpointers are the chosen branch k only (K bits, not the reference's
-//     int16 predecessor), written with coalesced 32-bit stores; pass 1 records
-//     them only for the half of the ring the end_state traceback visits;
-//   * steps whose backpointers are never read use a packed min (3 ops per
-//     candidate pair) instead of compare-and-select;
-//   * a tile containing NaN switches to the exact compare-and-select form on
-//     every step, which reproduces the reference's NaN stickiness.
+// This file holds the reference-layout split passes, which keep the
+// reference's scratch contract (temp_costs (B, 2, S) fp16, temp_edges
+// (B, L, S) int16 predecessors, every step recorded) for callers of
+// quantize_tiles_forward_pass / _backward_pass; the codebook and container
+// kernels; and the C-ABI entry points. exl3_quantize_tiles dispatches to the
+// checkpoint encoders in acs_pair.cu (tile pairs for K >= 2, single tiles
+// for K = 1).
+//
+// Reference-layout ACS: one tile per CTA iteration, 512 threads, persistent
+// CTAs; the tile's 65536 codebook values live in registers (64 packed half2
+// per thread); each thread owns adjacent edge pairs (one half2 lane each,
+// both lanes share every predecessor); the fp16 cost vector ping-pongs in
+// shared memory; compare-and-select on every branch (NaN-faithful), writing
+// the winning predecessor of every edge and step.
 #include "common.cuh"
 #include "encoder_shared.cuh"
 
@@ -53,19 +51,10 @@ struct Geo {
   static constexpr int CP = SPLIT ? 1 : (K == 1 ? 4 : (NP < 8 ? NP : 8));  // pairs per chunk
   static constexpr int NCH = NP / CP;                       // chunks per step
   static constexpr int CG = SPLIT ? 1 : (((2 * CP) >> K) > 0 ? ((2 * CP) >> K) : 1);
-  static constexpr int CPW = (K == 1) ? 16 : (K == 2) ? 8 : (K <= 4) ? 4 : 2;
-  static constexpr int NW = SPLIT ? 1 : (NP + CPW - 1) / CPW;  // bp words/thread
-  // backpointer bytes per trellis step of one tile
-  static constexpr int BPS = SPLIT ? (S / 2) * 2 : NW * kNT * 4;
   static constexpr int NCB = NP * QT;              // codebook half2 registers
   static_assert(NCB == 64, "codebook register budget");
 };
 
-__host__ __device__ constexpr int bp_step_bytes(int K) {
-  return K == 1 ? Geo<1>::BPS : K == 2 ? Geo<2>::BPS : K == 3 ? Geo<3>::BPS
-       : K == 4 ? Geo<4>::BPS : K == 5 ? Geo<5>::BPS : K == 6 ? Geo<6>::BPS
-       : K == 7 ? Geo<7>::BPS : Geo<8>::BPS;
-}
 
 // Codebook values of this thread's candidates, packed per edge pair.
 template <int K>
@@ -96,7 +85,7 @@ __device__ __forceinline__ void init_codebook(uint32_t (&cbv)[64], int cb, int t
 }
 
 // Backpointer storage modes.
-enum BpMode { BP_NONE = 0, BP_COMPACT = 1, BP_PRED16 = 2 };
+enum BpMode { BP_NONE = 0, BP_PRED16 = 2 };
 
 // One ACS step for K <= 6: thread owns NP adjacent edge pairs and all Q
 // branches of each.
@@ -110,10 +99,6 @@ __device__ __forceinline__ void step_pairs(const uint32_t (&cbv)[64], uint32_t w
                                            void* __restrict__ bp_step, int t,
                                            int pre_state) {
   using G = Geo<K>;
-  uint32_t bpw[G::NW];
-#pragma unroll
-  for (int w = 0; w < G::NW; ++w) bpw[w] = 0;
-
 #pragma unroll
   for (int c = 0; c < G::NCH; ++c) {
     const int e_base = t * G::EPT + 2 * c * G::CP;
@@ -169,9 +154,7 @@ __device__ __forceinline__ void step_pairs(const uint32_t (&cbv)[64], uint32_t w
         }
       }
       res[p] = best;
-      if constexpr (BPM == BP_COMPACT) {
-        bpw[pp / G::CPW] |= idx << (K * (pp % G::CPW));
-      } else if constexpr (BPM == BP_PRED16) {
+      if constexpr (BPM == BP_PRED16) {
         const uint32_t g = (uint32_t)((e_base + 2 * p) >> K);
         reinterpret_cast<uint32_t*>(bp_step)[(e_base >> 1) + p] =
             (idx << G::GB) | (g | (g << 16));
@@ -189,11 +172,6 @@ __device__ __forceinline__ void step_pairs(const uint32_t (&cbv)[64], uint32_t w
     } else {
       dst[0] = res[0];
     }
-  }
-  if constexpr (BPM == BP_COMPACT) {
-    uint32_t* bw = reinterpret_cast<uint32_t*>(bp_step);
-#pragma unroll
-    for (int w = 0; w < G::NW; ++w) bw[w * kNT + t] = bpw[w];
   }
 }
 
@@ -262,9 +240,7 @@ __device__ __forceinline__ void step_split(const uint32_t (&cbv)[64], uint32_t w
   }
   if (r == 0) {
     reinterpret_cast<uint32_t*>(cout)[P] = best;
-    if constexpr (BPM == BP_COMPACT) {
-      reinterpret_cast<uint16_t*>(bp_step)[P] = (uint16_t)__byte_perm(idx, 0, 0x0020);
-    } else if constexpr (BPM == BP_PRED16) {
+    if constexpr (BPM == BP_PRED16) {
       reinterpret_cast<uint32_t*>(bp_step)[P] =
           (idx << G::GB) | ((uint32_t)g | ((uint32_t)g << 16));
     }
@@ -301,186 +277,6 @@ __device__ __forceinline__ int load_tile(const float* __restrict__ src, int L,
     wt[i] = b | (b << 16);
   }
   return __syncthreads_or(nan);
-}
-
-// CTA-wide argmin over final costs: minimum cost, lowest edge on ties;
-// non-finite costs are skipped and an all-non-finite vector yields edge 0
-// (reference_encoder.py:206-214, quantize_kernels.sycl:161-234).
-template <int K>
-__device__ __forceinline__ int block_argmin(const uint16_t* costs, uint32_t* red, int t) {
-  using G = Geo<K>;
-  uint32_t key = 0xFFFFFFFFu;
-  for (int e = t; e < G::S; e += kNT) {
-    const uint32_t b = costs[e];
-    if ((b & 0x7C00u) != 0x7C00u) key = min(key, (b << 16) | (uint32_t)e);
-  }
-  key = __reduce_min_sync(0xFFFFFFFFu, key);
-  if ((t & 31) == 0) red[t >> 5] = key;
-  __syncthreads();
-  if (t < 32) {
-    uint32_t v = (t < kNT / 32) ? red[t] : 0xFFFFFFFFu;
-    v = __reduce_min_sync(0xFFFFFFFFu, v);
-    if (t == 0) red[0] = v;
-  }
-  __syncthreads();
-  const uint32_t v = red[0];
-  __syncthreads();
-  return v == 0xFFFFFFFFu ? 0 : (int)(v & 0xFFFFu);
-}
-
-// ---------------------------------------------------------------------------
-// Pass 1: roll = L/2, unconstrained. Records backpointers for ring indices
-// [0, L/2) (the steps i >= L/2 the end_state traceback walks) and the
-// argmin edge of the final costs.
-// ---------------------------------------------------------------------------
-template <int K, bool EXACT>
-__device__ __forceinline__ void run_pass1(const uint32_t (&cbv)[64], const uint32_t* wt,
-                                          uint16_t* cbuf0, uint16_t* cbuf1, uint8_t* bp,
-                                          int L, int t) {
-  using G = Geo<K>;
-  const int half = L / 2;
-  acs_step<K, true, BP_NONE, EXACT>(cbv, wt[half], nullptr, cbuf0, nullptr, t, -1);
-  __syncthreads();
-  for (int i = 1; i < half; ++i) {
-    const uint16_t* cin = (i & 1) ? cbuf0 : cbuf1;
-    uint16_t* cout = (i & 1) ? cbuf1 : cbuf0;
-    acs_step<K, false, BP_NONE, EXACT>(cbv, wt[i + half], cin, cout, nullptr, t, -1);
-    __syncthreads();
-  }
-  for (int i = half; i < L; ++i) {
-    const int ri = i - half;
-    const uint16_t* cin = (i & 1) ? cbuf0 : cbuf1;
-    uint16_t* cout = (i & 1) ? cbuf1 : cbuf0;
-    acs_step<K, false, BP_COMPACT, EXACT>(cbv, wt[ri], cin, cout,
-                                           bp + (size_t)ri * G::BPS, t, -1);
-    __syncthreads();
-  }
-}
-
-template <int K, bool EXACT>
-__device__ __forceinline__ void run_pass2(const uint32_t (&cbv)[64], const uint32_t* wt,
-                                          uint16_t* cbuf0, uint16_t* cbuf1, uint8_t* bp,
-                                          int L, int t, int pre) {
-  using G = Geo<K>;
-  acs_step<K, true, BP_COMPACT, EXACT>(cbv, wt[0], nullptr, cbuf0, bp, t, pre);
-  __syncthreads();
-  for (int i = 1; i < L; ++i) {
-    const uint16_t* cin = (i & 1) ? cbuf0 : cbuf1;
-    uint16_t* cout = (i & 1) ? cbuf1 : cbuf0;
-    acs_step<K, false, BP_COMPACT, EXACT>(cbv, wt[i], cin, cout,
-                                           bp + (size_t)i * G::BPS, t, -1);
-    __syncthreads();
-  }
-}
-
-template <int K, int PASS>
-__global__ void __launch_bounds__(kNT, 1)
-acs_kernel(const float* __restrict__ in, int n, int L, int cb,
-           uint8_t* __restrict__ bp, size_t bp_tile_bytes,
-           int32_t* __restrict__ best_edge,        // PASS 1 out
-           const int32_t* __restrict__ end_state,  // PASS 2 in
-           float* __restrict__ path_cost,          // PASS 2 out (nullable)
-           uint16_t* __restrict__ final_costs)     // (n, 2, S) fp16 (nullable)
-{
-  using G = Geo<K>;
-  extern __shared__ __align__(16) uint8_t smem[];
-  uint16_t* cbuf0 = reinterpret_cast<uint16_t*>(smem);
-  uint16_t* cbuf1 = cbuf0 + G::S;
-  uint32_t* wt = reinterpret_cast<uint32_t*>(smem + Smem<K>::costs);
-  __shared__ uint32_t red[kNT / 32];
-  const int t = threadIdx.x;
-
-  uint32_t cbv[64];
-  init_codebook<K>(cbv, cb, t);
-
-  for (int tile = blockIdx.x; tile < n; tile += gridDim.x) {
-    const int nan = load_tile(in + (size_t)tile * L, L, wt, t);
-    uint8_t* tbp = bp + (size_t)tile * bp_tile_bytes;
-    const uint16_t* final_buf = ((L - 1) & 1) ? cbuf1 : cbuf0;
-    if constexpr (PASS == 1) {
-      if (nan) run_pass1<K, true>(cbv, wt, cbuf0, cbuf1, tbp, L, t);
-      else     run_pass1<K, false>(cbv, wt, cbuf0, cbuf1, tbp, L, t);
-      const int be = block_argmin<K>(final_buf, red, t);
-      if (t == 0) best_edge[tile] = be;
-    } else {
-      const int pre = end_state[tile];
-      if (nan) run_pass2<K, true>(cbv, wt, cbuf0, cbuf1, tbp, L, t, pre);
-      else     run_pass2<K, false>(cbv, wt, cbuf0, cbuf1, tbp, L, t, pre);
-      if (t == 0 && path_cost) path_cost[tile] = half_bits_to_float(final_buf[pre]);
-    }
-    if (final_costs) {
-      uint16_t* dst = final_costs + ((size_t)tile * 2 + (PASS - 1)) * G::S;
-      for (int e = t; e < G::S; e += kNT) dst[e] = final_buf[e];
-    }
-    __syncthreads();
-  }
-}
-
-// ---------------------------------------------------------------------------
-// Traceback over compact backpointers.
-// ---------------------------------------------------------------------------
-template <int K>
-__device__ __forceinline__ int bp_branch(const uint8_t* step_base, int e) {
-  using G = Geo<K>;
-  if constexpr (!G::SPLIT) {
-    const int th = e / G::EPT, q = e % G::EPT;
-    const int p = q >> 1, b = q & 1;
-    const int w = p / G::CPW, pc = p % G::CPW;
-    const uint32_t word = reinterpret_cast<const uint32_t*>(step_base)[w * kNT + th];
-    return (int)((word >> (16 * b + K * pc)) & (G::Q - 1));
-  } else {
-    const uint32_t v = reinterpret_cast<const uint16_t*>(step_base)[e >> 1];
-    return (int)((v >> (8 * (e & 1))) & (G::Q - 1));
-  }
-}
-
-// Pass-1 traceback: from the argmin edge back through ring indices
-// L/2-1 .. 0; the edge reached is end_state (reference_encoder.py:216-251).
-template <int K>
-__global__ void tb1_kernel(const uint8_t* __restrict__ bp, size_t bp_tile_bytes, int n,
-                           int L, const int32_t* __restrict__ best_edge,
-                           int32_t* __restrict__ end_state) {
-  using G = Geo<K>;
-  const int tile = blockIdx.x * blockDim.x + threadIdx.x;
-  if (tile >= n) return;
-  const uint8_t* tbp = bp + (size_t)tile * bp_tile_bytes;
-  int e = best_edge[tile];
-  for (int ri = L / 2 - 1; ri >= 0; --ri) {
-    const int k = bp_branch<K>(tbp + (size_t)ri * G::BPS, e);
-    e = (k << G::GB) | (e >> K);
-  }
-  end_state[tile] = e;
-}
-
-// Pass-2 traceback: one warp per tile. Lane 0 walks the chain; the warp then
-// writes states, reconstruction and the packed container.
-template <int K>
-__global__ void tb2_kernel(const uint8_t* __restrict__ bp, size_t bp_tile_bytes, int n,
-                           int L, int cb, const int32_t* __restrict__ end_state,
-                           float* __restrict__ out_w, int16_t* __restrict__ out_idx,
-                           int16_t* __restrict__ out_packed) {
-  using G = Geo<K>;
-  __shared__ uint16_t st[kTbWarps][256];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x * kTbWarps + warp;
-  if (tile >= n) return;
-  const uint8_t* tbp = bp + (size_t)tile * bp_tile_bytes;
-  if (lane == 0) {
-    int e = end_state[tile];
-    for (int i = L - 1; i >= 0; --i) {
-      const int k = bp_branch<K>(tbp + (size_t)i * G::BPS, e);
-      st[warp][i] = (uint16_t)((k << G::Kr) | e);
-      e = (k << G::GB) | (e >> K);
-    }
-  }
-  __syncwarp();
-  for (int i = lane; i < L; i += 32) {
-    const uint16_t s = st[warp][i];
-    out_idx[(size_t)tile * L + i] = (int16_t)s;
-    out_w[(size_t)tile * L + i] = half_bits_to_float(cb_state_bits(cb, s));
-  }
-  if (out_packed && L == 256 && lane < 16)
-    pack_span(st[warp], K, lane, out_packed + (size_t)tile * 16 * K);
 }
 
 // ---------------------------------------------------------------------------
@@ -582,12 +378,8 @@ __global__ void pack_kernel(const int16_t* __restrict__ states, int16_t* __restr
 // ---------------------------------------------------------------------------
 namespace {
 
-constexpr size_t kAlign = 256;
-inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
-
-inline size_t tile_bp_bytes(int K, int L) { return align_up((size_t)L * bp_step_bytes(K)); }
 inline size_t tile_ws_bytes(int K, int L) {
-  return K >= 2 ? pair_tile_ws_bytes(K, L) : tile_bp_bytes(K, L) + 8;
+  return K >= 2 ? pair_tile_ws_bytes(K, L) : single_tile_ws_bytes(L);
 }
 
 int validate(int K, int cb, int L) {
@@ -605,60 +397,8 @@ int set_smem_attrs() {
   EXL3_CUDA(cudaGetDevice(&dev));
   if (dev < 32 && (done_mask & (1 << dev))) return EXL3_OK;
   const int bytes = (int)Smem<K>::bytes;
-  EXL3_CUDA(cudaFuncSetAttribute(acs_kernel<K, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-  EXL3_CUDA(cudaFuncSetAttribute(acs_kernel<K, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
   EXL3_CUDA(cudaFuncSetAttribute(acs_ref_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
   if (dev < 32) done_mask |= (1 << dev);
-  return EXL3_OK;
-}
-
-template <int K>
-int encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t* out_packed,
-                  float* out_cost, int64_t n, int cb, int L, uint8_t* ws, size_t ws_bytes,
-                  cudaStream_t stream) {
-  int rc = set_smem_attrs<K>();
-  if (rc) return rc;
-  const size_t per_tile = tile_ws_bytes(K, L);
-  int64_t cap = (int64_t)(ws_bytes / per_tile);
-  EXL3_REQUIRE(cap >= 1, "workspace of %zu bytes is smaller than one tile (%zu bytes)",
-               ws_bytes, per_tile);
-  if (cap > n) cap = n;
-  if (cap > (1 << 30)) cap = 1 << 30;
-  const size_t bp_tile = tile_bp_bytes(K, L);
-  uint8_t* bp = ws;
-  int32_t* best_edge = reinterpret_cast<int32_t*>(ws + (size_t)cap * bp_tile);
-  int32_t* end_state = best_edge + cap;
-  const int sms = sm_count();
-  for (int64_t start = 0; start < n; start += cap) {
-    const int m = (int)((n - start) < cap ? (n - start) : cap);
-    const float* cin = in + start * L;
-    const int grid = m < sms ? m : sms;
-    {
-      LaunchTimer lt(stream, 0);
-      acs_kernel<K, 1><<<grid, kNT, Smem<K>::bytes, stream>>>(
-          cin, m, L, cb, bp, bp_tile, best_edge, nullptr, nullptr, nullptr);
-    }
-    EXL3_LAUNCHED();
-    {
-      LaunchTimer lt(stream, 1);
-      tb1_kernel<K><<<(m + 127) / 128, 128, 0, stream>>>(bp, bp_tile, m, L, best_edge, end_state);
-    }
-    EXL3_LAUNCHED();
-    {
-      LaunchTimer lt(stream, 0);
-      acs_kernel<K, 2><<<grid, kNT, Smem<K>::bytes, stream>>>(
-          cin, m, L, cb, bp, bp_tile, nullptr, end_state, out_cost ? out_cost + start : nullptr,
-          nullptr);
-    }
-    EXL3_LAUNCHED();
-    {
-      LaunchTimer lt(stream, 1);
-      tb2_kernel<K><<<(m + kTbWarps - 1) / kTbWarps, 32 * kTbWarps, 0, stream>>>(
-          bp, bp_tile, m, L, cb, end_state, out_w + start * L, out_idx + start * L,
-          out_packed ? out_packed + start * 16 * K : nullptr);
-    }
-    EXL3_LAUNCHED();
-  }
   return EXL3_OK;
 }
 
@@ -724,8 +464,8 @@ extern "C" int exl3_quantize_tiles(const float* in, float* out_w, int16_t* out_i
   if (K >= 2)
     return pair_encode(K, in, out_w, out_idx, out_packed, out_cost, n, cb, L,
                        static_cast<uint8_t*>(ws), ws_bytes, (cudaStream_t)stream);
-  return encode_chunks<1>(in, out_w, out_idx, out_packed, out_cost, n, cb, L,
-                          static_cast<uint8_t*>(ws), ws_bytes, (cudaStream_t)stream);
+  return single_encode(in, out_w, out_idx, out_packed, out_cost, n, cb, L,
+                       static_cast<uint8_t*>(ws), ws_bytes, (cudaStream_t)stream);
 }
 
 extern "C" int exl3_forward_pass_ref_layout(const float* in, uint16_t* temp_costs,

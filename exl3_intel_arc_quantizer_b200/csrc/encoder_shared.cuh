@@ -68,6 +68,11 @@ struct LaunchTimer {
 // tile-pair encoder (acs_pair.cu)
 size_t pair_ck_bytes(int K, int L);       // cost checkpoints of one tile pair
 size_t pair_tile_ws_bytes(int K, int L);  // workspace per tile (half a pair + scalars)
+// single-tile K = 1 encoder (acs_pair.cu)
+size_t single_tile_ws_bytes(int L);
+int single_encode(const float* in, float* out_w, int16_t* out_idx, int16_t* out_packed,
+                  float* out_cost, int64_t n, int cb, int L, uint8_t* ws, size_t ws_bytes,
+                  cudaStream_t stream);
 int pair_encode(int K, const float* in, float* out_w, int16_t* out_idx, int16_t* out_packed,
                 float* out_cost, int64_t n, int cb, int L, uint8_t* ws, size_t ws_bytes,
                 cudaStream_t stream);

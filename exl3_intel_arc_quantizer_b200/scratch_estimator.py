@@ -109,50 +109,48 @@ class ScratchEstimator:
                                                 bytes_per_edge=bytes_per_edge)
 
 
-def b200_backpointer_step_bytes(k: int) -> int:
-    """Backpointer bytes per trellis step of one tile in the single-tile
-    (K = 1) B200 encoder (mirrors ``Geo<1>::BPS`` in csrc/encoder.cu)."""
-    if k != 1:
-        raise ValueError("only the K = 1 encoder stores backpointers; K >= 2 stores "
-                         "cost checkpoints (b200_checkpoint_bytes)")
-    return 2 * 512 * 4
-
-
 def b200_checkpoint_stride(k: int) -> int:
-    """Steps between cost checkpoints of the tile-pair encoder (K >= 2)."""
-    return 2 if k == 2 else 1
+    """Steps between cost checkpoints: the tile-pair encoder (K >= 2) every
+    2nd step at K=2 and every step above; the single-tile K=1 encoder every
+    4th step."""
+    if not 1 <= k <= 8:
+        raise ValueError(f"K must be in 1..8, got {k}")
+    return 4 if k == 1 else (2 if k == 2 else 1)
 
 
 def b200_checkpoint_slots(k: int, t: int = 256) -> Tuple[int, int]:
-    """Checkpointed steps of pass 1 and pass 2 (``ck_slots_pass1/2`` in
-    csrc/acs_pair.cu)."""
+    """Checkpointed steps of pass 1 and pass 2 (``ck_slots_pass1/2`` and
+    ``single_slots_pass1/2`` in csrc/acs_pair.cu)."""
     r = b200_checkpoint_stride(k)
     return (t - t // 2 - 1) // r + 1, (t - 1) // r
 
 
+def _checkpoint_word_bytes(k: int) -> int:
+    # a pair checkpoint holds {cost_A, cost_B} per edge; K=1's one fp16 per edge
+    return 2 if k == 1 else 4
+
+
 def b200_checkpoint_bytes(k: int, t: int = 256) -> int:
-    """Checkpoint workspace of one tile pair (``pair_ck_bytes``): the larger
-    pass's slots x (65536 >> K) edges x 4 bytes, 256-byte aligned."""
+    """Checkpoint workspace of one encoding unit (a tile pair for K >= 2,
+    ``pair_ck_bytes``; one tile for K = 1, ``single_ck_bytes``): the larger
+    pass's slots x (65536 >> K) edges x word bytes, 256-byte aligned."""
     s1, s2 = b200_checkpoint_slots(k, t)
-    b = max(s1, s2) * (65536 >> k) * 4
+    b = max(s1, s2) * (65536 >> k) * _checkpoint_word_bytes(k)
     return -(-b // 256) * 256
 
 
 def b200_hbm_bytes_written_per_tile(k: int, t: int = 256) -> int:
-    """Trellis bytes one tile writes to HBM over both passes: K = 1 its
-    backpointers (t/2 + t steps); K >= 2 half of every checkpoint of the
-    pair."""
-    if k == 1:
-        return (t // 2 + t) * b200_backpointer_step_bytes(1)
+    """Trellis bytes one tile writes to HBM over both passes: every
+    checkpoint of its unit (half of a pair's for K >= 2)."""
     s1, s2 = b200_checkpoint_slots(k, t)
-    return (s1 + s2) * (65536 >> k) * 4 // 2
+    per_unit = (s1 + s2) * (65536 >> k) * _checkpoint_word_bytes(k)
+    return per_unit if k == 1 else per_unit // 2
 
 
 def b200_workspace_bytes(k: int, t: int = 256, b: int = 1) -> int:
     """Device workspace of the B200 encoder for ``b`` tiles (matches
     ``exl3_quantize_tiles_ws_bytes``; K >= 2 rounds ``b`` up to whole pairs)."""
     if k == 1:
-        per = -(-(t * b200_backpointer_step_bytes(k)) // 256) * 256 + 8
-        return b * per
+        return b * (b200_checkpoint_bytes(k, t) + 8)
     b = b + (b & 1)
     return b * (b200_checkpoint_bytes(k, t) // 2 + 8)
