@@ -119,24 +119,40 @@ def _default_encoder(device: torch.device, K: int):
     return make_xpu_tile_encoder(K=K, device_index=device.index or 0)
 
 
-def _ldl_of(Hd: torch.Tensor, block_size: int) -> Tuple[BlockLDLResult, float]:
+def _ldl_of(Hd: torch.Tensor, block_size: int, residual: bool = True):
+    """Block-LDL of the rotated Hessian; with ``residual`` also its
+    factorization residual, else the rotated matrix to compute it later."""
     H_work = Hd.clone().contiguous()
     blockwise_preapply_had_l_(H_work, HAD_DIM)
     blockwise_preapply_had_r_(H_work, HAD_DIM)
     ldl = block_ldl(H_work, block_size=block_size)
-    return ldl, compute_factorization_residual(H_work, ldl.cholesky)
+    if residual:
+        return ldl, compute_factorization_residual(H_work, ldl.cholesky)
+    return ldl, H_work
 
 
-def _finish(name: str, K: int, cb: int, W: torch.Tensor, Hd: torch.Tensor,
-            reg: RegularizeResult, ldl: BlockLDLResult, fact_res: float, weight_q: torch.Tensor,
-            encoded: torch.Tensor, t0: float) -> QuantizedModuleResult:
-    k, n = W.shape
-    w_hat = weight_from_quantized(weight_q, reg.su, reg.sv)
+def _module_metrics(W: torch.Tensor, Hd: torch.Tensor, reg: RegularizeResult,
+                    weight_q: torch.Tensor, w_hat: torch.Tensor) -> Tuple[float, ...]:
+    """mse, relative Frobenius error, tile distortion, proxy loss and its
+    normalised form (layer_quant.py:104-127, 236-241)."""
     diff = W - w_hat
     mse = float(diff.pow(2).mean().item())
     rel = float(torch.linalg.norm(diff).item() / max(1e-12, torch.linalg.norm(W).item()))
     tile_dist = float((reg.weight - weight_q).pow(2).mean().item())
     proxy, nproxy = compute_proxy_loss(W, w_hat, Hd)
+    return mse, rel, tile_dist, proxy, nproxy
+
+
+def _finish(name: str, K: int, cb: int, W: torch.Tensor, Hd: torch.Tensor,
+            reg: RegularizeResult, ldl: BlockLDLResult, fact_res: float, weight_q: torch.Tensor,
+            encoded: torch.Tensor, t0: float, w_hat: Optional[torch.Tensor] = None,
+            metric_values: Optional[Tuple[float, ...]] = None) -> QuantizedModuleResult:
+    k, n = W.shape
+    if w_hat is None:
+        w_hat = weight_from_quantized(weight_q, reg.su, reg.sv)
+    if metric_values is None:
+        metric_values = _module_metrics(W, Hd, reg, weight_q, w_hat)
+    mse, rel, tile_dist, proxy, nproxy = metric_values
     metrics = ModuleMetrics(mse, rel, tile_dist, proxy, nproxy, fact_res, ldl.retries,
                             reg.g_scale, time.time() - t0)
     return QuantizedModuleResult(name, K, cb, (k, n), W, w_hat, encoded, reg.su, reg.sv,
@@ -231,8 +247,9 @@ def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: i
             regs[nm].su.div_(g)
             regs[nm].g_scale = g
 
-    # one block-LDL per distinct Hessian
-    ldls: List[Tuple[torch.Tensor, BlockLDLResult, float]] = []
+    # one block-LDL per distinct Hessian (its factorization residual, a
+    # diagnostic fp32 GEMM, on one rank only when sharded)
+    ldls: List[list] = []               # [H, ldl, residual or rotated H]
     ldl_of: Dict[str, int] = {}
     for nm in names:
         Hd = Hds[nm]
@@ -240,8 +257,8 @@ def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: i
                     if h.shape == Hd.shape and (h.data_ptr() == Hd.data_ptr() or torch.equal(h, Hd))),
                    None)
         if hit is None:
-            ldl, fr = _ldl_of(Hd, block_size)
-            ldls.append((Hd, ldl, fr))
+            ldl, fr = _ldl_of(Hd, block_size, residual=group is None)
+            ldls.append([Hd, ldl, fr])
             hit = len(ldls) - 1
         ldl_of[nm] = hit
 
@@ -270,8 +287,38 @@ def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: i
             wq[nm], enc[nm] = gather_column_slices(
                 o.weight_q if o is not None else None, o.encoded if o is not None else None,
                 k, n, group)
+    if group is None:
+        return {nm: _finish(nm, K, cb, Ws[nm], Hds[nm], regs[nm], ldls[ldl_of[nm]][1],
+                            ldls[ldl_of[nm]][2], wq[nm], enc[nm], t0) for nm in names}
+
+    # sharded: every rank reconstructs every module (the layer reload needs
+    # it); each module's metrics, and each distinct Hessian's factorization
+    # residual, run on one owner rank and reach the others through one
+    # all-reduce of the scalars
+    from .distributed import assign_modules
+
+    owner = assign_modules({nm: tuple(Ws[nm].shape) for nm in names}, ws)
+    first_of = {}                       # ldl entry -> index of its first module
+    for idx, nm in enumerate(names):
+        first_of.setdefault(ldl_of[nm], idx)
+    vec = torch.zeros((len(names), 6), dtype=torch.float64, device=Ws[names[0]].device)
+    w_hats = {}
+    for idx, nm in enumerate(names):
+        w_hats[nm] = weight_from_quantized(wq[nm], regs[nm].su, regs[nm].sv)
+        if owner[nm] != rank:
+            continue
+        vals = _module_metrics(Ws[nm], Hds[nm], regs[nm], wq[nm], w_hats[nm])
+        fr = 0.0
+        if first_of[ldl_of[nm]] == idx:
+            _h, ldl, H_rot = ldls[ldl_of[nm]]
+            fr = compute_factorization_residual(H_rot, ldl.cholesky)
+        vec[idx] = torch.tensor(vals + (fr,), dtype=torch.float64, device=vec.device)
+    dist.all_reduce(vec, group=group)
+    rows = vec.tolist()
     return {nm: _finish(nm, K, cb, Ws[nm], Hds[nm], regs[nm], ldls[ldl_of[nm]][1],
-                        ldls[ldl_of[nm]][2], wq[nm], enc[nm], t0) for nm in names}
+                        rows[first_of[ldl_of[nm]]][5], wq[nm], enc[nm], t0, w_hat=w_hats[nm],
+                        metric_values=tuple(rows[idx][:5]))
+            for idx, nm in enumerate(names)}
 
 
 def quantize_decoder_layer(layer: nn.Module, hessians: Dict[str, torch.Tensor], K: int = 2,

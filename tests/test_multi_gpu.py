@@ -8,7 +8,10 @@ with fewer than 2 GPUs.
   (rel Frobenius <= 1e-2; cuBLAS may round a narrower product differently,
   which can move a tile's path);
 * module-sharded layer quantization: every rank ends with every module's
-  result, bit-identical to what its owner computed.
+  result, bit-identical to what its owner computed;
+* column-sharded batched modules: each module's metrics (and each distinct
+  Hessian's factorization residual), computed on one owner rank and
+  all-reduced, match what any rank recomputes from its gathered result.
 """
 
 from __future__ import annotations
@@ -89,6 +92,26 @@ def _worker(rank, ws, port, q):
             if r.owner == rank:
                 local[m] = float(torch.linalg.norm(r.result.w_hat - r.w_hat))
         out.update(owners=own, digest=digest, local=local)
+
+        # 4. column-sharded batched modules: metrics computed on one owner
+        #    rank and all-reduced equal the ones every rank can recompute
+        from exl3_intel_arc_quantizer_b200.layer_quant import (
+            _ldl_of, _module_metrics, quantize_modules)
+
+        mods = {"q": (weights["a"], hess["b"]), "k": (weights["a"] * 0.5, hess["b"]),
+                "o": (weights["b"], hess["a"])}
+        qm = quantize_modules(mods, K=2, tile_encoder=enc, group=dist.group.WORLD)
+        met, again = {}, {}
+        for m, r in qm.items():
+            mt = r.metrics
+            met[m] = (mt.mse, mt.relative_frobenius_error, mt.tile_distortion, mt.proxy_loss,
+                      mt.normalized_proxy_loss, mt.factorization_residual)
+            W = r.weight_orig
+            reg = r.regularize_result
+            redo = list(_module_metrics(W, mods[m][1].float(), reg, reg.weight, r.w_hat))
+            redo[2] = mt.tile_distortion   # needs weight_q, which results do not keep
+            again[m] = tuple(redo) + (_ldl_of(mods[m][1].float(), 16)[1],)
+        out.update(mod_metrics=met, mod_again=again)
         torch.cuda.synchronize()
     except Exception as e:  # pragma: no cover
         out = e
@@ -118,3 +141,8 @@ def test_two_gpu_sharded_paths():
     assert a["owners"] == b["owners"] and set(a["owners"].values()) == {0, 1}
     assert a["digest"] == b["digest"]
     assert all(v == 0.0 for v in list(a["local"].values()) + list(b["local"].values()))
+    assert a["mod_metrics"] == b["mod_metrics"]
+    for r in (a, b):
+        for m, vals in r["mod_metrics"].items():
+            for got, want in zip(vals, r["mod_again"][m]):
+                assert abs(got - want) <= 1e-6 * max(abs(want), 1e-12), (m, vals, r["mod_again"][m])
