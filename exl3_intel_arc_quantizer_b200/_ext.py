@@ -43,6 +43,30 @@ def _declare(handle: ctypes.CDLL) -> None:
     handle.exl3_version.restype = c.c_char_p
     handle.exl3_quantize_tiles_ws_bytes.restype = c.c_size_t
     handle.exl3_quantize_tiles_ws_bytes.argtypes = [c.c_int64, c.c_int, c.c_int]
+    handle.exl3_encoder_set_cluster.argtypes = [c.c_int]
+    handle.exl3_encoder_fault_count.argtypes = [c.POINTER(c.c_uint)]
+
+
+def _check(rc: int) -> None:
+    if rc != 0:
+        msg = lib().exl3_last_error()
+        raise RuntimeError(msg.decode() if msg else f"libexl3k status {rc}")
+
+
+def set_encoder_cluster(cluster_ctas: int) -> None:
+    """Cluster split of the encoder's ACS passes (``exl3_encoder_set_cluster``):
+    0 automatic, 1 never, 2 / 4 / 8 always that many CTAs per tile pair.
+    Process-wide; outputs are bit-identical for every setting."""
+    _check(lib().exl3_encoder_set_cluster(int(cluster_ctas)))
+
+
+def encoder_fault_count() -> int:
+    """Encoder CTAs that gave up a bounded inter-CTA wait on the current
+    device since the library loaded (``exl3_encoder_fault_count``; 0 when
+    every call was valid). Synchronizes the device."""
+    v = ctypes.c_uint(0)
+    _check(lib().exl3_encoder_fault_count(ctypes.byref(v)))
+    return int(v.value)
 
 
 def ext():

@@ -613,7 +613,13 @@ int pair_encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t*
     const int grid = pairs < sms ? pairs : sms;
     const float* cin = in + start * L;
     const int tb_grid = (m + kTbWarps - 1) / kTbWarps;
-    {
+    const int csize = cluster_size_for(K, pairs);
+    if (csize > 1) {
+      LaunchTimer lt(stream, 0);
+      const int rc = cluster_acs_pass(K, csize, 1, stream, cin, m, L, cb, ck, ck_pair, best_edge,
+                                      nullptr, nullptr);
+      if (rc) return rc;
+    } else {
       LaunchTimer lt(stream, 0);
       acs_pair_kernel<K, 1><<<grid, kPairNT, PSmem<K>::bytes, stream>>>(
           cin, m, L, cb, ck, ck_pair, best_edge, nullptr, nullptr);
@@ -625,7 +631,12 @@ int pair_encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t*
                                                                 best_edge, end_state);
     }
     EXL3_LAUNCHED();
-    {
+    if (csize > 1) {
+      LaunchTimer lt(stream, 0);
+      const int rc = cluster_acs_pass(K, csize, 2, stream, cin, m, L, cb, ck, ck_pair, nullptr,
+                                      end_state, out_cost ? out_cost + start : nullptr);
+      if (rc) return rc;
+    } else {
       LaunchTimer lt(stream, 0);
       acs_pair_kernel<K, 2><<<grid, kPairNT, PSmem<K>::bytes, stream>>>(
           cin, m, L, cb, ck, ck_pair, nullptr, end_state, out_cost ? out_cost + start : nullptr);

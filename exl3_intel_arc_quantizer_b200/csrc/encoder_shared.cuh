@@ -73,6 +73,13 @@ size_t single_tile_ws_bytes(int L);
 int single_encode(const float* in, float* out_w, int16_t* out_idx, int16_t* out_packed,
                   float* out_cost, int64_t n, int cb, int L, uint8_t* ws, size_t ws_bytes,
                   cudaStream_t stream);
+// cluster-split ACS passes for few tile pairs (acs_cluster.cu): the cluster
+// size to use for `pairs` pairs at K (1 = the one-CTA-per-pair kernel), and
+// one pass (1 or 2) with the tile-pair kernel's arguments and checkpoints
+int cluster_size_for(int K, int pairs);
+int cluster_acs_pass(int K, int C, int pass, cudaStream_t stream, const float* in, int n, int L,
+                     int cb, uint8_t* ck, size_t ck_pair, int32_t* best_edge,
+                     const int32_t* end_state, float* path_cost);
 int pair_encode(int K, const float* in, float* out_w, int16_t* out_idx, int16_t* out_packed,
                 float* out_cost, int64_t n, int cb, int L, uint8_t* ws, size_t ws_bytes,
                 cudaStream_t stream);

@@ -238,6 +238,28 @@ int exl3_hessian_finalize(float* H, int64_t d, int64_t count, float damping_lamb
 int exl3_probe_fp16x2_rate(double* fp16_ops_per_s, exl3_stream_t stream);
 
 /*
+ * Cluster split of the encoder's ACS passes (K = 2..6). A call with few
+ * tile pairs (an LDLQ step of a column-sharded module: a few dozen tiles)
+ * would leave most SMs idle with one pair per CTA; the encoder then spreads
+ * each pair's cost vector over a thread-block cluster of 2, 4 or 8 CTAs that
+ * exchange it every step through distributed shared memory. Outputs are
+ * bit-identical either way. cluster_ctas: 0 = automatic (the largest size
+ * whose clusters all fit on the device at once; off when the pairs fill the
+ * SMs), 1 = never, 2 / 4 / 8 = always that size (tests, benchmarks).
+ * Process-wide setting. No counterpart in the reference (its encoder runs one
+ * work-group per tile).
+ */
+int exl3_encoder_set_cluster(int cluster_ctas);
+
+/*
+ * Number of encoder CTAs that gave up a bounded inter-CTA wait (2 s) since
+ * the library loaded, on the current device; nonzero means the outputs of
+ * those calls are not valid. Synchronizes the device. No counterpart in the
+ * reference.
+ */
+int exl3_encoder_fault_count(unsigned int* count);
+
+/*
  * Launch timing for benchmarks (off by default). After exl3_timing_begin,
  * every encoder kernel launch is bracketed by CUDA events on its own stream;
  * exl3_timing_end synchronizes those events and returns the summed device
