@@ -284,6 +284,42 @@ def run_layer(device, K=4, reps=2, skip_g_scale=True):
     }
 
 
+def run_small_calls(device, Ks=(2, 4), sizes=(2, 16, 30, 32, 64), reps=10):
+    """Latency of one encoder call of a few tiles (an LDLQ step of a
+    column-sharded module), with the cluster-split ACS (automatic choice)
+    and with one CTA per tile pair, in ms per call."""
+    import torch
+
+    from exl3_intel_arc_quantizer_b200._ext import set_encoder_cluster
+    from exl3_intel_arc_quantizer_b200.xpu_quantizer import XPUTrellisEncoder
+
+    out = []
+    try:
+        for K in Ks:
+            enc = XPUTrellisEncoder(K=K, device_index=device.index or 0)
+            for n in sizes:
+                x = make_tiles(n, 900 + n, device)
+                row = {"K": K, "tiles": n}
+                for name, pol in (("cluster_auto_ms", 0), ("one_cta_per_pair_ms", 1)):
+                    set_encoder_cluster(pol)
+                    for _ in range(3):
+                        enc.encode_device(x)
+                    torch.cuda.synchronize()
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    for _ in range(reps):
+                        enc.encode_device(x)
+                    e1.record()
+                    e1.synchronize()
+                    row[name] = e0.elapsed_time(e1) / reps
+                out.append(row)
+            enc.arena.release()
+    finally:
+        set_encoder_cluster(0)
+    return out
+
+
 def run_hessian(device, tokens=262144, dims=(4096, 12288), steps=3, warmup=2):
     """Hessian accumulation H += X^T X (tcgen05 kernel) on BASELINE config 4
     shapes: `tokens` bf16 activation rows, one group per width in `dims`.
@@ -635,6 +671,7 @@ def run_b200(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(K)
+    small = run_small_calls(device) if rank == 0 else None
     layer = layer2 = None
     if rank == 0 and not args.no_layer:
         layer = run_layer(device)
@@ -663,6 +700,7 @@ def run_b200(args):
             "layer": layer,
             "layer_k2_gss": layer2,
             "decoder_layer": declayer,
+            "small_calls": small,
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -45,6 +45,7 @@ def _declare(handle: ctypes.CDLL) -> None:
     handle.exl3_quantize_tiles_ws_bytes.argtypes = [c.c_int64, c.c_int, c.c_int]
     handle.exl3_encoder_set_cluster.argtypes = [c.c_int]
     handle.exl3_encoder_fault_count.argtypes = [c.POINTER(c.c_uint)]
+    handle.exl3_encoder_cluster_capacity.argtypes = [c.c_int, c.c_int, c.POINTER(c.c_int)]
 
 
 def _check(rc: int) -> None:
@@ -58,6 +59,15 @@ def set_encoder_cluster(cluster_ctas: int) -> None:
     0 automatic, 1 never, 2 / 4 / 8 always that many CTAs per tile pair.
     Process-wide; outputs are bit-identical for every setting."""
     _check(lib().exl3_encoder_set_cluster(int(cluster_ctas)))
+
+
+def encoder_cluster_capacity(K: int, cluster_ctas: int) -> int:
+    """Clusters of ``cluster_ctas`` CTAs of the K-bit encoder that the current
+    device holds at once (``exl3_encoder_cluster_capacity``; 0 = not
+    available for this K)."""
+    v = ctypes.c_int(0)
+    _check(lib().exl3_encoder_cluster_capacity(int(K), int(cluster_ctas), ctypes.byref(v)))
+    return int(v.value)
 
 
 def encoder_fault_count() -> int:

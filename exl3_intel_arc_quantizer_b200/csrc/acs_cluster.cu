@@ -565,7 +565,9 @@ template <int K>
 int choose(int pairs, int sms, int dev) {
   if (K < 2 || K > 6 || g_cluster_policy == 1) return 1;
   if (g_cluster_policy >= 2) return max_active_for<K>(g_cluster_policy, dev) > 0 ? g_cluster_policy : 1;
-  for (int C = 8; C >= 2; C >>= 1) {
+  // K = 2 with 2 CTAs moves 16 KiB per CTA and step through DSMEM, which
+  // costs as much as the halved arithmetic saves (measured): not used
+  for (int C = 8; C >= (K == 2 ? 4 : 2); C >>= 1) {
     if ((int64_t)pairs * C > sms) continue;
     if (max_active_for<K>(C, dev) >= pairs) return C;
   }
@@ -643,6 +645,26 @@ extern "C" int exl3_encoder_set_cluster(int cluster_ctas) {
                    cluster_ctas == 8,
                "cluster size must be 0 (automatic), 1 (off), 2, 4 or 8, got %d", cluster_ctas);
   g_cluster_policy = cluster_ctas;
+  return EXL3_OK;
+}
+
+extern "C" int exl3_encoder_cluster_capacity(int K, int cluster_ctas, int* clusters) {
+  EXL3_REQUIRE(clusters != nullptr, "clusters is NULL");
+  EXL3_REQUIRE(K >= 1 && K <= 8, "K must be in 1..8, got %d", K);
+  EXL3_REQUIRE(cluster_ctas == 2 || cluster_ctas == 4 || cluster_ctas == 8,
+               "cluster size must be 2, 4 or 8, got %d", cluster_ctas);
+  int dev = 0;
+  EXL3_CUDA(cudaGetDevice(&dev));
+  int n = 0;
+  switch (K) {
+    case 2: n = max_active_for<2>(cluster_ctas, dev); break;
+    case 3: n = max_active_for<3>(cluster_ctas, dev); break;
+    case 4: n = max_active_for<4>(cluster_ctas, dev); break;
+    case 5: n = max_active_for<5>(cluster_ctas, dev); break;
+    case 6: n = max_active_for<6>(cluster_ctas, dev); break;
+    default: n = 0;
+  }
+  *clusters = n > 0 ? n : 0;
   return EXL3_OK;
 }
 

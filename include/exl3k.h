@@ -252,6 +252,14 @@ int exl3_probe_fp16x2_rate(double* fp16_ops_per_s, exl3_stream_t stream);
 int exl3_encoder_set_cluster(int cluster_ctas);
 
 /*
+ * How many clusters of `cluster_ctas` CTAs (2, 4, 8) of the K-bit cluster
+ * encoder the current device runs at once (0: that split is not available
+ * for K, e.g. K = 1, 7, 8). Tile pairs beyond it take another wave. No
+ * counterpart in the reference.
+ */
+int exl3_encoder_cluster_capacity(int K, int cluster_ctas, int* clusters);
+
+/*
  * Number of encoder CTAs that gave up a bounded inter-CTA wait (2 s) since
  * the library loaded, on the current device; nonzero means the outputs of
  * those calls are not valid. Synchronizes the device. No counterpart in the

@@ -13,7 +13,11 @@ import pytest
 torch = pytest.importorskip("torch")
 
 from exl3_intel_arc_quantizer_b200 import trellis_format as tf  # noqa: E402
-from exl3_intel_arc_quantizer_b200._ext import encoder_fault_count, set_encoder_cluster  # noqa: E402
+from exl3_intel_arc_quantizer_b200._ext import (  # noqa: E402
+    encoder_cluster_capacity,
+    encoder_fault_count,
+    set_encoder_cluster,
+)
 from exl3_intel_arc_quantizer_b200.xpu_quantizer import XPUTrellisEncoder  # noqa: E402
 from oracle.trellis_oracle import COracle  # noqa: E402
 
@@ -115,3 +119,15 @@ def test_automatic_policy_matches_off():
         auto = _encode(2, tf.CB_MUL1, tiles, 0)
         for a, b in zip(auto, off):
             np.testing.assert_array_equal(a, b)
+
+
+def test_cluster_capacity_and_policy_validation():
+    for K in (2, 3, 4, 5, 6):
+        assert encoder_cluster_capacity(K, 8) >= 1
+        assert encoder_cluster_capacity(K, 2) >= encoder_cluster_capacity(K, 8)
+    for K in (1, 7, 8):
+        assert encoder_cluster_capacity(K, 4) == 0
+    with pytest.raises(RuntimeError):
+        set_encoder_cluster(3)
+    with pytest.raises(RuntimeError):
+        encoder_cluster_capacity(2, 16)
