@@ -19,11 +19,16 @@
 // plus, when a matrix finishes a span, ldlq_span_kernel: the trailing
 // update, restricted to the rows above the span (the only ones read later),
 // as a shared-memory tiled fp32 product (fixed summation order, so results
-// are deterministic).
+// are deterministic). Matrices shorter than the longest start at the step
+// schedule_jobs picks, so that a column-sharded layer's short matrices fill
+// steps that would otherwise encode a few tiles at the encoder's latency
+// floor instead of pushing early steps into a second wave.
 #include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
+#include "encoder_shared.cuh"
 
 namespace exl3 {
 namespace {
@@ -176,14 +181,14 @@ using namespace exl3;
 
 namespace {
 
-int check_jobs(const exl3_ldlq_job* jobs, int njobs, int buf) {
+int check_jobs(const exl3_ldlq_job* jobs, int njobs, int buf, bool ptrs = true) {
   EXL3_REQUIRE(jobs != nullptr && njobs >= 1 && njobs <= kMaxJobs,
                "need 1..%d jobs, got %d", kMaxJobs, njobs);
   EXL3_REQUIRE(buf >= 16 && buf <= 128 && buf % 16 == 0,
                "buf_size_k must be a multiple of 16 in [16, 128], got %d", buf);
   for (int i = 0; i < njobs; ++i) {
     const exl3_ldlq_job& J = jobs[i];
-    EXL3_REQUIRE(J.W && J.L && J.W_q && J.encoded, "job %d: NULL pointer", i);
+    EXL3_REQUIRE(!ptrs || (J.W && J.L && J.W_q && J.encoded), "job %d: NULL pointer", i);
     EXL3_REQUIRE(J.k > 0 && J.k % buf == 0, "job %d: rows (%lld) must be a multiple of buf (%d)",
                  i, (long long)J.k, buf);
     EXL3_REQUIRE(J.n > 0 && J.n % 128 == 0, "job %d: columns (%lld) must be a multiple of 128", i,
@@ -216,7 +221,77 @@ void ws_layout(const exl3_ldlq_job* jobs, int njobs, int K, size_t* prod_off, si
   *total = off + *enc_bytes;
 }
 
+// Estimated device time (arbitrary units) of one LDLQ step that encodes
+// `tiles` tiles at K bits: the encoder's latency floor by cluster split for
+// few tile pairs (measured: ~0.45 at 8 CTAs per pair, 0.57-0.78 at 4, 0.8 at
+// 2), one unit per wave of one pair per SM beyond that.
+void step_costs(int K, int max_tiles, std::vector<double>& cost) {
+  cost.assign((size_t)max_tiles + 1, 0.0);
+  const int sms = sm_count();
+  for (int t = 1; t <= max_tiles; ++t) {
+    if (K == 1) {
+      cost[t] = 1.3 * (double)((t + sms - 1) / sms);
+      continue;
+    }
+    const int pairs = (t + 1) / 2;
+    const int c = cluster_size_for(K, pairs);
+    if (c == 8) cost[t] = 0.45;
+    else if (c == 4) cost[t] = K == 2 ? 0.78 : 0.57;
+    else if (c == 2) cost[t] = 0.8;
+    else cost[t] = (double)((pairs + sms - 1) / sms);
+  }
+}
+
+// First step of each job. The longest job spans every step; the others are
+// independent of it, so each may start at any step that lets it finish by
+// the end. Jobs are placed longest first, then widest, each at the start
+// that adds the least estimated time (earliest on ties): on one GPU this
+// front-loads the short matrices into steps that already take several
+// waves; on a column-sharded GPU it keeps a step out of a second wave by
+// moving a matrix into steps that encode only a few tiles.
+void schedule_jobs(const exl3_ldlq_job* jobs, int njobs, int K, int64_t* start) {
+  int64_t H = 0, total = 0;
+  for (int i = 0; i < njobs; ++i) {
+    H = std::max<int64_t>(H, jobs[i].k / 16);
+    total += jobs[i].n / 16;
+  }
+  std::vector<double> cost;
+  step_costs(K, (int)total, cost);
+  std::vector<int> order(njobs);
+  for (int i = 0; i < njobs; ++i) order[i] = i;
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
+    if (jobs[a].k != jobs[b].k) return jobs[a].k > jobs[b].k;
+    return jobs[a].n > jobs[b].n;
+  });
+  std::vector<int64_t> load((size_t)H, 0);
+  std::vector<double> delta((size_t)H + 1, 0.0);
+  for (int i : order) {
+    const int64_t len = jobs[i].k / 16, tl = jobs[i].n / 16;
+    for (int64_t st = 0; st < H; ++st) delta[st + 1] = delta[st] + cost[load[st] + tl] - cost[load[st]];
+    int64_t best = 0;
+    double best_c = delta[len] - delta[0];
+    for (int64_t s0 = 1; s0 + len <= H; ++s0) {
+      const double c = delta[s0 + len] - delta[s0];
+      if (c < best_c - 1e-9) {
+        best_c = c;
+        best = s0;
+      }
+    }
+    start[i] = best;
+    for (int64_t st = best; st < best + len; ++st) load[st] += tl;
+  }
+}
+
 }  // namespace
+
+extern "C" int exl3_ldlq_schedule(const exl3_ldlq_job* jobs, int njobs, int K, int buf,
+                                  int64_t* start_steps) {
+  if (int rc = check_jobs(jobs, njobs, buf, false)) return rc;
+  EXL3_REQUIRE(K >= 1 && K <= 8, "K must be in 1..8, got %d", K);
+  EXL3_REQUIRE(start_steps != nullptr, "start_steps is NULL");
+  schedule_jobs(jobs, njobs, K, start_steps);
+  return EXL3_OK;
+}
 
 extern "C" size_t exl3_ldlq_ws_bytes(const exl3_ldlq_job* jobs, int njobs, int K, int buf) {
   if (check_jobs(jobs, njobs, buf) != EXL3_OK || K < 1 || K > 8) return 0;
@@ -260,6 +335,8 @@ extern "C" int exl3_ldlq(const exl3_ldlq_job* jobs, int njobs, int K, int cb, in
     EXL3_CUDA(cudaMemsetAsync(jobs[i].W_q, 0, (size_t)jobs[i].k * jobs[i].n * 4, s));
     steps = std::max<int64_t>(steps, jobs[i].k / 16);
   }
+  int64_t start[kMaxJobs];
+  schedule_jobs(jobs, njobs, K, start);
   const int bps = buf / 16;  // blocks per span
   for (int64_t st = 0; st < steps; ++st) {
     StepTable tab;
@@ -267,8 +344,9 @@ extern "C" int exl3_ldlq(const exl3_ldlq_job* jobs, int njobs, int K, int cb, in
     int tiles_now = 0;
     for (int i = 0; i < njobs; ++i) {
       const exl3_ldlq_job& J = jobs[i];
-      if (st >= J.k / 16) continue;
-      const int span = (int)(st / bps), blk = (int)(st % bps);
+      const int64_t ls = st - start[i];  // the job's own step
+      if (ls < 0 || ls >= J.k / 16) continue;
+      const int span = (int)(ls / bps), blk = (int)(ls % bps);
       const int span0 = (int)(J.k - (int64_t)(span + 1) * buf);
       const int bi = buf - 16 * (blk + 1);
       StepJob& q = tab.j[tab.njobs++];
@@ -296,8 +374,9 @@ extern "C" int exl3_ldlq(const exl3_ldlq_job* jobs, int njobs, int K, int cb, in
     // spans that just finished: trailing update of the rows above them
     for (int i = 0; i < njobs; ++i) {
       const exl3_ldlq_job& J = jobs[i];
-      if (st >= J.k / 16 || st % bps != bps - 1) continue;
-      const int span = (int)(st / bps);
+      const int64_t ls = st - start[i];
+      if (ls < 0 || ls >= J.k / 16 || ls % bps != bps - 1) continue;
+      const int span = (int)(ls / bps);
       const int span0 = (int)(J.k - (int64_t)(span + 1) * buf);
       if (span0 == 0) continue;  // nothing above
       const dim3 grid((unsigned)((J.n + 63) / 64), (unsigned)((span0 + 63) / 64));

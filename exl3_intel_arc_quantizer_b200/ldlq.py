@@ -221,8 +221,10 @@ def ldlq_native(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor]], K: int, cb: i
                 buf_size_k: int = DEFAULT_BUF_SIZE_K) -> List[LDLQResult]:
     """The LDLQ loop of every ``(weight, L)`` job on the GPU (``exl3_ldlq``):
     the same spans, blocks and feedback as :func:`ldlq` with the B200 encoder,
-    without a host round trip per block; all jobs advance in lockstep with one
-    encoder launch per step. The compensation and trailing products are the
+    without a host round trip per block; one encoder launch per step encodes
+    the current block of every active job (the longest job runs throughout,
+    the others start where :func:`ldlq_schedule` places them; results do not
+    depend on the placement). The compensation and trailing products are the
     library's own fp32 kernels (fixed summation order), so results are close
     to, not bit-identical with, the cuBLAS products of :func:`ldlq`."""
     from ._ext import ext, require_cuda
@@ -241,6 +243,27 @@ def ldlq_native(jobs: Sequence[Tuple[torch.Tensor, torch.Tensor]], K: int, cb: i
     ext().ldlq_(Ws, Ls, Wqs, encs, int(K), int(cb), int(buf))
     return [LDLQResult(wq, e, w.shape[0] // 16, w.shape[1] // 16, int(buf_size_k))
             for w, wq, e in zip(Ws, Wqs, encs)]
+
+
+def ldlq_schedule(shapes: Sequence[Tuple[int, int]], K: int,
+                  buf_size_k: int = DEFAULT_BUF_SIZE_K) -> List[int]:
+    """First step of each ``(k, n)`` job in :func:`ldlq_native` on the current
+    device (``exl3_ldlq_schedule``): longest first, then widest, each at the
+    start that adds the least estimated encoder time."""
+    import ctypes
+
+    from ._ext import lib
+
+    class _Job(ctypes.Structure):
+        _fields_ = [("W", ctypes.c_void_p), ("L", ctypes.c_void_p), ("W_q", ctypes.c_void_p),
+                    ("encoded", ctypes.c_void_p), ("k", ctypes.c_int64), ("n", ctypes.c_int64)]
+
+    arr = (_Job * len(shapes))(*[_Job(None, None, None, None, int(k), int(n)) for k, n in shapes])
+    out = (ctypes.c_int64 * len(shapes))()
+    rc = lib().exl3_ldlq_schedule(arr, len(shapes), int(K), int(buf_size_k), out)
+    if rc:
+        raise ValueError(lib().exl3_last_error().decode())
+    return [int(v) for v in out]
 
 
 def make_xpu_tile_encoder(K: int = 2, device_index: int = 0, arena=None, sg_size: int = 32,

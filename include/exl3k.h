@@ -153,15 +153,29 @@ typedef struct exl3_ldlq_job {
 /*
  * The LDLQ loop (spans of `buf` rows bottom-up, 16-row blocks bottom-up,
  * compensation through L, trailing update after each span) for 1..32
- * independent matrices advanced in lockstep: every step encodes the current
- * 16-row block of all unfinished matrices in one encoder launch. Replaces
- * ldlq (exl3_quant/ldlq.py:163-309) with the B200 encoder as its tile
- * encoder (make_xpu_tile_encoder, ldlq.py:344-387). exl3_ldlq_ws_bytes
+ * independent matrices advanced together: every step encodes the current
+ * 16-row block of each matrix active at that step in one encoder launch.
+ * The longest matrix runs from the first step to the last; every other one
+ * starts at the step exl3_ldlq_schedule picks and then runs its own blocks
+ * without a gap (each matrix's results do not depend on the placement).
+ * Replaces ldlq (exl3_quant/ldlq.py:163-309) with the B200 encoder as its
+ * tile encoder (make_xpu_tile_encoder, ldlq.py:344-387). exl3_ldlq_ws_bytes
  * returns the workspace size (0 on invalid arguments).
  */
 size_t exl3_ldlq_ws_bytes(const exl3_ldlq_job* jobs, int njobs, int K, int buf);
 int exl3_ldlq(const exl3_ldlq_job* jobs, int njobs, int K, int cb, int buf, void* ws,
               size_t ws_bytes, exl3_stream_t stream);
+
+/*
+ * The first step of each job in exl3_ldlq (host array of njobs): jobs go
+ * longest first, then widest, to the start that adds the least estimated
+ * encoder time, from
+ * the current device's SM count and cluster capacity (earliest on ties).
+ * Only the shapes (k, n) of the jobs are read; their pointers may be NULL.
+ * No counterpart in the reference (its loop handles one matrix).
+ */
+int exl3_ldlq_schedule(const exl3_ldlq_job* jobs, int njobs, int K, int buf,
+                       int64_t* start_steps);
 
 /* ------------------------------------------------------------------ */
 /* Storage side: container unpack and weight decode                    */

@@ -226,3 +226,44 @@ def test_ldlq_native_loop(ldlq_golden):
     for (wx, Lx), r in zip(((w1, L1), (w2, L2)), both):
         one = ldlq_native([(wx, Lx)], K=2)[0]
         assert torch.equal(one.weight_q, r.weight_q) and torch.equal(one.encoded, r.encoded)
+
+
+def test_ldlq_schedule_spreads_short_jobs_and_keeps_results():
+    """exl3_ldlq places shorter matrices where they add the least encoder
+    time; a matrix's results do not depend on where it starts."""
+    from exl3_intel_arc_quantizer_b200.ldlq import ldlq_native, ldlq_schedule
+
+    # a column-sharded decoder layer on 8 GPUs (config 4 shapes per rank)
+    shapes = [(4096, 512), (4096, 128), (4096, 128), (4096, 512), (4096, 1536), (4096, 1536),
+              (12288, 512)]
+    st = ldlq_schedule(shapes, K=4)
+    H = 12288 // 16
+    assert st[-1] == 0
+    assert all(0 <= s and s + k // 16 <= H for s, (k, _) in zip(st, shapes))
+    per_step = [0] * H
+    for s, (k, n) in zip(st, shapes):
+        for i in range(s, s + k // 16):
+            per_step[i] += n // 16
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert max(per_step) <= 2 * sms          # no step needs a second wave
+    # the whole layer on one GPU: the short matrices stay in the first steps,
+    # which take several waves anyway
+    full = [(4096, 4096), (4096, 1024), (4096, 1024), (4096, 4096), (4096, 12288),
+            (4096, 12288), (12288, 4096)]
+    assert ldlq_schedule(full, K=2) == [0] * 7
+    with pytest.raises(ValueError):
+        ldlq_schedule([(100, 128)], K=2)
+
+    # placement does not change results: C is moved behind B, each equals alone
+    g = torch.Generator(device="cpu").manual_seed(11)
+    jobs = []
+    for k, n in ((512, 128), (128, 2560), (128, 2560)):
+        a = torch.randn(k, 32, generator=g).to(DEV)
+        L = block_ldl(a @ a.T / 32 + 0.1 * torch.eye(k, device=DEV)).transformed
+        jobs.append((torch.randn(k, n, generator=g).to(DEV), L))
+    st = ldlq_schedule([tuple(w.shape) for w, _ in jobs], K=2)
+    assert st[0] == 0 and st[1] != st[2]
+    together = ldlq_native(jobs, K=2)
+    for job, r in zip(jobs, together):
+        one = ldlq_native([job], K=2)[0]
+        assert torch.equal(one.weight_q, r.weight_q) and torch.equal(one.encoded, r.encoded)
