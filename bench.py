@@ -63,6 +63,11 @@ def parse():
     ap.add_argument("--hessian-tokens", type=int, default=262144)
     ap.add_argument("--layer-only", action="store_true",
                     help="only the 4096x4096 K=4 layer measurement (config 3)")
+    ap.add_argument("--small-call-only", action="store_true",
+                    help="time one encoder call of --tiles tiles at --K (latency of an LDLQ "
+                         "step) with --cluster CTAs per tile pair and exit")
+    ap.add_argument("--cluster", type=int, default=0,
+                    help="encoder cluster split: 0 automatic, 1 off, 2/4/8 forced")
     return ap.parse_args()
 
 
@@ -282,6 +287,46 @@ def run_layer(device, K=4, reps=2, skip_g_scale=True):
         "reference_published_note": "Arc B580, 4096x4096 o_proj, K=2 with global-scale search "
                                     "(reports/discrete_phase_c.md); no K=4 figure is published",
     }
+
+
+def layer_cpu_baseline(K=4, crop=512, threads=None):
+    """Config-3 layer on the host cores through the module oracle
+    (oracle/module_oracle.py: the reference's float stages with torch on the
+    CPU, the C restatement of the encoder on every host thread). The float
+    stages run at full size with a rounding stand-in for the encoder; the
+    encoder runs on a crop x crop corner of the layer (W and its Hessian), and
+    its time is scaled to the layer's 65,536 tiles (extrapolated)."""
+    import torch
+
+    from oracle import module_oracle as mo
+
+    threads = threads or os.cpu_count() or 1
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        W, X = layer_config3("cpu")
+        W, X = W.float(), X.float()
+        t0 = time.perf_counter()
+        H = mo.hessian(X)
+        t_hess = time.perf_counter() - t0
+
+        def rounding(tiles):
+            return torch.round(tiles * 8.0) / 8.0, torch.zeros(tiles.shape, dtype=torch.int16)
+
+        t_float = mo.quantize_module(W, H, K, encode=rounding).seconds
+        Hc = mo.hessian(X[:, :crop])
+        rc = mo.quantize_module(W[:crop, :crop].contiguous(), Hc, K,
+                                encode=mo.c_encoder(K, 2, threads))
+        tiles = crop * crop // 256
+        est = t_hess + t_float + rc.seconds * (65536 / tiles)
+        return {"value": est, "unit": "s per 4096x4096 layer (extrapolated)", "cores": threads,
+                "kind": "port",
+                "sample": f"Hessian {t_hess:.2f}s and float stages {t_float:.2f}s at full size "
+                          f"(rounding stand-in encoder); module with the C encoder on the "
+                          f"{crop}x{crop} corner ({tiles} tiles, {rc.seconds:.1f}s) scaled "
+                          f"x{65536 // tiles} by tiles; K={K}, torch CPU + oracle/trellis_oracle.c"}
+    finally:
+        torch.set_num_threads(prev)
 
 
 def run_small_calls(device, Ks=(2, 4), sizes=(2, 16, 30, 32, 64), reps=10):
@@ -515,6 +560,31 @@ def run_b200(args):
             print(json.dumps({"hessian": run_hessian(device, tokens=args.hessian_tokens)}),
                   flush=True)
         return 0
+    if args.small_call_only:
+        if rank == 0:
+            from exl3_intel_arc_quantizer_b200._ext import set_encoder_cluster
+
+            set_encoder_cluster(args.cluster)
+            try:
+                enc = XPUTrellisEncoder(K=K, cb=2, device_index=local)
+                x = make_tiles(n, 4321, device)
+                for _ in range(args.warmup):
+                    enc.encode_device(x)
+                torch.cuda.synchronize()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(args.steps):
+                    enc.encode_device(x)
+                e1.record()
+                e1.synchronize()
+                print(json.dumps({"small_call": {"K": K, "tiles": n, "cluster": args.cluster,
+                                                 "ms_per_call": e0.elapsed_time(e1) / args.steps}}),
+                      flush=True)
+                enc.arena.release()
+            finally:
+                set_encoder_cluster(0)
+        return 0
     if args.layer_only:
         if rank == 0:
             print(json.dumps({"layer": run_layer(device),
@@ -675,6 +745,8 @@ def run_b200(args):
     layer = layer2 = None
     if rank == 0 and not args.no_layer:
         layer = run_layer(device)
+        if world == 1 and not args.no_cpu_baseline:
+            layer["cpu_baseline"] = layer_cpu_baseline(K=4)
         layer2 = run_layer(device, K=2, skip_g_scale=False)
     if world > 1:
         dist.barrier()
