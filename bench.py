@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--hessian-tokens", type=int, default=262144)
     ap.add_argument("--layer-only", action="store_true",
                     help="only the 4096x4096 K=4 layer measurement (config 3)")
+    ap.add_argument("--storage-only", action="store_true",
+                    help="time pack / unpack / weight decode on config-4 module shapes and exit")
     ap.add_argument("--small-call-only", action="store_true",
                     help="time one encoder call of --tiles tiles at --K (latency of an LDLQ "
                          "step) with --cluster CTAs per tile pair and exit")
@@ -329,6 +331,69 @@ def layer_cpu_baseline(K=4, crop=512, threads=None):
         torch.set_num_threads(prev)
 
 
+def run_storage(device, K=4, shapes=((4096, 4096), (12288, 4096)), reps=5):
+    """Storage side on config-4/5 module shapes: pack (states -> container),
+    unpack (container -> states) and the one-pass weight decode (container ->
+    codebook -> both rotations -> fp32 weight). Each launch timed alone with
+    CUDA events, L2 flushed before it (512 MiB write); bandwidth from the
+    algorithmic bytes: decode K/8 B read + 4 B written per weight, pack
+    2 B read + K/8 B written, unpack K/8 B read + 2 B written."""
+    import torch
+
+    from exl3_intel_arc_quantizer_b200._ext import ext
+
+    peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text()) \
+        if (REPO / "MEASURED_PEAKS.json").exists() else {}
+    hbm = float(peaks.get("hbm_gbs") or 6650.0)
+    e = ext()
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=device)
+    out = []
+    for k, n in shapes:
+        g = torch.Generator(device=device).manual_seed(k + n)
+        tk, tn = k // 16, n // 16
+        # a random container is a valid trellis stream: unpack gives its states
+        container = torch.randint(-32768, 32767, (tk * tn, 16 * K), generator=g, device=device,
+                                  dtype=torch.int32).to(torch.int16)
+        states = torch.empty((tk * tn, 256), dtype=torch.int16, device=device)
+        e.unpack_trellis(container, states, K)
+        packed = torch.empty_like(container)
+        unpacked = torch.empty_like(states)
+        su = (torch.rand(k, generator=g, device=device) + 0.5).half()
+        sv = (torch.rand(n, generator=g, device=device) + 0.5).half()
+        w = torch.empty((k, n), dtype=torch.float32, device=device)
+
+        def timed(fn):
+            best = []
+            for r in range(reps + 1):
+                flush.fill_(r & 0xFF)
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                e1.synchronize()
+                if r:
+                    best.append(e0.elapsed_time(e1))
+            return statistics.median(best)
+
+        t_pack = timed(lambda: e.pack_trellis(states, packed, K))
+        t_unpack = timed(lambda: e.unpack_trellis(packed.view(tk, tn, 16 * K),
+                                                  unpacked.view(tk, tn, 256), K))
+        t_dec = timed(lambda: e.decode_weight(packed.view(tk, tn, 16 * K), su, sv, w, None, K, 2))
+        assert torch.equal(packed, container) and torch.equal(unpacked, states)
+        wts = k * n
+        row = {"shape": [k, n], "K": K,
+               "pack_ms": t_pack, "pack_gbs": wts * (2 + K / 8) / t_pack / 1e6,
+               "unpack_ms": t_unpack, "unpack_gbs": wts * (K / 8 + 2) / t_unpack / 1e6,
+               "decode_ms": t_dec, "decode_gbs": wts * (K / 8 + 4) / t_dec / 1e6}
+        for key in ("pack", "unpack", "decode"):
+            row[f"{key}_frac_of_measured_hbm"] = row[f"{key}_gbs"] / hbm
+        out.append(row)
+    del flush
+    return {"kernels": out, "hbm_peak_gbs": hbm,
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs (copy)" if peaks else "fallback 6650"}
+
+
 def run_small_calls(device, Ks=(2, 4), sizes=(2, 16, 30, 32, 64), reps=10):
     """Latency of one encoder call of a few tiles (an LDLQ step of a
     column-sharded module), with the cluster-split ACS (automatic choice)
@@ -560,6 +625,10 @@ def run_b200(args):
             print(json.dumps({"hessian": run_hessian(device, tokens=args.hessian_tokens)}),
                   flush=True)
         return 0
+    if args.storage_only:
+        if rank == 0:
+            print(json.dumps({"storage": run_storage(device)}), flush=True)
+        return 0
     if args.small_call_only:
         if rank == 0:
             from exl3_intel_arc_quantizer_b200._ext import set_encoder_cluster
@@ -742,6 +811,7 @@ def run_b200(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(K)
     small = run_small_calls(device) if rank == 0 else None
+    storage = run_storage(device) if rank == 0 else None
     layer = layer2 = None
     if rank == 0 and not args.no_layer:
         layer = run_layer(device)
@@ -773,6 +843,7 @@ def run_b200(args):
             "layer_k2_gss": layer2,
             "decoder_layer": declayer,
             "small_calls": small,
+            "storage": storage,
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -28,6 +28,7 @@
 // the winning predecessor of every edge and step.
 #include "common.cuh"
 #include "encoder_shared.cuh"
+#include "trellis_span.cuh"
 
 namespace exl3 {
 
@@ -362,15 +363,36 @@ __global__ void decode_codebook_kernel(int cb, uint16_t* __restrict__ out) {
   if (s < 65536) out[s] = cb_state_bits(cb, (uint32_t)s);
 }
 
-__global__ void pack_kernel(const int16_t* __restrict__ states, int16_t* __restrict__ packed,
-                            int n, int K) {
-  __shared__ uint16_t st[kTbWarps][256];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x * kTbWarps + warp;
-  if (tile >= n) return;
-  for (int i = lane; i < 256; i += 32) st[warp][i] = (uint16_t)states[(size_t)tile * 256 + i];
+// One thread per span: its 16 states come in as two 16-byte loads (a warp
+// reads two tiles' states, 1 KiB, contiguously), its K packed words go to a
+// warp-private shared buffer in storage (SWAP16) order, and the warp writes
+// its two tiles' containers with coalesced 32-bit stores.
+constexpr int kPackThreads = 256;
+
+template <int K>
+__global__ void __launch_bounds__(kPackThreads)
+pack_kernel(const int16_t* __restrict__ states, uint32_t* __restrict__ packed, int64_t n) {
+  __shared__ uint16_t words[kPackThreads / 32][2 * 16 * K];
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int64_t tile0 = ((int64_t)blockIdx.x * (kPackThreads / 32) + warp) * 2;
+  const int nt = (int)(n - tile0 < 2 ? n - tile0 : 2);
+  if (nt <= 0) return;
+  const int tt = lane >> 4, sp = lane & 15;
+  if (tt < nt) {
+    const uint4* src = reinterpret_cast<const uint4*>(states + (tile0 + tt) * 256 + 16 * sp);
+    const uint4 a = src[0], b = src[1];
+    const uint32_t st[16] = {a.x & 0xFFFFu, a.x >> 16, a.y & 0xFFFFu, a.y >> 16,
+                             a.z & 0xFFFFu, a.z >> 16, a.w & 0xFFFFu, a.w >> 16,
+                             b.x & 0xFFFFu, b.x >> 16, b.y & 0xFFFFu, b.y >> 16,
+                             b.z & 0xFFFFu, b.z >> 16, b.w & 0xFFFFu, b.w >> 16};
+    uint32_t w[K];
+    span_words<K>(st, w);
+#pragma unroll
+    for (int j = 0; j < K; ++j) words[warp][tt * 16 * K + ((sp * K + j) ^ 1)] = (uint16_t)w[j];
+  }
   __syncwarp();
-  if (lane < 16) pack_span(st[warp], K, lane, packed + (size_t)tile * 16 * K);
+  const uint32_t* wsm = reinterpret_cast<const uint32_t*>(words[warp]);
+  for (int i = lane; i < nt * 8 * K; i += 32) packed[tile0 * 8 * K + i] = wsm[i];
 }
 
 // ---------------------------------------------------------------------------
@@ -506,8 +528,14 @@ extern "C" int exl3_pack_trellis(const int16_t* states, int16_t* packed, int64_t
                                  exl3_stream_t stream) {
   EXL3_REQUIRE(K >= 1 && K <= 8, "K must be in 1..8, got %d", K);
   EXL3_REQUIRE(n > 0 && states && packed, "bad arguments");
-  pack_kernel<<<(int)((n + kTbWarps - 1) / kTbWarps), 32 * kTbWarps, 0, (cudaStream_t)stream>>>(
-      states, packed, (int)n, K);
+  EXL3_REQUIRE(reinterpret_cast<uintptr_t>(states) % 16 == 0, "states must be 16-byte aligned");
+  EXL3_REQUIRE(reinterpret_cast<uintptr_t>(packed) % 4 == 0, "packed must be 4-byte aligned");
+  const int64_t tiles_per_cta = 2 * (kPackThreads / 32);
+  const int64_t blocks = (n + tiles_per_cta - 1) / tiles_per_cta;
+  EXL3_REQUIRE(blocks < (1ll << 31), "too many tiles");
+  uint32_t* pw = reinterpret_cast<uint32_t*>(packed);
+  cudaStream_t s = (cudaStream_t)stream;
+  EXL3_SWITCH_K(K, (pack_kernel<KK><<<(unsigned)blocks, kPackThreads, 0, s>>>(states, pw, n)));
   EXL3_LAUNCHED();
   return EXL3_OK;
 }

@@ -11,16 +11,19 @@ namespace exl3 {
 
 constexpr float kHad128Scale = 0.08838834764831845f;  // 1/sqrt(128)
 
-__device__ __forceinline__ float had_bfly(float mine, float other, bool upper) {
-  return upper ? (other - mine) : (mine + other);
+// Butterfly across lanes: the lower element keeps mine + other, the upper
+// one other - mine, as one fma with a +-1 factor (an exact product, so the
+// single rounding is that of the addition or subtraction).
+__device__ __forceinline__ float had_bfly(float mine, float other, float sign) {
+  return fmaf(sign, mine, other);
 }
 
 __device__ __forceinline__ void fwht128_warp(float (&v)[4], int lane) {
 #pragma unroll
   for (int h = 1; h < 32; h <<= 1) {
-    const bool up = (lane & h) != 0;
+    const float sign = (lane & h) ? -1.0f : 1.0f;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) v[q] = had_bfly(v[q], __shfl_xor_sync(0xFFFFFFFFu, v[q], h), up);
+    for (int q = 0; q < 4; ++q) v[q] = had_bfly(v[q], __shfl_xor_sync(0xFFFFFFFFu, v[q], h), sign);
   }
   const float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
   v[0] = a0 + a2;

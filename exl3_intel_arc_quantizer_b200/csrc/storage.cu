@@ -20,48 +20,42 @@
 
 #include "common.cuh"
 #include "hadamard.cuh"
+#include "trellis_span.cuh"
 
 namespace exl3 {
 namespace {
 
 constexpr int kDB = 128;          // block edge
 constexpr int kDPitch = kDB + 1;  // padded row pitch (conflict-free column walks)
-constexpr int kDThreads = 256;
+constexpr int kDThreads = 256;   // unpack
+constexpr int kDecThreads = 256; // decode: four spans per thread
+constexpr int kUTiles = 16;       // tiles per unpack CTA (two per warp)
 
-// packed (un-swapped) word j of a tile whose storage starts at `st`
-__device__ __forceinline__ uint32_t packed_word(const uint16_t* st, int j) {
-  return st[j ^ 1];
-}
-
-// the 16-bit state of element t from a tile's storage words (16*K words)
-__device__ __forceinline__ uint32_t tile_state(const uint16_t* st, int K, int t) {
-  const int nbits = 256 * K;
-  const int nwords = 16 * K;
-  int b0 = (t + 1) * K - 16;
-  if (b0 < 0) b0 += nbits;
-  const int j = b0 >> 4;
-  const int j1 = (j + 1 == nwords) ? 0 : j + 1;
-  const uint32_t w = (packed_word(st, j) << 16) | packed_word(st, j1);
-  return (w >> (16 - (b0 & 15))) & 0xFFFFu;
-}
-
-// tensor-core permutation: encoded element t sits at tile position r*16+c
-// (trellis_format.py:88-108)
-__device__ __forceinline__ void tc_position(int t, int& r, int& c) {
-  const int g = t >> 3, w = t & 7;
-  const int i = w & 3, j = w >> 2;
-  const int r0 = (g & 3) * 2, c0 = g >> 2;
-  r = r0 + (i & 1) + ((i >> 1) << 3);
-  c = c0 + (j << 3);
-}
-
-__global__ void unpack_trellis_kernel(const uint16_t* __restrict__ trellis,
-                                      int16_t* __restrict__ states, int64_t ntiles, int K) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= ntiles * 256) return;
-  const int64_t tile = i >> 8;
-  const int t = (int)(i & 255);
-  states[i] = (int16_t)tile_state(trellis + tile * 16 * K, K, t);
+// unpack: one thread per span. A warp stages its two tiles' container words
+// in shared memory with coalesced 32-bit loads, then each lane extracts the
+// 16 states of one span and writes them as two 16-byte stores.
+template <int K>
+__global__ void __launch_bounds__(kDThreads)
+unpack_trellis_kernel(const uint32_t* __restrict__ trellis, int16_t* __restrict__ states,
+                      int64_t ntiles) {
+  __shared__ uint16_t words[kUTiles * 16 * K];
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int64_t tile0 = (int64_t)blockIdx.x * kUTiles + 2 * warp;  // this warp's first tile
+  const int nt = (int)(ntiles - tile0 < 2 ? ntiles - tile0 : 2);
+  if (nt <= 0) return;
+  uint32_t* wsm = reinterpret_cast<uint32_t*>(words + 2 * warp * 16 * K);
+  for (int i = lane; i < nt * 8 * K; i += 32) wsm[i] = trellis[tile0 * 8 * K + i];
+  __syncwarp();
+  const int tt = lane >> 4, sp = lane & 15;
+  if (tt >= nt) return;
+  const uint16_t* tw = words + (2 * warp + tt) * 16 * K;
+  uint32_t st[16];
+  span_states<K>([&](int j) { return (uint32_t)tw[j ^ 1]; }, sp, st);
+  uint4* dst = reinterpret_cast<uint4*>(states + (tile0 + tt) * 256 + 16 * sp);
+  dst[0] = make_uint4(st[0] | (st[1] << 16), st[2] | (st[3] << 16), st[4] | (st[5] << 16),
+                      st[6] | (st[7] << 16));
+  dst[1] = make_uint4(st[8] | (st[9] << 16), st[10] | (st[11] << 16), st[12] | (st[13] << 16),
+                      st[14] | (st[15] << 16));
 }
 
 template <int SCALE_F32>
@@ -70,77 +64,128 @@ __device__ __forceinline__ float load_scale(const void* p, int64_t i) {
   return __half2float(static_cast<const __half*>(p)[i]);
 }
 
-template <int SCALE_F32>
-__global__ void __launch_bounds__(kDThreads)
+// decode_weight_kernel: one CTA per 128x128 block of the (k, n) weight (8x8
+// tiles). The block's container words are read once; each thread decodes
+// four spans (16 states each, fixed tile positions) into a padded fp32
+// shared tile; the left rotation (columns, then x su) and the right rotation
+// (rows, then x sv) run in shared memory and the block is written once:
+// HBM traffic = K/8 B read + 4 B written per weight.
+template <int K, int CB, int SCALE_F32>
+__global__ void __launch_bounds__(kDecThreads)
 decode_weight_kernel(const uint16_t* __restrict__ trellis, const void* __restrict__ su,
                      const void* __restrict__ sv, float* __restrict__ out,
-                     float* __restrict__ out_w_hat, int64_t tiles_n, int64_t n, int K, int cb) {
+                     float* __restrict__ out_w_hat, int64_t tiles_n, int64_t n) {
   extern __shared__ __align__(16) uint8_t dsmem[];
   float* blk = reinterpret_cast<float*>(dsmem);                       // 128 x 129 fp32
   uint16_t* words = reinterpret_cast<uint16_t*>(blk + kDB * kDPitch);  // 64 tiles x 16K
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t rb = blockIdx.y, cbk = blockIdx.x;
-  const int wpt = 16 * K;  // storage words per tile
+  constexpr int wpt = 16 * K;  // storage words per tile
 
-  // 1. container words of the 8x8 tiles: each tile row of the block is one
-  //    contiguous run of 8 tiles (8 * 32K bytes), copied as 32-bit words
+  // scales of this block's rows and columns, four per lane
+  float su_r[4], sv_c[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    su_r[q] = load_scale<SCALE_F32>(su, rb * kDB + lane + 32 * q);
+    sv_c[q] = load_scale<SCALE_F32>(sv, cbk * kDB + lane + 32 * q);
+  }
+
+  // 1. container words: each tile row of the block is one contiguous run of
+  //    8 tiles (8 * 32K bytes), copied as 32-bit words
+#pragma unroll
   for (int tr = 0; tr < 8; ++tr) {
     const uint32_t* src = reinterpret_cast<const uint32_t*>(
         trellis + ((rb * 8 + tr) * tiles_n + cbk * 8) * (int64_t)wpt);
     uint32_t* dst = reinterpret_cast<uint32_t*>(words + tr * 8 * wpt);
-    for (int i = tid; i < 4 * wpt; i += kDThreads) dst[i] = src[i];
+    for (int i = tid; i < 4 * wpt; i += kDecThreads) dst[i] = src[i];
   }
   __syncthreads();
 
-  // 2. decode: warp-consecutive elements of one tile
-  for (int i = tid; i < 64 * 256; i += kDThreads) {
-    const int tt = i >> 8, t = i & 255;
-    const uint32_t s = tile_state(words + tt * wpt, K, t);
-    const float v = __half2float(__ushort_as_half(cb_state_bits(cb, s)));
-    int r, c;
-    tc_position(t, r, c);
-    blk[((tt >> 3) * 16 + r) * kDPitch + (tt & 7) * 16 + c] = v;
+  // 2. decode: four spans per thread; span s of tile tt holds elements
+  //    16s..16s+15, whose tensor-core positions (trellis_format.py:88-108)
+  //    are (4(s&1) + dr(u), (s>>1) + dc(u)) with compile-time dr, dc
+#pragma unroll
+  for (int q = 0; q < 1024 / kDecThreads; ++q) {
+    const int spid = q * kDecThreads + tid;
+    const int tt = spid >> 4, s = spid & 15;
+    const uint16_t* tw = words + tt * wpt;
+    uint32_t st[16];
+    span_states<K>([&](int j) { return (uint32_t)tw[j ^ 1]; }, s, st);
+    float* base = blk + ((tt >> 3) * 16 + 4 * (s & 1)) * kDPitch + (tt & 7) * 16 + (s >> 1);
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const int dr = 2 * (u >> 3) + (u & 1) + 8 * ((u >> 1) & 1);
+      const int dc = 8 * ((u >> 2) & 1);
+      base[dr * kDPitch + dc] = __half2float(__ushort_as_half(cb_state_bits(CB, st[u])));
+    }
   }
   __syncthreads();
 
   if (out_w_hat) {  // transformed-basis reconstruction, before the rotations
-    for (int i = tid; i < kDB * kDB; i += kDThreads) {
+    for (int i = tid; i < kDB * kDB; i += kDecThreads) {
       const int r = i >> 7, c = i & 127;
       out_w_hat[(rb * kDB + r) * n + cbk * kDB + c] = blk[r * kDPitch + c];
     }
   }
 
   // 3. H_l on every column, then x su (per row)
-  for (int c = warp; c < kDB; c += kDThreads / 32) {
+  for (int c = warp; c < kDB; c += kDecThreads / 32) {
     float v[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) v[q] = blk[(lane + 32 * q) * kDPitch + c];
     fwht128_warp(v, lane);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float h = v[q] * kHad128Scale;
-      blk[(lane + 32 * q) * kDPitch + c] = h * load_scale<SCALE_F32>(su, rb * kDB + lane + 32 * q);
-    }
+    for (int q = 0; q < 4; ++q) blk[(lane + 32 * q) * kDPitch + c] = (v[q] * kHad128Scale) * su_r[q];
   }
   __syncthreads();
 
   // 4. H_r on every row, then x sv (per column), written straight out
-  for (int r = warp; r < kDB; r += kDThreads / 32) {
+  for (int r = warp; r < kDB; r += kDecThreads / 32) {
     float v[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) v[q] = blk[r * kDPitch + lane + 32 * q];
     fwht128_warp(v, lane);
     float* dst = out + (rb * kDB + r) * n + cbk * kDB;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float h = v[q] * kHad128Scale;
-      dst[lane + 32 * q] = h * load_scale<SCALE_F32>(sv, cbk * kDB + lane + 32 * q);
-    }
+    for (int q = 0; q < 4; ++q) dst[lane + 32 * q] = (v[q] * kHad128Scale) * sv_c[q];
   }
 }
 
 constexpr size_t decode_smem_bytes(int K) {
   return (size_t)kDB * kDPitch * 4 + (size_t)64 * 16 * K * 2;
+}
+
+template <int K, int CB, int F32>
+int launch_decode(const uint16_t* tw, const void* su, const void* sv, float* out, float* w_hat,
+                  int64_t tiles_k, int64_t tiles_n, cudaStream_t stream) {
+  static uint32_t attr_done = 0;  // one bit per device
+  int dev = 0;
+  EXL3_CUDA(cudaGetDevice(&dev));
+  const uint32_t bit = dev < 32 ? (1u << dev) : 0u;
+  if (!(attr_done & bit)) {
+    EXL3_CUDA(cudaFuncSetAttribute(decode_weight_kernel<K, CB, F32>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)decode_smem_bytes(K)));
+    attr_done |= bit;
+  }
+  const dim3 grid((unsigned)(tiles_n / 8), (unsigned)(tiles_k / 8));
+  decode_weight_kernel<K, CB, F32><<<grid, kDecThreads, decode_smem_bytes(K), stream>>>(
+      tw, su, sv, out, w_hat, tiles_n, tiles_n * 16);
+  EXL3_LAUNCHED();
+  return EXL3_OK;
+}
+
+template <int K>
+int decode_k(int cb, int f32, const uint16_t* tw, const void* su, const void* sv, float* out,
+             float* w_hat, int64_t tiles_k, int64_t tiles_n, cudaStream_t stream) {
+  if (cb == 0)
+    return f32 ? launch_decode<K, 0, 1>(tw, su, sv, out, w_hat, tiles_k, tiles_n, stream)
+               : launch_decode<K, 0, 0>(tw, su, sv, out, w_hat, tiles_k, tiles_n, stream);
+  if (cb == 1)
+    return f32 ? launch_decode<K, 1, 1>(tw, su, sv, out, w_hat, tiles_k, tiles_n, stream)
+               : launch_decode<K, 1, 0>(tw, su, sv, out, w_hat, tiles_k, tiles_n, stream);
+  return f32 ? launch_decode<K, 2, 1>(tw, su, sv, out, w_hat, tiles_k, tiles_n, stream)
+             : launch_decode<K, 2, 0>(tw, su, sv, out, w_hat, tiles_k, tiles_n, stream);
 }
 
 }  // namespace
@@ -154,11 +199,14 @@ extern "C" int exl3_unpack_trellis(const int16_t* trellis, int16_t* states, int6
   EXL3_REQUIRE(ntiles >= 0, "ntiles must be non-negative");
   if (ntiles == 0) return EXL3_OK;
   EXL3_REQUIRE(trellis && states, "NULL pointer argument");
-  const int64_t total = ntiles * 256;
-  const int64_t blocks = (total + 255) / 256;
+  EXL3_REQUIRE(reinterpret_cast<uintptr_t>(trellis) % 4 == 0, "trellis must be 4-byte aligned");
+  EXL3_REQUIRE(reinterpret_cast<uintptr_t>(states) % 16 == 0, "states must be 16-byte aligned");
+  const int64_t blocks = (ntiles + kUTiles - 1) / kUTiles;
   EXL3_REQUIRE(blocks < (1ll << 31), "too many tiles");
-  unpack_trellis_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const uint16_t*>(trellis), states, ntiles, K);
+  const uint32_t* tw = reinterpret_cast<const uint32_t*>(trellis);
+  cudaStream_t s = (cudaStream_t)stream;
+  EXL3_SWITCH_K(K, (unpack_trellis_kernel<KK><<<(unsigned)blocks, kDThreads, 0, s>>>(tw, states,
+                                                                                     ntiles)));
   EXL3_LAUNCHED();
   return EXL3_OK;
 }
@@ -176,33 +224,10 @@ extern "C" int exl3_decode_weight(const int16_t* trellis, const void* su, const 
   EXL3_REQUIRE(trellis && su && sv && out, "NULL pointer argument");
   EXL3_REQUIRE(reinterpret_cast<uintptr_t>(trellis) % 4 == 0, "trellis must be 4-byte aligned");
   EXL3_REQUIRE(tiles_k / 8 < 65536, "too many row blocks");
-  const size_t smem = decode_smem_bytes(K);
-  static uint32_t attr_done[2] = {0u, 0u};
-  int dev = 0;
-  EXL3_CUDA(cudaGetDevice(&dev));
-  const uint32_t bit = dev < 32 ? (1u << dev) : 0u;
-  const dim3 grid((unsigned)(tiles_n / 8), (unsigned)(tiles_k / 8));
-  const int64_t n = tiles_n * 16;
   const uint16_t* tw = reinterpret_cast<const uint16_t*>(trellis);
-  if (scale_dtype == 0) {
-    if (!(attr_done[0] & bit)) {
-      EXL3_CUDA(cudaFuncSetAttribute(decode_weight_kernel<0>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)decode_smem_bytes(8)));
-      attr_done[0] |= bit;
-    }
-    decode_weight_kernel<0><<<grid, kDThreads, smem, (cudaStream_t)stream>>>(
-        tw, su, sv, out, out_w_hat, tiles_n, n, K, cb);
-  } else {
-    if (!(attr_done[1] & bit)) {
-      EXL3_CUDA(cudaFuncSetAttribute(decode_weight_kernel<1>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)decode_smem_bytes(8)));
-      attr_done[1] |= bit;
-    }
-    decode_weight_kernel<1><<<grid, kDThreads, smem, (cudaStream_t)stream>>>(
-        tw, su, sv, out, out_w_hat, tiles_n, n, K, cb);
-  }
-  EXL3_LAUNCHED();
-  return EXL3_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  int rc = EXL3_OK;
+  EXL3_SWITCH_K(K, (rc = decode_k<KK>(cb, scale_dtype, tw, su, sv, out, out_w_hat, tiles_k,
+                                      tiles_n, s)));
+  return rc;
 }

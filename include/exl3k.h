@@ -113,8 +113,8 @@ int exl3_backward_pass_ref_layout(const uint16_t* temp_costs,
 
 /*
  * Pack 16-bit states into the EXL3 container on the device:
- * states (n, 256) int16 -> packed (n, 16*K) int16 (pack_trellis + SWAP16,
- * trellis_format.py:120-174).
+ * states (n, 256) int16 (16-byte aligned) -> packed (n, 16*K) int16
+ * (4-byte aligned) (pack_trellis + SWAP16, trellis_format.py:120-174).
  */
 int exl3_pack_trellis(const int16_t* states, int16_t* packed, int64_t n, int K,
                       exl3_stream_t stream);
@@ -183,8 +183,9 @@ int exl3_ldlq_schedule(const exl3_ldlq_job* jobs, int njobs, int K, int buf,
 
 /*
  * Container words -> 16-bit states: trellis (ntiles, 16*K) int16 in SWAP16
- * storage order -> states (ntiles, 256) int16. Replaces
- * unpack_module_trellis (exl3_quant/serialization.py:65-84).
+ * storage order (4-byte aligned) -> states (ntiles, 256) int16 (16-byte
+ * aligned). Replaces unpack_module_trellis
+ * (exl3_quant/serialization.py:65-84).
  */
 int exl3_unpack_trellis(const int16_t* trellis, int16_t* states, int64_t ntiles, int K,
                         exl3_stream_t stream);

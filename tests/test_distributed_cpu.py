@@ -30,17 +30,18 @@ def _run(rank, ws, port, fn, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import datetime
 
-    dist.init_process_group("gloo", rank=rank, world_size=ws,
-                            timeout=datetime.timedelta(seconds=60))
     try:
+        dist.init_process_group("gloo", rank=rank, world_size=ws,
+                                timeout=datetime.timedelta(seconds=60))
         q.put((rank, fn(rank, ws)))
     except Exception as e:  # pragma: no cover - reported to the parent
         q.put((rank, e))
     finally:
-        dist.destroy_process_group()
+        if dist.is_initialized():
+            dist.destroy_process_group()
 
 
-def spawn(fn, ws=2):
+def _spawn_once(fn, ws):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -50,10 +51,23 @@ def spawn(fn, ws=2):
     out = dict(q.get(timeout=120) for _ in range(ws))
     for p in procs:
         p.join(timeout=60)
-    for r, v in out.items():
-        if isinstance(v, Exception):
-            raise v
     return out
+
+
+def spawn(fn, ws=2, attempts=2):
+    """Run fn(rank, ws) on ws gloo ranks; a rendezvous failure (the free port
+    taken by another process between probe and bind) is retried once on a
+    new port."""
+    for attempt in range(attempts):
+        out = _spawn_once(fn, ws)
+        errs = [v for v in out.values() if isinstance(v, Exception)]
+        if errs and attempt + 1 < attempts and any(
+                "address already in use" in str(e).lower() or "store" in str(e).lower()
+                for e in errs):
+            continue
+        for v in errs:
+            raise v
+        return out
 
 
 class GridEncoder:
