@@ -57,7 +57,7 @@ struct CGeo {
   static constexpr int NCH = E / CE;                 // chunks per thread
   static constexpr int NGC = ((CE >> K) > 0) ? (CE >> K) : 1;
   static constexpr int KB = Q < 8 ? Q : 8;
-  static constexpr int R = (K == 2) ? 2 : 1;         // checkpoint stride (as acs_pair.cu)
+  static constexpr int R = ck_stride(K);              // checkpoint stride (as acs_pair.cu)
   static constexpr int CKB = S * 4;
   static constexpr int NCB = E * Q / 2;              // codebook registers
   static constexpr size_t SMEM = (size_t)6 * SL * 4 + 256 * 4;  // 4 in + 2 own + weights

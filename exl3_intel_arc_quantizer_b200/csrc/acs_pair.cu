@@ -43,12 +43,10 @@ struct PGeo {
   static constexpr int NCH = E / CE;                    // chunks per step
   static constexpr int NGC = SPLIT ? 1 : (((CE >> K) > 0) ? (CE >> K) : 1);
   static constexpr int KB = QT < 8 ? QT : 8;            // branches per load batch
-  static constexpr int R = (K == 2) ? 2 : 1;           // checkpoint stride
+  static constexpr int R = ck_stride(K);               // checkpoint stride
   static constexpr int CKB = S * 4;                     // bytes per pair checkpoint
   static_assert(E * QT == 128, "codebook register budget: 128 values per thread");
 };
-
-__host__ __device__ constexpr int ck_stride(int K) { return K == 2 ? 2 : 1; }
 
 // Checkpointed steps. Pass 1 (roll L/2): steps half-1, half-1+R, ... <= L-2,
 // the ones the end-state traceback over [half, L) needs. Pass 2 (roll 0):
@@ -530,6 +528,116 @@ __device__ int ck_walk(const uint8_t* __restrict__ pck, int b, int cb, const uin
   return e;
 }
 
+// The pair walk without shared-memory levels. K >= 3 (a checkpoint every
+// step, one level): lane k loads the checkpoint cost of branch k's
+// predecessor and evaluates candidate k itself; its codebook value does not
+// depend on the load, so it is computed while the load is in flight.
+// K = 2 (a checkpoint every 2nd step; with L even every segment spans two
+// steps): the Q^2 level-2 nodes (costs at the checkpoint) are spread
+// over the lanes, node (kb << K) | j1 in register r of lane
+// ((kb << K) | j1) & 31; each lane evaluates branch kb of level-1 node j1
+// for its nodes, keeps the lowest key, and lanes holding the same j1 combine
+// by xor shuffles; the two path steps then read level-1 costs from lanes
+// 0..Q-1 and level-2 costs by shuffles. The candidate costs, the ordering
+// keys and the first-minimum rule are ck_walk's, so the path is the same.
+template <int K, int PASS>
+__device__ int ck_walk_reg(const uint8_t* __restrict__ pck, int b, int cb, const uint16_t* w,
+                           int L, int e_top, int pre, uint16_t* st, int lane) {
+  using G = PGeo<K>;
+  constexpr int R = G::R;
+  constexpr int Q = G::Q;
+  const int half = L / 2;
+  const int i_stop = PASS == 1 ? half : 0;
+  auto wt = [&](int s) { return w[PASS == 1 ? (s < half ? s + half : s - half) : s]; };
+  auto cost_of = [&](const uint32_t* ckb, int x) -> uint16_t {
+    return ckb ? (uint16_t)((__ldg(ckb + x) >> (16 * b)) & 0xFFFFu) : (uint16_t)0;
+  };
+  auto pick = [&](uint32_t bk) { return (bk == 0u || bk == 0xFFFFFFFFu) ? 0 : (int)(bk & 0xFFFFu); };
+  int i = L - 1, e = e_top;
+  while (i >= i_stop) {
+    int c, slot;
+    if (PASS == 1) {
+      const int rel = ((i - 1) - (half - 1)) / R;
+      c = (half - 1) + rel * R;
+      slot = rel;
+    } else {
+      c = (i / R) * R - 1;
+      slot = (c + 1) / R - 1;
+    }
+    const uint32_t* ckb =
+        c >= 0 ? reinterpret_cast<const uint32_t*>(pck + (size_t)slot * G::CKB) : nullptr;
+    if constexpr (R == 1) {
+      const uint16_t ws = wt(i);
+      const bool first = PASS == 2 && i == 0;
+      uint32_t bk = 0xFFFFFFFFu;
+#pragma unroll
+      for (int k = lane; k < Q; k += 32) {
+        const uint16_t prev = cost_of(ckb, (k << G::GB) | (e >> K));
+        const uint32_t key = cand_key(k, cand_cost<K>(cb, k, e, ws, prev, first, pre));
+        bk = key < bk ? key : bk;
+      }
+      const int k = pick(__reduce_min_sync(0xFFFFFFFFu, bk));
+      if (PASS == 2 && lane == 0) st[i] = (uint16_t)((k << G::Kr) | e);
+      e = (k << G::GB) | (e >> K);
+    } else {
+      static_assert(R == 2 && Q * Q <= 256, "two-level register walk: Q^2 <= 256");
+      constexpr int NPL = (Q * Q + 31) / 32;  // level-2 nodes per lane
+      const int s1 = i - 1;
+      const uint16_t ws1 = wt(s1);
+      uint16_t v2[NPL];
+      uint32_t key1 = 0xFFFFFFFFu, cost1 = 0;
+#pragma unroll
+      for (int r = 0; r < NPL; ++r) {
+        const int node = (lane + 32 * r) & (Q * Q - 1);
+        v2[r] = cost_of(ckb, (node << (G::Kr - 2 * K)) | (e >> (2 * K)));
+        const int j1 = node & (Q - 1), kb = node >> K;
+        const uint16_t cst = cand_cost<K>(cb, kb, (j1 << (G::Kr - K)) | (e >> K), ws1, v2[r],
+                                          PASS == 2 && s1 == 0, pre);
+        const uint32_t key = cand_key(kb, cst);
+        if (key < key1) {
+          key1 = key;
+          cost1 = cst;
+        }
+      }
+#pragma unroll
+      for (int h = Q; h < 32; h <<= 1) {  // lanes with the same j1 = lane & (Q-1)
+        const uint32_t ok = __shfl_xor_sync(0xFFFFFFFFu, key1, h);
+        const uint32_t oc = __shfl_xor_sync(0xFFFFFFFFu, cost1, h);
+        if (ok < key1) {
+          key1 = ok;
+          cost1 = oc;
+        }
+      }
+      // step i: branch k = lane < Q from level-1 node k (lane k holds it)
+      uint32_t bk = 0xFFFFFFFFu;
+      if (lane < Q)
+        bk = cand_key(lane, cand_cost<K>(cb, lane, e, wt(i), (uint16_t)cost1, PASS == 2 && i == 0,
+                                         pre));
+      const int k0 = pick(__reduce_min_sync(0xFFFFFFFFu, bk));
+      if (PASS == 2 && lane == 0) st[i] = (uint16_t)((k0 << G::Kr) | e);
+      e = (k0 << G::GB) | (e >> K);
+      if (s1 >= i_stop) {
+        // step i - 1: branch k from level-2 node (k << K) | k0
+        const int node = (((lane & (Q - 1)) << K) | k0);
+        uint16_t prev2 = 0;
+#pragma unroll
+        for (int r = 0; r < NPL; ++r) {
+          const uint16_t t = (uint16_t)__shfl_sync(0xFFFFFFFFu, (uint32_t)v2[r], node & 31);
+          if ((node >> 5) == r) prev2 = t;
+        }
+        uint32_t bk2 = 0xFFFFFFFFu;
+        if (lane < Q)
+          bk2 = cand_key(lane, cand_cost<K>(cb, lane, e, ws1, prev2, PASS == 2 && s1 == 0, pre));
+        const int k1 = pick(__reduce_min_sync(0xFFFFFFFFu, bk2));
+        if (PASS == 2 && lane == 0) st[s1] = (uint16_t)((k1 << G::Kr) | e);
+        e = (k1 << G::GB) | (e >> K);
+      }
+    }
+    i = c;
+  }
+  return e;
+}
+
 template <int K>
 __device__ __forceinline__ void tb_load_weights(const float* __restrict__ in, int tile, int L,
                                                 uint16_t* w, int lane) {
@@ -543,14 +651,13 @@ __global__ void __launch_bounds__(32 * kTbWarps)
 pair_tb1_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck, size_t ck_pair_bytes,
                 int n, int L, int cb, const int32_t* __restrict__ best_edge,
                 int32_t* __restrict__ end_state) {
-  __shared__ uint16_t vals[kTbWarps][kTbVals];
   __shared__ uint16_t w[kTbWarps][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x * kTbWarps + warp;
   if (tile >= n) return;
   tb_load_weights<K>(in, tile, L, w[warp], lane);
-  const int e = ck_walk<K, 1>(ck + (size_t)(tile >> 1) * ck_pair_bytes, tile & 1, cb, w[warp], L,
-                              best_edge[tile], -1, vals[warp], nullptr, lane);
+  const int e = ck_walk_reg<K, 1>(ck + (size_t)(tile >> 1) * ck_pair_bytes, tile & 1, cb, w[warp],
+                                  L, best_edge[tile], -1, nullptr, lane);
   if (lane == 0) end_state[tile] = e;
 }
 
@@ -560,7 +667,6 @@ pair_tb2_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck, si
                 int n, int L, int cb, const int32_t* __restrict__ end_state,
                 float* __restrict__ out_w, int16_t* __restrict__ out_idx,
                 int16_t* __restrict__ out_packed) {
-  __shared__ uint16_t vals[kTbWarps][kTbVals];
   __shared__ uint16_t w[kTbWarps][256];
   __shared__ uint16_t st[kTbWarps][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -568,8 +674,8 @@ pair_tb2_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck, si
   if (tile >= n) return;
   tb_load_weights<K>(in, tile, L, w[warp], lane);
   const int pre = end_state[tile];
-  ck_walk<K, 2>(ck + (size_t)(tile >> 1) * ck_pair_bytes, tile & 1, cb, w[warp], L, pre, pre,
-                vals[warp], st[warp], lane);
+  ck_walk_reg<K, 2>(ck + (size_t)(tile >> 1) * ck_pair_bytes, tile & 1, cb, w[warp], L, pre, pre,
+                    st[warp], lane);
   __syncwarp();
   for (int i = lane; i < L; i += 32) {
     const uint16_t s = st[warp][i];

@@ -111,8 +111,8 @@ class ScratchEstimator:
 
 def b200_checkpoint_stride(k: int) -> int:
     """Steps between cost checkpoints: the tile-pair encoder (K >= 2) every
-    2nd step at K=2 and every step above; the single-tile K=1 encoder every
-    4th step."""
+    2nd step at K=2 and every step above (``ck_stride``); the single-tile K=1
+    encoder every 4th step."""
     if not 1 <= k <= 8:
         raise ValueError(f"K must be in 1..8, got {k}")
     return 4 if k == 1 else (2 if k == 2 else 1)
