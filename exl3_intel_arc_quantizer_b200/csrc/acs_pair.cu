@@ -569,12 +569,21 @@ __device__ int ck_walk_reg(const uint8_t* __restrict__ pck, int b, int cb, const
     if constexpr (R == 1) {
       const uint16_t ws = wt(i);
       const bool first = PASS == 2 && i == 0;
+      constexpr int NPL = (Q + 31) / 32;  // branches per lane, all loads issued first
+      uint16_t prev[NPL];
+#pragma unroll
+      for (int r = 0; r < NPL; ++r) {
+        const int k = lane + 32 * r;
+        prev[r] = k < Q ? cost_of(ckb, (k << G::GB) | (e >> K)) : (uint16_t)0;
+      }
       uint32_t bk = 0xFFFFFFFFu;
 #pragma unroll
-      for (int k = lane; k < Q; k += 32) {
-        const uint16_t prev = cost_of(ckb, (k << G::GB) | (e >> K));
-        const uint32_t key = cand_key(k, cand_cost<K>(cb, k, e, ws, prev, first, pre));
-        bk = key < bk ? key : bk;
+      for (int r = 0; r < NPL; ++r) {
+        const int k = lane + 32 * r;
+        if (k < Q) {
+          const uint32_t key = cand_key(k, cand_cost<K>(cb, k, e, ws, prev[r], first, pre));
+          bk = key < bk ? key : bk;
+        }
       }
       const int k = pick(__reduce_min_sync(0xFFFFFFFFu, bk));
       if (PASS == 2 && lane == 0) st[i] = (uint16_t)((k << G::Kr) | e);
