@@ -9,6 +9,7 @@ until the scalar metrics are read.
 
 from __future__ import annotations
 
+import math
 import time
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Tuple
@@ -247,9 +248,8 @@ def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: i
             regs[nm].su.div_(g)
             regs[nm].g_scale = g
 
-    # one block-LDL per distinct Hessian (its factorization residual, a
-    # diagnostic fp32 GEMM, on one rank only when sharded)
-    ldls: List[list] = []               # [H, ldl, residual or rotated H]
+    # one block-LDL per distinct Hessian
+    ldls: List[list] = []               # [H, ldl, rotated H]
     ldl_of: Dict[str, int] = {}
     for nm in names:
         Hd = Hds[nm]
@@ -257,10 +257,38 @@ def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: i
                     if h.shape == Hd.shape and (h.data_ptr() == Hd.data_ptr() or torch.equal(h, Hd))),
                    None)
         if hit is None:
-            ldl, fr = _ldl_of(Hd, block_size, residual=group is None)
-            ldls.append([Hd, ldl, fr])
+            ldl, H_rot = _ldl_of(Hd, block_size, residual=False)
+            ldls.append([Hd, ldl, H_rot])
             hit = len(ldls) - 1
         ldl_of[nm] = hit
+
+    if group is None:
+        ws, rank = 1, 0
+    else:
+        import torch.distributed as dist
+
+        from .distributed import gather_column_slices, shard_range
+
+        ws, rank = dist.get_world_size(group), dist.get_rank(group)
+
+    # The diagnostics that need no quantized weight (each Hessian's
+    # factorization residual, each module's energy tr(W^T H W)) are fp32
+    # GEMMs; they run on a side stream while the LDLQ loop, whose launches
+    # leave most SMs idle, runs on the current one. With a group each rank
+    # computes column slices of every product and the sums are all-reduced.
+    main = torch.cuda.current_stream(device)
+    side = torch.cuda.Stream(device=device)
+    side.wait_stream(main)
+    res_parts, energy_parts = [], {}
+    with torch.cuda.stream(side):
+        for _h, ldl, H_rot in ldls:
+            for t in (H_rot, ldl.cholesky):
+                t.record_stream(side)
+            res_parts.append(_residual_parts(H_rot, ldl.cholesky, ws, rank))
+        for nm in names:
+            for t in (Ws[nm], Hds[nm]):
+                t.record_stream(side)
+            energy_parts[nm] = _energy_part(Hds[nm], Ws[nm], ws, rank)
 
     if group is None:
         jobs = [(regs[nm].weight, ldls[ldl_of[nm]][1].transformed) for nm in names]
@@ -268,11 +296,6 @@ def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: i
         wq = {nm: o.weight_q for nm, o in zip(names, outs)}
         enc = {nm: o.encoded for nm, o in zip(names, outs)}
     else:
-        from .distributed import gather_column_slices, shard_range
-
-        import torch.distributed as dist
-
-        ws, rank = dist.get_world_size(group), dist.get_rank(group)
         local = [nm for nm in names
                  if (lambda r: r[1] > r[0])(shard_range(Ws[nm].shape[1], ws, rank, 128))]
         jobs = []
@@ -287,38 +310,90 @@ def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: i
             wq[nm], enc[nm] = gather_column_slices(
                 o.weight_q if o is not None else None, o.encoded if o is not None else None,
                 k, n, group)
+    main.wait_stream(side)
+
+    w_hats = {nm: weight_from_quantized(wq[nm], regs[nm].su, regs[nm].sv) for nm in names}
     if group is None:
-        return {nm: _finish(nm, K, cb, Ws[nm], Hds[nm], regs[nm], ldls[ldl_of[nm]][1],
-                            ldls[ldl_of[nm]][2], wq[nm], enc[nm], t0) for nm in names}
+        # the arithmetic of compute_factorization_residual / _module_metrics
+        fres = [float(a.item() / max(1e-12, b.item())) for a, b in res_parts]
+        out = {}
+        for nm in names:
+            W, w_hat = Ws[nm], w_hats[nm]
+            diff = W - w_hat
+            mse = float(diff.pow(2).mean().item())
+            rel = float(torch.linalg.norm(diff).item() / max(1e-12, torch.linalg.norm(W).item()))
+            tile_dist = float((regs[nm].weight - wq[nm]).pow(2).mean().item())
+            proxy = float(((Hds[nm] @ diff) * diff).sum().item())
+            energy = max(1e-12, float(energy_parts[nm].item()))
+            out[nm] = _finish(nm, K, cb, W, Hds[nm], regs[nm], ldls[ldl_of[nm]][1],
+                              fres[ldl_of[nm]], wq[nm], enc[nm], t0, w_hat=w_hat,
+                              metric_values=(mse, rel, tile_dist, proxy, proxy / energy))
+        return out
 
-    # sharded: every rank reconstructs every module (the layer reload needs
-    # it); each module's metrics, and each distinct Hessian's factorization
-    # residual, run on one owner rank and reach the others through one
-    # all-reduce of the scalars
-    from .distributed import assign_modules
+    # sharded: partial sums over this rank's column slice of every module,
+    # fp64, one all-reduce; every rank ends with every module's metrics
+    parts = torch.zeros((len(names) * 5 + len(ldls) * 2,), dtype=torch.float64, device=device)
+    for idx, nm in enumerate(names):
+        k, n = Ws[nm].shape
+        c0, c1 = shard_range(n, ws, rank, 128)
+        p = parts[5 * idx:5 * idx + 5]
+        p[4] = energy_parts[nm]
+        if c1 > c0:
+            W = Ws[nm][:, c0:c1]
+            d = W - w_hats[nm][:, c0:c1]
+            p[0] = d.double().pow(2).sum()
+            p[1] = W.double().pow(2).sum()
+            p[2] = (regs[nm].weight[:, c0:c1] - wq[nm][:, c0:c1]).double().pow(2).sum()
+            p[3] = ((Hds[nm] @ d) * d).double().sum()
+    base = len(names) * 5
+    for li, (a, b) in enumerate(res_parts):
+        parts[base + 2 * li] = a
+        parts[base + 2 * li + 1] = b
+    dist.all_reduce(parts, group=group)
+    v = parts.tolist()
+    fres = [math.sqrt(v[base + 2 * li]) / max(1e-12, math.sqrt(v[base + 2 * li + 1]))
+            for li in range(len(ldls))]
+    out = {}
+    for idx, nm in enumerate(names):
+        k, n = Ws[nm].shape
+        sd, sw, st, proxy, energy = v[5 * idx:5 * idx + 5]
+        metric = (sd / (k * n), math.sqrt(sd) / max(1e-12, math.sqrt(sw)), st / (k * n), proxy,
+                  proxy / max(1e-12, energy))
+        out[nm] = _finish(nm, K, cb, Ws[nm], Hds[nm], regs[nm], ldls[ldl_of[nm]][1],
+                          fres[ldl_of[nm]], wq[nm], enc[nm], t0, w_hat=w_hats[nm],
+                          metric_values=metric)
+    return out
 
-    owner = assign_modules({nm: tuple(Ws[nm].shape) for nm in names}, ws)
-    first_of = {}                       # ldl entry -> index of its first module
-    for idx, nm in enumerate(names):
-        first_of.setdefault(ldl_of[nm], idx)
-    vec = torch.zeros((len(names), 6), dtype=torch.float64, device=Ws[names[0]].device)
-    w_hats = {}
-    for idx, nm in enumerate(names):
-        w_hats[nm] = weight_from_quantized(wq[nm], regs[nm].su, regs[nm].sv)
-        if owner[nm] != rank:
-            continue
-        vals = _module_metrics(Ws[nm], Hds[nm], regs[nm], wq[nm], w_hats[nm])
-        fr = 0.0
-        if first_of[ldl_of[nm]] == idx:
-            _h, ldl, H_rot = ldls[ldl_of[nm]]
-            fr = compute_factorization_residual(H_rot, ldl.cholesky)
-        vec[idx] = torch.tensor(vals + (fr,), dtype=torch.float64, device=vec.device)
-    dist.all_reduce(vec, group=group)
-    rows = vec.tolist()
-    return {nm: _finish(nm, K, cb, Ws[nm], Hds[nm], regs[nm], ldls[ldl_of[nm]][1],
-                        rows[first_of[ldl_of[nm]]][5], wq[nm], enc[nm], t0, w_hat=w_hats[nm],
-                        metric_values=tuple(rows[idx][:5]))
-            for idx, nm in enumerate(names)}
+
+def _residual_parts(H_rot: torch.Tensor, chol: torch.Tensor, ws: int, rank: int):
+    """Numerator and denominator of ||H - L L^T||_F / ||H||_F. One rank: the
+    two fp32 norms of compute_factorization_residual; several: the fp64
+    sums of squares over this rank's 16-aligned column slice."""
+    if ws == 1:
+        return torch.linalg.norm(H_rot - chol @ chol.T), torch.linalg.norm(H_rot)
+    from .distributed import shard_range
+
+    k = H_rot.shape[0]
+    c0, c1 = shard_range(k, ws, rank, 16)
+    if c1 <= c0:
+        z = torch.zeros((), dtype=torch.float64, device=H_rot.device)
+        return z, z.clone()
+    d = H_rot[:, c0:c1] - chol @ chol[c0:c1].T
+    return d.double().pow(2).sum(), H_rot[:, c0:c1].double().pow(2).sum()
+
+
+def _energy_part(H: torch.Tensor, W: torch.Tensor, ws: int, rank: int) -> torch.Tensor:
+    """tr(W^T H W) (compute_proxy_loss's normalizer): whole on one rank,
+    the fp64 sum over this rank's LDLQ column slice on several."""
+    if ws == 1:
+        return ((H @ W) * W).sum()
+    from .distributed import shard_range
+
+    c0, c1 = shard_range(W.shape[1], ws, rank, 128)
+    if c1 <= c0:
+        return torch.zeros((), dtype=torch.float64, device=W.device)
+    Wc = W[:, c0:c1]
+    return ((H @ Wc) * Wc).double().sum()
 
 
 def quantize_decoder_layer(layer: nn.Module, hessians: Dict[str, torch.Tensor], K: int = 2,

@@ -10,8 +10,10 @@ with fewer than 2 GPUs.
 * module-sharded layer quantization: every rank ends with every module's
   result, bit-identical to what its owner computed;
 * column-sharded batched modules: each module's metrics (and each distinct
-  Hessian's factorization residual), computed on one owner rank and
-  all-reduced, match what any rank recomputes from its gathered result.
+  Hessian's factorization residual), summed over every rank's column slice
+  and all-reduced, match what any rank recomputes whole from its gathered
+  result (rtol 1e-4: fp64 partial sums against fp32 whole-matrix
+  reductions; the residual, itself a rounding-error measure, within 2x).
 """
 
 from __future__ import annotations
@@ -93,8 +95,8 @@ def _worker(rank, ws, port, q):
                 local[m] = float(torch.linalg.norm(r.result.w_hat - r.w_hat))
         out.update(owners=own, digest=digest, local=local)
 
-        # 4. column-sharded batched modules: metrics computed on one owner
-        #    rank and all-reduced equal the ones every rank can recompute
+        # 4. column-sharded batched modules: metrics summed over the ranks'
+        #    column slices equal the ones every rank can recompute whole
         from exl3_intel_arc_quantizer_b200.layer_quant import (
             _ldl_of, _module_metrics, quantize_modules)
 
@@ -144,5 +146,9 @@ def test_two_gpu_sharded_paths():
     assert a["mod_metrics"] == b["mod_metrics"]
     for r in (a, b):
         for m, vals in r["mod_metrics"].items():
-            for got, want in zip(vals, r["mod_again"][m]):
-                assert abs(got - want) <= 1e-6 * max(abs(want), 1e-12), (m, vals, r["mod_again"][m])
+            again = r["mod_again"][m]
+            for got, want in zip(vals[:5], again[:5]):
+                assert abs(got - want) <= 1e-4 * max(abs(want), 1e-12), (m, vals, again)
+            # the factorization residual measures fp32 rounding of L L^T itself,
+            # so a column-sliced product only has to agree in size
+            assert vals[5] <= 1e-5 and again[5] <= 1e-5 and 0.5 <= vals[5] / again[5] <= 2.0
