@@ -69,7 +69,7 @@ def parse():
                     help="time one encoder call of --tiles tiles at --K (latency of an LDLQ "
                          "step) with --cluster CTAs per tile pair and exit")
     ap.add_argument("--cluster", type=int, default=0,
-                    help="encoder cluster split: 0 automatic, 1 off, 2/4/8 forced")
+                    help="encoder cluster split for every mode: 0 automatic, 1 off, 2/4/8 forced")
     return ap.parse_args()
 
 
@@ -604,6 +604,10 @@ def run_b200(args):
     from exl3_intel_arc_quantizer_b200.xpu_quantizer import ScratchArena, XPUTrellisEncoder
 
     K, n = args.K, args.tiles
+    if args.cluster:
+        from exl3_intel_arc_quantizer_b200._ext import set_encoder_cluster
+
+        set_encoder_cluster(args.cluster)   # encoder cluster split for every mode below
     if args.model_only:
         out = {"model": run_model(device, world, rank, K=4, nlayers=args.model_layers)}
         if rank == 0:

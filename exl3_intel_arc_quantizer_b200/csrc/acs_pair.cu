@@ -725,20 +725,43 @@ int pair_encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t*
   for (int64_t start = 0; start < n; start += cap) {
     const int m = (int)((n - start) < cap ? (n - start) : cap);
     const int pairs = (m + 1) / 2;
-    const int grid = pairs < sms ? pairs : sms;
     const float* cin = in + start * L;
     const int tb_grid = (m + kTbWarps - 1) / kTbWarps;
+    // few pairs: every pair split over a cluster; more than one wave: whole
+    // waves one pair per CTA, and the last partial wave, if it is small
+    // enough, split over clusters (it would otherwise leave most SMs idle
+    // for a whole wave)
     const int csize = cluster_size_for(K, pairs);
-    if (csize > 1) {
-      LaunchTimer lt(stream, 0);
-      const int rc = cluster_acs_pass(K, csize, 1, stream, cin, m, L, cb, ck, ck_pair, best_edge,
-                                      nullptr, nullptr);
-      if (rc) return rc;
-    } else {
-      LaunchTimer lt(stream, 0);
-      acs_pair_kernel<K, 1><<<grid, kPairNT, PSmem<K>::bytes, stream>>>(
-          cin, m, L, cb, ck, ck_pair, best_edge, nullptr, nullptr);
+    int bulk = pairs, tail = 0, tail_c = 1;
+    if (csize == 1 && pairs > sms && pairs % sms) {
+      tail_c = cluster_size_for(K, pairs % sms);
+      if (tail_c > 1) {
+        tail = pairs % sms;
+        bulk = pairs - tail;
+      }
     }
+    const int mb = 2 * bulk < m ? 2 * bulk : m;  // tiles of the whole waves
+    auto acs_pass = [&](int pass) -> int {
+      LaunchTimer lt(stream, 0);
+      int32_t* be = pass == 1 ? best_edge : nullptr;
+      const int32_t* es = pass == 2 ? end_state : nullptr;
+      float* pc = (pass == 2 && out_cost) ? out_cost + start : nullptr;
+      if (csize > 1) return cluster_acs_pass(K, csize, pass, stream, cin, m, L, cb, ck, ck_pair, be,
+                                              es, pc);
+      const int g = bulk < sms ? bulk : sms;
+      if (pass == 1)
+        acs_pair_kernel<K, 1><<<g, kPairNT, PSmem<K>::bytes, stream>>>(cin, mb, L, cb, ck, ck_pair,
+                                                                      be, es, pc);
+      else
+        acs_pair_kernel<K, 2><<<g, kPairNT, PSmem<K>::bytes, stream>>>(cin, mb, L, cb, ck, ck_pair,
+                                                                      be, es, pc);
+      EXL3_LAUNCHED();
+      if (!tail) return EXL3_OK;
+      return cluster_acs_pass(K, tail_c, pass, stream, cin + (size_t)mb * L, m - mb, L, cb,
+                              ck + (size_t)bulk * ck_pair, ck_pair, be ? be + mb : nullptr,
+                              es ? es + mb : nullptr, pc ? pc + mb : nullptr);
+    };
+    if (int rc = acs_pass(1)) return rc;
     EXL3_LAUNCHED();
     {
       LaunchTimer lt(stream, 1);
@@ -746,16 +769,7 @@ int pair_encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t*
                                                                 best_edge, end_state);
     }
     EXL3_LAUNCHED();
-    if (csize > 1) {
-      LaunchTimer lt(stream, 0);
-      const int rc = cluster_acs_pass(K, csize, 2, stream, cin, m, L, cb, ck, ck_pair, nullptr,
-                                      end_state, out_cost ? out_cost + start : nullptr);
-      if (rc) return rc;
-    } else {
-      LaunchTimer lt(stream, 0);
-      acs_pair_kernel<K, 2><<<grid, kPairNT, PSmem<K>::bytes, stream>>>(
-          cin, m, L, cb, ck, ck_pair, nullptr, end_state, out_cost ? out_cost + start : nullptr);
-    }
+    if (int rc = acs_pass(2)) return rc;
     EXL3_LAUNCHED();
     {
       LaunchTimer lt(stream, 1);

@@ -131,3 +131,19 @@ def test_cluster_capacity_and_policy_validation():
         set_encoder_cluster(3)
     with pytest.raises(RuntimeError):
         encoder_cluster_capacity(2, 16)
+
+
+@pytest.mark.parametrize("K", [2, 4])
+def test_last_partial_wave_split_matches_off(K):
+    """More pairs than SMs with a small remainder: the whole waves run one
+    pair per CTA and the last 11 pairs (one of them a lone tile) over
+    clusters; identical to running everything one pair per CTA."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    n = 2 * (sms + 10) + 1
+    tiles = _tiles(n, 7600 + K)
+    off = _encode(K, tf.CB_MUL1, tiles, 1)
+    auto = _encode(K, tf.CB_MUL1, tiles, 0)
+    for a, b, what in zip(auto, off, ("indices", "packed", "cost", "recon")):
+        np.testing.assert_array_equal(a, b, err_msg=what)
+    ref = COracle(K, tf.CB_MUL1).encode_batch(tiles[-24:])   # the tail pairs, checked whole
+    np.testing.assert_array_equal(auto[0][-24:], ref["indices"])
