@@ -207,13 +207,21 @@ def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: i
     * the global-scale searches of all modules run as one batched search
       (every candidate tile of every module in shared encoder launches);
     * one block-LDL per distinct Hessian (q/k/v share one, gate/up share one);
-    * one interleaved LDLQ: each step encodes the current 16-row block of
-      every module in a single launch (``ldlq.ldlq_batched``).
+    * one LDLQ over all modules: each step encodes the current 16-row block
+      of every active module in a single launch (``ldlq.ldlq_native``; the
+      longest module runs throughout, the others start where
+      ``ldlq.ldlq_schedule`` places them; ``ldlq.ldlq_batched`` for other
+      encoders);
+    * the diagnostics that need no quantized weight (factorization
+      residuals, the proxy-loss normalizers) run on a side stream while the
+      LDLQ loop runs.
 
     With a process ``group`` (``torch.distributed``), every module's
     128-aligned column slices are dealt over the ranks, each rank runs the
-    interleaved LDLQ on its slices, and one all-gather per module rebuilds
-    the full result on every rank (column slices never interact in LDLQ).
+    LDLQ on its slices, and one all-gather per module rebuilds the full
+    result on every rank (column slices never interact in LDLQ). The metrics
+    are then sums over every rank's column slices (fp64 partial sums, one
+    all-reduce), so every rank ends with the same metrics.
     """
     t0 = time.time()
     if not modules:
