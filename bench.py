@@ -394,6 +394,48 @@ def run_storage(device, K=4, shapes=((4096, 4096), (12288, 4096)), reps=5):
             "peak_source": "MEASURED_PEAKS.json hbm_gbs (copy)" if peaks else "fallback 6650"}
 
 
+def run_layer_sharded(device, world, rank, K=4, reps=2):
+    """Config 3 on several GPUs: the 4096x4096 layer's calibration tokens
+    sharded over the ranks (tensor-core X^T X of each shard, one NCCL
+    all-reduce, finalize), then quantize_modules with the process group
+    (column slices of the LDLQ per rank, one all-gather). Seconds are the
+    max over ranks of the best repetition after a warm-up."""
+    import torch
+    import torch.distributed as dist
+
+    from exl3_intel_arc_quantizer_b200.calibration import hessian_accumulate_, hessian_finalize_
+    from exl3_intel_arc_quantizer_b200.distributed import shard_range
+    from exl3_intel_arc_quantizer_b200.layer_quant import quantize_modules
+    from exl3_intel_arc_quantizer_b200.ldlq import make_xpu_tile_encoder
+
+    W, X = layer_config3(device)
+    t0, t1 = shard_range(X.shape[0], world, rank, 64)
+    Xs = X[t0:t1].contiguous()
+    enc = make_xpu_tile_encoder(K=K, device_index=device.index or 0)
+    best, rel = None, None
+    for rep in range(reps + 1):
+        dist.barrier()
+        torch.cuda.synchronize()
+        a = time.perf_counter()
+        H = torch.zeros(4096, 4096, dtype=torch.float32, device=device)
+        hessian_accumulate_(H, Xs)
+        dist.all_reduce(H)
+        hessian_finalize_(H, X.shape[0], 0.01, 1e-7)
+        res = quantize_modules({"o_proj": (W, H)}, K=K, tile_encoder=enc, skip_g_scale=True,
+                               buf_size_k=128, block_size=16, group=dist.group.WORLD)
+        torch.cuda.synchronize()
+        t = torch.tensor([time.perf_counter() - a], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        if rep > 0:
+            best = float(t.item()) if best is None else min(best, float(t.item()))
+        rel = res["o_proj"].metrics.relative_frobenius_error
+    enc.encoder.arena.release()
+    return {"workload": f"config 3: 4096x4096 bf16 layer, K={K}, Hessian from 2048x4096 bf16 "
+                        f"(tokens sharded), skip_g_scale, LDLQ columns over {world} GPUs",
+            "seconds_per_layer": best, "tiles": 65536, "K": K, "n_gpus": world,
+            "relative_frobenius_error": rel}
+
+
 def run_small_calls(device, Ks=(2, 4), sizes=(2, 16, 30, 32, 64), reps=10):
     """Latency of one encoder call of a few tiles (an LDLQ step of a
     column-sharded module), with the cluster-split ACS (automatic choice)
@@ -659,6 +701,13 @@ def run_b200(args):
                 set_encoder_cluster(0)
         return 0
     if args.layer_only:
+        if world > 1:
+            out = {"layer_sharded": run_layer_sharded(device, world, rank)}
+            if rank == 0:
+                print(json.dumps(out), flush=True)
+            dist.barrier()
+            dist.destroy_process_group()
+            return 0
         if rank == 0:
             print(json.dumps({"layer": run_layer(device),
                               "layer_k2_gss": run_layer(device, K=2, skip_g_scale=False)}),
@@ -824,6 +873,9 @@ def run_b200(args):
         layer2 = run_layer(device, K=2, skip_g_scale=False)
     if world > 1:
         dist.barrier()
+    layer_sh = None
+    if world > 1 and not args.no_layer:
+        layer_sh = run_layer_sharded(device, world, rank)
     declayer = None
     if not args.no_decoder_layer:
         declayer = [run_decoder_layer(device, world, rank, k) for k in (2, 4)]
@@ -845,6 +897,7 @@ def run_b200(args):
             "k_sweep_tiles_per_s": ksweep,
             "layer": layer,
             "layer_k2_gss": layer2,
+            "layer_sharded": layer_sh,
             "decoder_layer": declayer,
             "small_calls": small,
             "storage": storage,
