@@ -799,13 +799,33 @@ def run_b200(args):
         d_p = torch.empty((n, 16 * K), dtype=torch.int16, device=device)
         ws, per, adm = enc.arena.acquire(K, 256, args.chunk)
         e = ext()
+        # chunks of the workspace's size go through three streams: pinned
+        # host -> device copies, the encoder (op binding, current stream),
+        # device -> pinned host copies; per chunk, events order each stage
+        # after the one before and after the previous step's use of the buffers
+        comp = torch.cuda.current_stream(device)
+        s_in, s_out = torch.cuda.Stream(device=device), torch.cuda.Stream(device=device)
+        chunks = [(c, min(c + args.chunk, n)) for c in range(0, n, args.chunk)]
+        ev_in = [torch.cuda.Event() for _ in chunks]
+        ev_c = [torch.cuda.Event() for _ in chunks]
+        ev_out = [torch.cuda.Event() for _ in chunks]
 
         def one():
-            d_in.copy_(host_in, non_blocking=True)
-            e.encode_tiles(d_in, d_w, d_i, d_p, None, ws, K, 2)
-            h_w.copy_(d_w, non_blocking=True)
-            h_i.copy_(d_i, non_blocking=True)
-            h_p.copy_(d_p, non_blocking=True)
+            for q, (a, b) in enumerate(chunks):
+                s_in.wait_event(ev_c[q])        # the last step's encode has read d_in[a:b]
+                with torch.cuda.stream(s_in):
+                    d_in[a:b].copy_(host_in[a:b], non_blocking=True)
+                    ev_in[q].record(s_in)
+                comp.wait_event(ev_in[q])
+                comp.wait_event(ev_out[q])      # the last step's outputs have left
+                e.encode_tiles(d_in[a:b], d_w[a:b], d_i[a:b], d_p[a:b], None, ws, K, 2)
+                ev_c[q].record(comp)
+                s_out.wait_event(ev_c[q])
+                with torch.cuda.stream(s_out):
+                    h_w[a:b].copy_(d_w[a:b], non_blocking=True)
+                    h_i[a:b].copy_(d_i[a:b], non_blocking=True)
+                    h_p[a:b].copy_(d_p[a:b], non_blocking=True)
+                    ev_out[q].record(s_out)
 
         for _ in range(2):
             one()
@@ -813,10 +833,13 @@ def run_b200(args):
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
+        e0.record(comp)
+        s_in.wait_event(e0)
         for _ in range(args.steps):
             one()
-        e1.record()
+        for ev in ev_out:
+            comp.wait_event(ev)
+        e1.record(comp)
         e1.synchronize()
         t_e2e = e0.elapsed_time(e1)
         if world > 1:
