@@ -392,8 +392,6 @@ acs_pair_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* __r
 // Traceback from checkpoints (one warp per tile)
 // ---------------------------------------------------------------------------
 
-constexpr int kTbVals = 256;  // per-warp ancestor costs (at most Q + Q^2 + ... <= 256)
-
 __device__ __forceinline__ uint16_t h_sub(uint16_t a, uint16_t b) {
   uint16_t r;
   asm("sub.rn.f16 %0, %1, %2;" : "=h"(r) : "h"(a), "h"(b));
@@ -429,104 +427,7 @@ __device__ __forceinline__ uint16_t cand_cost(int cb, int k, int x, uint16_t w, 
   return c;
 }
 
-// Checkpoint geometry of the traceback: pair checkpoints hold {cost_A,
-// cost_B} words (stride PGeo<K>::R); the single-tile K=1 encoder's hold one
-// fp16 cost per edge every kSingleR steps.
-constexpr int kSingleR = 4;
-
-template <int K, bool SINGLE>
-struct WGeo {
-  static constexpr int R = SINGLE ? kSingleR : PGeo<K>::R;
-  static constexpr int CKB = SINGLE ? PGeo<K>::S * 2 : PGeo<K>::CKB;
-};
-
-// Walk the path back from `e_top` at step `i_top` down to step `i_stop`
-// (inclusive) for lane b of a pair (or the one tile of a single-tile
-// checkpoint set). PASS 1: roll L/2, first checkpoint at half-1, returns the
-// edge before step i_stop (the end state). PASS 2: roll 0, constrained start
-// `pre`, writes each step's state to st[].
-template <int K, int PASS, bool SINGLE = false>
-__device__ int ck_walk(const uint8_t* __restrict__ pck, int b, int cb, const uint16_t* w,
-                       int L, int e_top, int pre, uint16_t* vals, uint16_t* st, int lane) {
-  using G = PGeo<K>;
-  using W = WGeo<K, SINGLE>;
-  const int half = L / 2;
-  const int i_stop = PASS == 1 ? half : 0;
-  int i = L - 1, e = e_top;
-  while (i >= i_stop) {
-    // nearest checkpoint c <= i - 1 (c = -1: the all-zero start of pass 2)
-    int c, slot;
-    if (PASS == 1) {
-      const int rel = ((i - 1) - (half - 1)) / W::R;
-      c = (half - 1) + rel * W::R;
-      slot = rel;
-    } else {
-      c = (i / W::R) * W::R - 1;
-      slot = (c + 1) / W::R - 1;
-    }
-    const int D = i - 1 - c;  // levels recomputed above the checkpoint
-    const int Lv = D + 1;     // level of the checkpoint (step i - Lv == c)
-    // level m holds the costs after step i - m at the Q^m ancestors of e at
-    // depth m: node j <-> edge (j << (Kr - m*K)) | (e >> (m*K)); levels are
-    // packed one after another (level m starts at Q + Q^2 + ... + Q^(m-1))
-    auto off = [](int m) { return ((1 << (m * K)) - (1 << K)) / ((1 << K) - 1); };
-    const int nL = 1 << (Lv * K);
-    const uint8_t* ckb = c >= 0 ? pck + (size_t)slot * W::CKB : nullptr;
-    for (int j = lane; j < nL; j += 32) {
-      uint16_t v = 0;
-      if (ckb) {
-        const int x = (j << (G::Kr - Lv * K)) | (e >> (Lv * K));
-        if (SINGLE)
-          v = reinterpret_cast<const uint16_t*>(ckb)[x];
-        else
-          v = (uint16_t)((reinterpret_cast<const uint32_t*>(ckb)[x] >> (16 * b)) & 0xFFFFu);
-      }
-      vals[off(Lv) + j] = v;
-    }
-    __syncwarp();
-    for (int m = Lv - 1; m >= 1; --m) {
-      const int s = i - m;
-      const uint16_t ws = w[PASS == 1 ? (s < half ? s + half : s - half) : s];
-      const int nm = 1 << (m * K);
-      for (int j = lane; j < nm; j += 32) {
-        const int x = (j << (G::Kr - m * K)) | (e >> (m * K));
-        uint32_t bk = 0xFFFFFFFFu;
-        uint16_t bv = 0;
-        for (int k = 0; k < G::Q; ++k) {
-          const uint16_t prev = vals[off(m + 1) + ((k << (m * K)) | j)];
-          const uint16_t cst = cand_cost<K>(cb, k, x, ws, prev, PASS == 2 && s == 0, pre);
-          const uint32_t key = cand_key(k, cst);
-          if (key < bk) {
-            bk = key;
-            bv = cst;
-          }
-        }
-        vals[off(m) + j] = bv;
-      }
-      __syncwarp();
-    }
-    // the path through this segment: steps i .. c+1 (not below i_stop)
-    int j = 0;
-    for (int tt = 0; tt <= D && i - tt >= i_stop; ++tt) {
-      const int s = i - tt;
-      const uint16_t ws = w[PASS == 1 ? (s < half ? s + half : s - half) : s];
-      uint32_t bk = 0xFFFFFFFFu;
-      for (int k = lane; k < G::Q; k += 32) {
-        const uint16_t prev = vals[off(tt + 1) + ((k << (tt * K)) | j)];
-        const uint32_t key = cand_key(k, cand_cost<K>(cb, k, e, ws, prev, PASS == 2 && s == 0, pre));
-        bk = key < bk ? key : bk;
-      }
-      bk = __reduce_min_sync(0xFFFFFFFFu, bk);
-      const int k = (bk == 0u || bk == 0xFFFFFFFFu) ? 0 : (int)(bk & 0xFFFFu);
-      if (PASS == 2 && lane == 0) st[s] = (uint16_t)((k << G::Kr) | e);
-      j |= k << (tt * K);
-      e = (k << G::GB) | (e >> K);
-    }
-    __syncwarp();
-    i = c;
-  }
-  return e;
-}
+constexpr int kSingleR = 4;  // the single-tile K=1 encoder checkpoints every 4th step
 
 // The pair walk without shared-memory levels. K >= 3 (a checkpoint every
 // step, one level): lane k loads the checkpoint cost of branch k's
@@ -539,7 +440,8 @@ __device__ int ck_walk(const uint8_t* __restrict__ pck, int b, int cb, const uin
 // for its nodes, keeps the lowest key, and lanes holding the same j1 combine
 // by xor shuffles; the two path steps then read level-1 costs from lanes
 // 0..Q-1 and level-2 costs by shuffles. The candidate costs, the ordering
-// keys and the first-minimum rule are ck_walk's, so the path is the same.
+// keys (cand_key) and the first-minimum rule are those of the forward pass,
+// so the path is the one a tracked forward pass would record.
 template <int K, int PASS>
 __device__ int ck_walk_reg(const uint8_t* __restrict__ pck, int b, int cb, const uint16_t* w,
                            int L, int e_top, int pre, uint16_t* st, int lane) {
@@ -641,6 +543,83 @@ __device__ int ck_walk_reg(const uint8_t* __restrict__ pck, int b, int cb, const
         if (PASS == 2 && lane == 0) st[s1] = (uint16_t)((k1 << G::Kr) | e);
         e = (k1 << G::GB) | (e >> K);
       }
+    }
+    i = c;
+  }
+  return e;
+}
+
+// The K = 1 single-tile walk in registers (checkpoints hold one fp16 cost
+// per edge every kSingleR = 4 steps; with L a multiple of 4 every segment
+// spans four steps). Lane j < 16 loads level-4 node j (the 16 ancestors of
+// the path edge four steps up); level m < 4 node j lives in every lane with
+// lane & (2^m - 1) == j: such a lane evaluates branch k = (lane >> m) & 1
+// from its own level-(m+1) cost and the two branches meet by one xor
+// shuffle. The path steps read the level costs back by shuffles. Costs,
+// keys (cand_key) and the first-minimum rule are the forward pass's.
+template <int PASS>
+__device__ int ck_walk_single_reg(const uint8_t* __restrict__ pck, int cb, const uint16_t* w,
+                                  int L, int e_top, int pre, uint16_t* st, int lane) {
+  using G = PGeo<1>;
+  constexpr int R = kSingleR;
+  constexpr int CKB = G::S * 2;
+  const int half = L / 2;
+  const int i_stop = PASS == 1 ? half : 0;
+  auto wt = [&](int s) { return w[PASS == 1 ? (s < half ? s + half : s - half) : s]; };
+  auto pick = [&](uint32_t bk) { return (bk == 0u || bk == 0xFFFFFFFFu) ? 0 : (int)(bk & 0xFFFFu); };
+  int i = L - 1, e = e_top;
+  while (i >= i_stop) {
+    int c, slot;
+    if (PASS == 1) {
+      const int rel = ((i - 1) - (half - 1)) / R;
+      c = (half - 1) + rel * R;
+      slot = rel;
+    } else {
+      c = (i / R) * R - 1;
+      slot = (c + 1) / R - 1;
+    }
+    const int Lv = i - c;  // 4
+    const uint16_t* ckb =
+        c >= 0 ? reinterpret_cast<const uint16_t*>(pck + (size_t)slot * CKB) : nullptr;
+    uint32_t cost[5];  // cost[m]: this lane's level-m node
+    {
+      const int node = lane & ((1 << Lv) - 1);
+      cost[4] = ckb ? (uint32_t)__ldg(ckb + ((node << (G::Kr - Lv)) | (e >> Lv))) : 0u;
+    }
+#pragma unroll
+    for (int m = 3; m >= 1; --m) {
+      if (m >= Lv) {
+        cost[m] = cost[m + 1];  // levels above the segment's top are not used
+        continue;
+      }
+      const int j = lane & ((1 << m) - 1), kb = (lane >> m) & 1;
+      const int s = i - m;
+      const uint16_t cst = cand_cost<1>(cb, kb, (j << (G::Kr - m)) | (e >> m), wt(s),
+                                        (uint16_t)cost[m + 1], PASS == 2 && s == 0, pre);
+      uint32_t key = cand_key(kb, cst), cv = cst;
+      const uint32_t ok = __shfl_xor_sync(0xFFFFFFFFu, key, 1 << m);
+      const uint32_t oc = __shfl_xor_sync(0xFFFFFFFFu, cv, 1 << m);
+      if (ok < key) {
+        key = ok;
+        cv = oc;
+      }
+      cost[m] = cv;
+    }
+    // the path: steps i .. c+1; step i - tt reads level tt+1 node (k << tt) | j
+    int j = 0;
+#pragma unroll
+    for (int tt = 0; tt < 4; ++tt) {
+      if (tt >= Lv || i - tt < i_stop) break;
+      const int s = i - tt;
+      const int src = (((lane & 1) << tt) | j) & 31;
+      const uint16_t prev = (uint16_t)__shfl_sync(0xFFFFFFFFu, cost[tt + 1], src);
+      uint32_t bk = 0xFFFFFFFFu;
+      if (lane < 2)
+        bk = cand_key(lane, cand_cost<1>(cb, lane, e, wt(s), prev, PASS == 2 && s == 0, pre));
+      const int k = pick(__reduce_min_sync(0xFFFFFFFFu, bk));
+      if (PASS == 2 && lane == 0) st[s] = (uint16_t)((k << G::Kr) | e);
+      j |= k << tt;
+      e = (k << G::GB) | (e >> 1);
     }
     i = c;
   }
@@ -987,14 +966,13 @@ __global__ void __launch_bounds__(32 * kTbWarps)
 single_tb1_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck,
                   size_t ck_tile_bytes, int n, int L, int cb,
                   const int32_t* __restrict__ best_edge, int32_t* __restrict__ end_state) {
-  __shared__ uint16_t vals[kTbWarps][kTbVals];
   __shared__ uint16_t w[kTbWarps][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x * kTbWarps + warp;
   if (tile >= n) return;
   tb_load_weights<1>(in, tile, L, w[warp], lane);
-  const int e = ck_walk<1, 1, true>(ck + (size_t)tile * ck_tile_bytes, 0, cb, w[warp], L,
-                                    best_edge[tile], -1, vals[warp], nullptr, lane);
+  const int e = ck_walk_single_reg<1>(ck + (size_t)tile * ck_tile_bytes, cb, w[warp], L,
+                                      best_edge[tile], -1, nullptr, lane);
   if (lane == 0) end_state[tile] = e;
 }
 
@@ -1003,7 +981,6 @@ single_tb2_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck,
                   size_t ck_tile_bytes, int n, int L, int cb,
                   const int32_t* __restrict__ end_state, float* __restrict__ out_w,
                   int16_t* __restrict__ out_idx, int16_t* __restrict__ out_packed) {
-  __shared__ uint16_t vals[kTbWarps][kTbVals];
   __shared__ uint16_t w[kTbWarps][256];
   __shared__ uint16_t st[kTbWarps][256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1011,8 +988,8 @@ single_tb2_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck,
   if (tile >= n) return;
   tb_load_weights<1>(in, tile, L, w[warp], lane);
   const int pre = end_state[tile];
-  ck_walk<1, 2, true>(ck + (size_t)tile * ck_tile_bytes, 0, cb, w[warp], L, pre, pre,
-                      vals[warp], st[warp], lane);
+  ck_walk_single_reg<2>(ck + (size_t)tile * ck_tile_bytes, cb, w[warp], L, pre, pre, st[warp],
+                        lane);
   __syncwarp();
   for (int i = lane; i < L; i += 32) {
     const uint16_t s = st[warp][i];
