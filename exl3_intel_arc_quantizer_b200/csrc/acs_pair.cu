@@ -498,9 +498,13 @@ __device__ int ck_walk_reg(const uint8_t* __restrict__ pck, int b, int cb, const
       uint16_t v2[NPL];
       uint32_t key1 = 0xFFFFFFFFu, cost1 = 0;
 #pragma unroll
-      for (int r = 0; r < NPL; ++r) {
+      for (int r = 0; r < NPL; ++r) {  // every load in flight before the candidates
         const int node = (lane + 32 * r) & (Q * Q - 1);
         v2[r] = cost_of(ckb, (node << (G::Kr - 2 * K)) | (e >> (2 * K)));
+      }
+#pragma unroll
+      for (int r = 0; r < NPL; ++r) {
+        const int node = (lane + 32 * r) & (Q * Q - 1);
         const int j1 = node & (Q - 1), kb = node >> K;
         const uint16_t cst = cand_cost<K>(cb, kb, (j1 << (G::Kr - K)) | (e >> K), ws1, v2[r],
                                           PASS == 2 && s1 == 0, pre);

@@ -14,7 +14,8 @@ constexpr int kPairNT = 512;  // threads per tile-pair ACS CTA
 // Steps between cost checkpoints of the tile-pair encoders (acs_pair.cu,
 // acs_cluster.cu): every 2nd step at K = 2 (the traceback recomputes one
 // level of 16 ancestors per two-step segment), every step above (measured:
-// a stride of 2 at K = 3 and 4 made the tracebacks 1.5-3x slower).
+// a stride of 2 at K = 3 and 4 cut the LDLQ tracebacks by 8% but the bulk
+// encoder's throughput by 2-4%).
 __host__ __device__ constexpr int ck_stride(int K) { return K == 2 ? 2 : 1; }
 constexpr int kTbWarps = 4;   // tiles (warps) per traceback CTA
 
