@@ -82,3 +82,50 @@ extern "C" int exl3_probe_fp16x2_rate(double* fp16_ops_per_s, exl3_stream_t stre
   *fp16_ops_per_s = ops / (ms * 1e-3);
   return EXL3_OK;
 }
+
+// ---------------------------------------------------------------------------
+// fp16 FMA rounding probe (probe_kernels.sycl:45-70): one thread per element
+// pair, so mode 0 feeds the two elements through one packed instruction as
+// the ACS kernels do.
+// ---------------------------------------------------------------------------
+namespace exl3 {
+__global__ void hfma_probe_kernel(const uint16_t* __restrict__ dh,
+                                  const uint16_t* __restrict__ cost, uint16_t* __restrict__ out,
+                                  int64_t n, int mode) {
+  const int64_t i0 = 2 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
+  if (i0 >= n) return;
+  const bool two = i0 + 1 < n;
+  const uint16_t a0 = dh[i0], c0 = cost[i0];
+  const uint16_t a1 = two ? dh[i0 + 1] : (uint16_t)0, c1 = two ? cost[i0 + 1] : (uint16_t)0;
+  uint16_t r0, r1;
+  if (mode == 0) {
+    const uint32_t a = (uint32_t)a0 | ((uint32_t)a1 << 16);
+    const uint32_t d = h2_fma(a, a, (uint32_t)c0 | ((uint32_t)c1 << 16));
+    r0 = (uint16_t)(d & 0xFFFFu);
+    r1 = (uint16_t)(d >> 16);
+  } else {
+    r0 = h_fma(a0, a0, c0);
+    r1 = h_fma(a1, a1, c1);
+  }
+  out[i0] = r0;
+  if (two) out[i0 + 1] = r1;
+}
+}  // namespace exl3
+
+extern "C" int exl3_probe_hfma(const uint16_t* dh, const uint16_t* cost, uint16_t* out, int64_t n,
+                               int mode, exl3_stream_t stream) {
+  using namespace exl3;
+  EXL3_REQUIRE(mode == 0 || mode == 1, "mode must be 0 (packed fma.rn.f16x2) or 1 (scalar "
+               "fma.rn.f16), got %d", mode);
+  EXL3_REQUIRE(n >= 0, "n must be >= 0, got %lld", (long long)n);
+  if (n == 0) return EXL3_OK;
+  EXL3_REQUIRE(dh && cost && out, "dh, cost and out must not be NULL");
+  const int threads = 256;
+  const int64_t pairs = (n + 1) / 2;
+  const int64_t blocks = (pairs + threads - 1) / threads;
+  EXL3_REQUIRE(blocks <= 0x7FFFFFFF, "n = %lld is too large", (long long)n);
+  hfma_probe_kernel<<<(unsigned)blocks, threads, 0, (cudaStream_t)stream>>>(dh, cost, out, n,
+                                                                            mode);
+  EXL3_LAUNCHED();
+  return EXL3_OK;
+}

@@ -392,17 +392,6 @@ acs_pair_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* __r
 // Traceback from checkpoints (one warp per tile)
 // ---------------------------------------------------------------------------
 
-__device__ __forceinline__ uint16_t h_sub(uint16_t a, uint16_t b) {
-  uint16_t r;
-  asm("sub.rn.f16 %0, %1, %2;" : "=h"(r) : "h"(a), "h"(b));
-  return r;
-}
-__device__ __forceinline__ uint16_t h_fma(uint16_t a, uint16_t b, uint16_t c) {
-  uint16_t r;
-  asm("fma.rn.f16 %0, %1, %2, %3;" : "=h"(r) : "h"(a), "h"(b), "h"(c));
-  return r;
-}
-
 // Ordering key of candidate k with cost bits v under the sequential rule
 // (strict < over ascending k; a NaN at k = 0 wins; later NaNs never win):
 // the smallest key is the candidate a forward pass keeps. Costs are >= +0,

@@ -63,6 +63,17 @@ __device__ __forceinline__ uint32_t h2_fma(uint32_t a, uint32_t b, uint32_t c) {
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
   return d;
 }
+// The scalar forms (the tracebacks' candidate re-evaluation).
+__device__ __forceinline__ uint16_t h_sub(uint16_t a, uint16_t b) {
+  uint16_t r;
+  asm("sub.rn.f16 %0, %1, %2;" : "=h"(r) : "h"(a), "h"(b));
+  return r;
+}
+__device__ __forceinline__ uint16_t h_fma(uint16_t a, uint16_t b, uint16_t c) {
+  uint16_t r;
+  asm("fma.rn.f16 %0, %1, %2, %3;" : "=h"(r) : "h"(a), "h"(b), "h"(c));
+  return r;
+}
 // {v, v} - w with v the low (HI = false) or high lane of `cb`. One asm block,
 // so the lane broadcast cannot be hoisted away from the subtraction (keeping
 // 128 broadcast copies of a thread's codebook live would exhaust registers).

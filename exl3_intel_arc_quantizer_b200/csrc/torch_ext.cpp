@@ -65,6 +65,26 @@ void decode_codebook(int64_t cb, at::Tensor out_lut) {
                "decode_codebook");
 }
 
+// probe_hfma (probe_xpu.cpp:47-62): out = fma(dh, dh, cost) in fp16, mode 0 =
+// the ACS kernels' packed instruction, mode 1 = the tracebacks' scalar one.
+void probe_hfma(at::Tensor dh, at::Tensor cost, at::Tensor out, int64_t mode) {
+  const int64_t dev = check_cuda_tensor(dh, "dh", at::kHalf, dh.dim());
+  TORCH_CHECK(check_cuda_tensor(cost, "cost", at::kHalf, cost.dim()) == dev,
+              "dh and cost must share a device");
+  TORCH_CHECK(check_cuda_tensor(out, "out", at::kHalf, out.dim()) == dev,
+              "dh and out must share a device");
+  TORCH_CHECK(dh.numel() == cost.numel() && dh.numel() == out.numel(),
+              "probe_hfma tensors must have equal numel");
+  TORCH_CHECK(mode == 0 || mode == 1,
+              "mode must be 0 (packed fma.rn.f16x2) or 1 (scalar fma.rn.f16)");
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(dev));
+  check_status(exl3_probe_hfma(reinterpret_cast<const uint16_t*>(dh.data_ptr()),
+                               reinterpret_cast<const uint16_t*>(cost.data_ptr()),
+                               reinterpret_cast<uint16_t*>(out.data_ptr()), dh.numel(),
+                               static_cast<int>(mode), stream_of(dev)),
+               "probe_hfma");
+}
+
 int64_t quantize_tiles_ws_bytes(int64_t n, int64_t K, int64_t L) {
   return static_cast<int64_t>(
       exl3_quantize_tiles_ws_bytes(n, static_cast<int>(K), static_cast<int>(L)));
@@ -256,6 +276,9 @@ void pack_trellis(at::Tensor states, at::Tensor packed, int64_t K) {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_codebook", &decode_codebook,
         "Decode all 65536 states of codebook cb into an fp16 CUDA tensor");
+  m.def("probe_hfma", &probe_hfma, py::arg("dh"), py::arg("cost"), py::arg("out"), py::arg("mode"),
+        "out[i] = fma(dh[i], dh[i], cost[i]) in fp16; mode 0 = packed fma.rn.f16x2 (ACS), "
+        "mode 1 = scalar fma.rn.f16 (traceback)");
   m.def("quantize_tiles_ws_bytes", &quantize_tiles_ws_bytes, py::arg("n"), py::arg("K"),
         py::arg("L") = 256, "Workspace bytes for encode_tiles over n tiles");
   m.def("encode_tiles", &encode_tiles, py::arg("input_tiles"), py::arg("output_tiles"),

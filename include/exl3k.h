@@ -253,6 +253,21 @@ int exl3_hessian_finalize(float* H, int64_t d, int64_t count, float damping_lamb
 int exl3_probe_fp16x2_rate(double* fp16_ops_per_s, exl3_stream_t stream);
 
 /*
+ * fp16 FMA rounding probe: out[i] = dh[i] * dh[i] + cost[i] rounded once to
+ * binary16 (round to nearest even), for the encoder's metric. Replaces
+ * `probe_hfma(dh, cost, out, mode)` (csrc/probe_xpu/probe_xpu.cpp:47-62,
+ * kernel csrc/probe_xpu/probe_kernels.sycl:45-70), whose tests
+ * (tests/test_xpu_extension.py:64-80, exl3_quant/xpu_probe.py:153-270) check
+ * it against an exact single rounding. mode 0: the packed fma.rn.f16x2 the
+ * ACS kernels issue (elements 2j and 2j+1 share one instruction); mode 1: the
+ * scalar fma.rn.f16 the tracebacks issue. Arrays hold binary16 bit patterns;
+ * n == 0 is a no-op. Asynchronous on `stream`. EXL3_EINVAL for another mode,
+ * a negative n or a NULL array with n > 0.
+ */
+int exl3_probe_hfma(const uint16_t* dh, const uint16_t* cost, uint16_t* out, int64_t n, int mode,
+                    exl3_stream_t stream);
+
+/*
  * Cluster split of the encoder's ACS passes (K = 2..6). A call with few
  * tile pairs (an LDLQ step of a column-sharded module: a few dozen tiles)
  * would leave most SMs idle with one pair per CTA; the encoder then spreads
