@@ -405,15 +405,31 @@ __device__ __forceinline__ uint32_t cand_key(int k, uint16_t v) {
 // Cost of candidate k into edge x at step s. prev = predecessor's cost after
 // step s-1 (0 before step 0); at step 0 of a constrained pass, a candidate
 // whose predecessor is not `pre` costs +inf.
+// cand_diff is the part that does not depend on prev (codebook value minus
+// the weight), cand_finish the rest.
 template <int K>
-__device__ __forceinline__ uint16_t cand_cost(int cb, int k, int x, uint16_t w, uint16_t prev,
-                                              bool first, int pre) {
+__device__ __forceinline__ uint16_t cand_diff(int cb, int k, int x, uint16_t w) {
   using G = PGeo<K>;
-  const uint16_t v = cb_state_bits(cb, ((uint32_t)k << G::Kr) | (uint32_t)x);
-  const uint16_t d = h_sub(v, w);
+  return h_sub(cb_state_bits(cb, ((uint32_t)k << G::Kr) | (uint32_t)x), w);
+}
+template <int K>
+__device__ __forceinline__ uint16_t cand_finish(uint16_t d, uint16_t prev, int k, int x,
+                                                bool first, int pre) {
+  using G = PGeo<K>;
   uint16_t c = h_fma(d, d, prev);
   if (first && pre >= 0 && (((k << G::GB) | (x >> K)) != pre)) c = 0x7C00u;
   return c;
+}
+template <int K>
+__device__ __forceinline__ uint16_t cand_cost(int cb, int k, int x, uint16_t w, uint16_t prev,
+                                              bool first, int pre) {
+  return cand_finish<K>(cand_diff<K>(cb, k, x, w), prev, k, x, first, pre);
+}
+
+// The cost bits a winning key was made from (cand_key inverted). Key 0 is a
+// NaN at k = 0: any NaN stands for it, since later keys see only NaN-ness.
+__device__ __forceinline__ uint16_t key_cost(uint32_t key) {
+  return key == 0u ? (uint16_t)0x7FFFu : (uint16_t)((key >> 16) - 1u);
 }
 
 constexpr int kSingleR = 4;  // the single-tile K=1 encoder checkpoints every 4th step
@@ -427,8 +443,10 @@ constexpr int kSingleR = 4;  // the single-tile K=1 encoder checkpoints every 4t
 // over the lanes, node (kb << K) | j1 in register r of lane
 // ((kb << K) | j1) & 31; each lane evaluates branch kb of level-1 node j1
 // for its nodes, keeps the lowest key, and lanes holding the same j1 combine
-// by xor shuffles; the two path steps then read level-1 costs from lanes
-// 0..Q-1 and level-2 costs by shuffles. The candidate costs, the ordering
+// by xor shuffles of the keys alone (a key holds its cost bits). Step i then
+// takes the minimum over branch kq = lane & (Q-1) of node kq; step i-1's
+// candidates are the level-1 candidates of the node step i picked, so their
+// keys are reused rather than evaluated again. The candidate costs, the ordering
 // keys (cand_key) and the first-minimum rule are those of the forward pass,
 // so the path is the one a tracked forward pass would record.
 template <int K, int PASS>
@@ -485,53 +503,41 @@ __device__ int ck_walk_reg(const uint8_t* __restrict__ pck, int b, int cb, const
       const int s1 = i - 1;
       const uint16_t ws1 = wt(s1);
       uint16_t v2[NPL];
-      uint32_t key1 = 0xFFFFFFFFu, cost1 = 0;
 #pragma unroll
       for (int r = 0; r < NPL; ++r) {  // every load in flight before the candidates
         const int node = (lane + 32 * r) & (Q * Q - 1);
         v2[r] = cost_of(ckb, (node << (G::Kr - 2 * K)) | (e >> (2 * K)));
       }
+      // step i, branch kq = lane & (Q-1): its difference needs no load
+      const int kq = lane & (Q - 1);
+      const uint16_t d0 = cand_diff<K>(cb, kq, e, wt(i));
+      // level 1: node (kb << K) | j1 is branch kb of step i-1 into the edge
+      // that step i leaves when it picks j1; own[r] keeps that candidate's key
+      uint32_t own[NPL], key1 = 0xFFFFFFFFu;
 #pragma unroll
       for (int r = 0; r < NPL; ++r) {
         const int node = (lane + 32 * r) & (Q * Q - 1);
         const int j1 = node & (Q - 1), kb = node >> K;
-        const uint16_t cst = cand_cost<K>(cb, kb, (j1 << (G::Kr - K)) | (e >> K), ws1, v2[r],
-                                          PASS == 2 && s1 == 0, pre);
-        const uint32_t key = cand_key(kb, cst);
-        if (key < key1) {
-          key1 = key;
-          cost1 = cst;
-        }
+        const int x1 = (j1 << (G::Kr - K)) | (e >> K);
+        own[r] = cand_key(kb, cand_finish<K>(cand_diff<K>(cb, kb, x1, ws1), v2[r], kb, x1,
+                                             PASS == 2 && s1 == 0, pre));
+        key1 = min(key1, own[r]);
       }
 #pragma unroll
-      for (int h = Q; h < 32; h <<= 1) {  // lanes with the same j1 = lane & (Q-1)
-        const uint32_t ok = __shfl_xor_sync(0xFFFFFFFFu, key1, h);
-        const uint32_t oc = __shfl_xor_sync(0xFFFFFFFFu, cost1, h);
-        if (ok < key1) {
-          key1 = ok;
-          cost1 = oc;
-        }
-      }
-      // step i: branch k = lane < Q from level-1 node k (lane k holds it)
-      uint32_t bk = 0xFFFFFFFFu;
-      if (lane < Q)
-        bk = cand_key(lane, cand_cost<K>(cb, lane, e, wt(i), (uint16_t)cost1, PASS == 2 && i == 0,
-                                         pre));
+      for (int h = Q; h < 32; h <<= 1)  // lanes with the same j1 = lane & (Q-1)
+        key1 = min(key1, __shfl_xor_sync(0xFFFFFFFFu, key1, h));
+      // step i: branch kq from level-1 node kq, whose minimum this lane holds
+      const uint32_t bk = cand_key(kq, cand_finish<K>(d0, key_cost(key1), kq, e,
+                                                      PASS == 2 && i == 0, pre));
       const int k0 = pick(__reduce_min_sync(0xFFFFFFFFu, bk));
       if (PASS == 2 && lane == 0) st[i] = (uint16_t)((k0 << G::Kr) | e);
       e = (k0 << G::GB) | (e >> K);
       if (s1 >= i_stop) {
-        // step i - 1: branch k from level-2 node (k << K) | k0
-        const int node = (((lane & (Q - 1)) << K) | k0);
-        uint16_t prev2 = 0;
-#pragma unroll
-        for (int r = 0; r < NPL; ++r) {
-          const uint16_t t = (uint16_t)__shfl_sync(0xFFFFFFFFu, (uint32_t)v2[r], node & 31);
-          if ((node >> 5) == r) prev2 = t;
-        }
+        // step i - 1: the candidates of level-1 node k0 are its branches
         uint32_t bk2 = 0xFFFFFFFFu;
-        if (lane < Q)
-          bk2 = cand_key(lane, cand_cost<K>(cb, lane, e, ws1, prev2, PASS == 2 && s1 == 0, pre));
+#pragma unroll
+        for (int r = 0; r < NPL; ++r)
+          if (((lane + 32 * r) & (Q - 1)) == k0) bk2 = min(bk2, own[r]);
         const int k1 = pick(__reduce_min_sync(0xFFFFFFFFu, bk2));
         if (PASS == 2 && lane == 0) st[s1] = (uint16_t)((k1 << G::Kr) | e);
         e = (k1 << G::GB) | (e >> K);
@@ -548,8 +554,10 @@ __device__ int ck_walk_reg(const uint8_t* __restrict__ pck, int b, int cb, const
 // the path edge four steps up); level m < 4 node j lives in every lane with
 // lane & (2^m - 1) == j: such a lane evaluates branch k = (lane >> m) & 1
 // from its own level-(m+1) cost and the two branches meet by one xor
-// shuffle. The path steps read the level costs back by shuffles. Costs,
-// keys (cand_key) and the first-minimum rule are the forward pass's.
+// shuffle of their keys (a key holds its cost bits). The path steps below
+// the top reuse those keys: step i - tt's candidates are the level-tt
+// candidates of the node the steps before it picked. Costs, keys
+// (cand_key) and the first-minimum rule are the forward pass's.
 template <int PASS>
 __device__ int ck_walk_single_reg(const uint8_t* __restrict__ pck, int cb, const uint16_t* w,
                                   int L, int e_top, int pre, uint16_t* st, int lane) {
@@ -579,36 +587,37 @@ __device__ int ck_walk_single_reg(const uint8_t* __restrict__ pck, int cb, const
       const int node = lane & ((1 << Lv) - 1);
       cost[4] = ckb ? (uint32_t)__ldg(ckb + ((node << (G::Kr - Lv)) | (e >> Lv))) : 0u;
     }
+    // step i, branch lane & 1: its difference needs no load
+    const uint16_t d0 = cand_diff<1>(cb, lane & 1, e, wt(i));
+    uint32_t own[4];  // own[m]: this lane's branch of level-m node lane & (2^m - 1)
 #pragma unroll
     for (int m = 3; m >= 1; --m) {
       if (m >= Lv) {
         cost[m] = cost[m + 1];  // levels above the segment's top are not used
+        own[m] = 0xFFFFFFFFu;
         continue;
       }
       const int j = lane & ((1 << m) - 1), kb = (lane >> m) & 1;
       const int s = i - m;
-      const uint16_t cst = cand_cost<1>(cb, kb, (j << (G::Kr - m)) | (e >> m), wt(s),
-                                        (uint16_t)cost[m + 1], PASS == 2 && s == 0, pre);
-      uint32_t key = cand_key(kb, cst), cv = cst;
-      const uint32_t ok = __shfl_xor_sync(0xFFFFFFFFu, key, 1 << m);
-      const uint32_t oc = __shfl_xor_sync(0xFFFFFFFFu, cv, 1 << m);
-      if (ok < key) {
-        key = ok;
-        cv = oc;
-      }
-      cost[m] = cv;
+      const int x = (j << (G::Kr - m)) | (e >> m);
+      own[m] = cand_key(kb, cand_finish<1>(cand_diff<1>(cb, kb, x, wt(s)), (uint16_t)cost[m + 1],
+                                           kb, x, PASS == 2 && s == 0, pre));
+      cost[m] = key_cost(min(own[m], __shfl_xor_sync(0xFFFFFFFFu, own[m], 1 << m)));
     }
-    // the path: steps i .. c+1; step i - tt reads level tt+1 node (k << tt) | j
+    // the path: steps i .. c+1. Step i: branch lane & 1 from level-1 node
+    // lane & 1 (this lane's cost[1]); step i - tt (tt >= 1): the level-tt
+    // candidates of the node the steps before picked (j), keys reused.
     int j = 0;
 #pragma unroll
     for (int tt = 0; tt < 4; ++tt) {
       if (tt >= Lv || i - tt < i_stop) break;
       const int s = i - tt;
-      const int src = (((lane & 1) << tt) | j) & 31;
-      const uint16_t prev = (uint16_t)__shfl_sync(0xFFFFFFFFu, cost[tt + 1], src);
-      uint32_t bk = 0xFFFFFFFFu;
-      if (lane < 2)
-        bk = cand_key(lane, cand_cost<1>(cb, lane, e, wt(s), prev, PASS == 2 && s == 0, pre));
+      uint32_t bk;
+      if (tt == 0)
+        bk = cand_key(lane & 1, cand_finish<1>(d0, (uint16_t)cost[1], lane & 1, e,
+                                               PASS == 2 && s == 0, pre));
+      else
+        bk = (lane & ((1 << tt) - 1)) == j ? own[tt] : 0xFFFFFFFFu;
       const int k = pick(__reduce_min_sync(0xFFFFFFFFu, bk));
       if (PASS == 2 && lane == 0) st[s] = (uint16_t)((k << G::Kr) | e);
       j |= k << tt;
