@@ -433,6 +433,7 @@ __device__ __forceinline__ uint16_t key_cost(uint32_t key) {
 }
 
 constexpr int kSingleR = 4;  // the single-tile K=1 encoder checkpoints every 4th step
+constexpr size_t kTbDeepBytes = size_t(64) << 20;  // checkpoints of a call beyond L2
 
 // The pair walk without shared-memory levels. K >= 3 (a checkpoint every
 // step, one level): lane k loads the checkpoint cost of branch k's
@@ -449,12 +450,13 @@ constexpr int kSingleR = 4;  // the single-tile K=1 encoder checkpoints every 4t
 // keys are reused rather than evaluated again. The candidate costs, the ordering
 // keys (cand_key) and the first-minimum rule are those of the forward pass,
 // so the path is the one a tracked forward pass would record.
-template <int K, int PASS>
+template <int K, int PASS, int D>
 __device__ int ck_walk_reg(const uint8_t* __restrict__ pck, int b, int cb, const uint16_t* w,
                            int L, int e_top, int pre, uint16_t* st, int lane) {
   using G = PGeo<K>;
-  constexpr int R = G::R;
+  constexpr int R = G::R;  // checkpoint stride; D = steps per segment
   constexpr int Q = G::Q;
+  static_assert(D % R == 0 && (D == 1 || D == 2), "a segment spans 1 or 2 checkpoint strides");
   const int half = L / 2;
   const int i_stop = PASS == 1 ? half : 0;
   auto wt = [&](int s) { return w[PASS == 1 ? (s < half ? s + half : s - half) : s]; };
@@ -466,16 +468,16 @@ __device__ int ck_walk_reg(const uint8_t* __restrict__ pck, int b, int cb, const
   while (i >= i_stop) {
     int c, slot;
     if (PASS == 1) {
-      const int rel = ((i - 1) - (half - 1)) / R;
-      c = (half - 1) + rel * R;
-      slot = rel;
+      const int rel = ((i - 1) - (half - 1)) / D;
+      c = (half - 1) + rel * D;
+      slot = rel * (D / R);
     } else {
-      c = (i / R) * R - 1;
+      c = (i / D) * D - 1;
       slot = (c + 1) / R - 1;
     }
     const uint32_t* ckb =
         c >= 0 ? reinterpret_cast<const uint32_t*>(pck + (size_t)slot * G::CKB) : nullptr;
-    if constexpr (R == 1) {
+    if constexpr (D == 1) {
       const uint16_t ws = wt(i);
       const bool first = PASS == 2 && i == 0;
       constexpr int NPL = (Q + 31) / 32;  // branches per lane, all loads issued first
@@ -498,7 +500,7 @@ __device__ int ck_walk_reg(const uint8_t* __restrict__ pck, int b, int cb, const
       if (PASS == 2 && lane == 0) st[i] = (uint16_t)((k << G::Kr) | e);
       e = (k << G::GB) | (e >> K);
     } else {
-      static_assert(R == 2 && Q * Q <= 256, "two-level register walk: Q^2 <= 256");
+      static_assert(Q * Q <= 256, "two-level register walk: Q^2 <= 256");
       constexpr int NPL = (Q * Q + 31) / 32;  // level-2 nodes per lane
       const int s1 = i - 1;
       const uint16_t ws1 = wt(s1);
@@ -636,7 +638,7 @@ __device__ __forceinline__ void tb_load_weights(const float* __restrict__ in, in
   __syncwarp();
 }
 
-template <int K>
+template <int K, int D>
 __global__ void __launch_bounds__(32 * kTbWarps)
 pair_tb1_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck, size_t ck_pair_bytes,
                 int n, int L, int cb, const int32_t* __restrict__ best_edge,
@@ -646,12 +648,12 @@ pair_tb1_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck, si
   const int tile = blockIdx.x * kTbWarps + warp;
   if (tile >= n) return;
   tb_load_weights<K>(in, tile, L, w[warp], lane);
-  const int e = ck_walk_reg<K, 1>(ck + (size_t)(tile >> 1) * ck_pair_bytes, tile & 1, cb, w[warp],
+  const int e = ck_walk_reg<K, 1, D>(ck + (size_t)(tile >> 1) * ck_pair_bytes, tile & 1, cb, w[warp],
                                   L, best_edge[tile], -1, nullptr, lane);
   if (lane == 0) end_state[tile] = e;
 }
 
-template <int K>
+template <int K, int D>
 __global__ void __launch_bounds__(32 * kTbWarps)
 pair_tb2_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck, size_t ck_pair_bytes,
                 int n, int L, int cb, const int32_t* __restrict__ end_state,
@@ -664,7 +666,7 @@ pair_tb2_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck, si
   if (tile >= n) return;
   tb_load_weights<K>(in, tile, L, w[warp], lane);
   const int pre = end_state[tile];
-  ck_walk_reg<K, 2>(ck + (size_t)(tile >> 1) * ck_pair_bytes, tile & 1, cb, w[warp], L, pre, pre,
+  ck_walk_reg<K, 2, D>(ck + (size_t)(tile >> 1) * ck_pair_bytes, tile & 1, cb, w[warp], L, pre, pre,
                     st[warp], lane);
   __syncwarp();
   for (int i = lane; i < L; i += 32) {
@@ -722,6 +724,17 @@ int pair_encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t*
       }
     }
     const int mb = 2 * bulk < m ? 2 * bulk : m;  // tiles of the whole waves
+    // Tracebacks at K = 3 (a checkpoint every step) take two steps per
+    // segment in calls of at most one wave of pairs whose checkpoints do not
+    // fit in L2: each segment is then a round trip to HBM on the path's
+    // critical chain, and halving their number outweighs evaluating 64
+    // ancestors per segment (measured: 256 tiles 1.000 -> 0.916 ms per call).
+    // Larger calls keep one step per segment, and so does K = 4, whose 256
+    // ancestors per segment made its tracebacks twice as slow. Outputs are
+    // identical either way.
+    constexpr int RD = PGeo<K>::R;
+    constexpr bool kDeepOk = K == 3 && RD == 1;
+    const bool deep = kDeepOk && pairs <= sms && (size_t)pairs * ck_pair > kTbDeepBytes;
     auto acs_pass = [&](int pass) -> int {
       LaunchTimer lt(stream, 0);
       int32_t* be = pass == 1 ? best_edge : nullptr;
@@ -746,17 +759,25 @@ int pair_encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t*
     EXL3_LAUNCHED();
     {
       LaunchTimer lt(stream, 1);
-      pair_tb1_kernel<K><<<tb_grid, 32 * kTbWarps, 0, stream>>>(cin, ck, ck_pair, m, L, cb,
-                                                                best_edge, end_state);
+      if (deep)
+        pair_tb1_kernel<K, kDeepOk ? 2 : RD><<<tb_grid, 32 * kTbWarps, 0, stream>>>(
+            cin, ck, ck_pair, m, L, cb, best_edge, end_state);
+      else
+        pair_tb1_kernel<K, RD><<<tb_grid, 32 * kTbWarps, 0, stream>>>(cin, ck, ck_pair, m, L, cb,
+                                                                     best_edge, end_state);
     }
     EXL3_LAUNCHED();
     if (int rc = acs_pass(2)) return rc;
     EXL3_LAUNCHED();
     {
       LaunchTimer lt(stream, 1);
-      pair_tb2_kernel<K><<<tb_grid, 32 * kTbWarps, 0, stream>>>(
-          cin, ck, ck_pair, m, L, cb, end_state, out_w + start * L, out_idx + start * L,
-          out_packed ? out_packed + start * 16 * K : nullptr);
+      int16_t* pk = out_packed ? out_packed + start * 16 * K : nullptr;
+      if (deep)
+        pair_tb2_kernel<K, kDeepOk ? 2 : RD><<<tb_grid, 32 * kTbWarps, 0, stream>>>(
+            cin, ck, ck_pair, m, L, cb, end_state, out_w + start * L, out_idx + start * L, pk);
+      else
+        pair_tb2_kernel<K, RD><<<tb_grid, 32 * kTbWarps, 0, stream>>>(
+            cin, ck, ck_pair, m, L, cb, end_state, out_w + start * L, out_idx + start * L, pk);
     }
     EXL3_LAUNCHED();
   }
