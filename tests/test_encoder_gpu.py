@@ -107,6 +107,24 @@ def test_random_batch_matches_c_oracle(K):
     enc.arena.release()
 
 
+@pytest.mark.parametrize("n,L", [(64, 160), (40, 256), (400, 256), (16, 256)])
+def test_k3_traceback_walks_match_c_oracle(n, L):
+    """K=3 tracebacks walk two steps per segment in calls of at most one wave
+    of pairs whose checkpoints exceed L2 (64 x L=160, 40 tiles) and one step
+    otherwise (400 tiles: more pairs than SMs; 16 tiles: checkpoints in L2);
+    every choice gives the oracle's states."""
+    rng = np.random.default_rng(7000 + n + L)
+    tiles = (rng.standard_normal((n, L)) *
+             np.exp(0.5 * rng.standard_normal((n, 1)))).astype(np.float32)
+    enc = XPUTrellisEncoder(K=3, cb=tf.CB_MUL1, tile_len=L)
+    w, i, packed, cost = enc.encode_device(torch.from_numpy(tiles).to(DEV))
+    ref = COracle(3, tf.CB_MUL1, L).encode_batch(tiles)
+    np.testing.assert_array_equal(i.cpu().numpy().view(np.uint16), ref["indices"])
+    np.testing.assert_array_equal(np.float16(cost.cpu().numpy()).view(np.uint16),
+                                  ref["path_cost"].view(np.uint16))
+    enc.arena.release()
+
+
 def test_chunked_workspace_matches_single_chunk():
     """Partial chunks: 19 tiles through a workspace of 6 (chunks 6,6,6,1)."""
     rng = np.random.default_rng(555)
