@@ -32,7 +32,7 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 METRIC = "encoder tiles/s at K=2/4 (1/2/4/8 B200); seconds per 4096x4096 layer"
-PUBLISHED_K2_TILES_PER_S = 1711.5     # Arc B580, K=2 mul1, 65,536 tiles
+PUBLISHED_K2_TILES_PER_S = 1711.5     # the reference's published Arc B580 rate, K=2 mul1
 ACS_PER_TILE = 2 * 256 * 65536        # candidate add-compare-selects per tile (both passes)
 FP16_OPS_PER_ACS = 2                  # sub + fma per candidate on the fp16 FMA pipe
                                       # (the running min is an ALU-pipe op)

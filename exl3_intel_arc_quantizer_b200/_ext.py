@@ -45,6 +45,7 @@ def _declare(handle: ctypes.CDLL) -> None:
     handle.exl3_quantize_tiles_ws_bytes.argtypes = [c.c_int64, c.c_int, c.c_int]
     handle.exl3_encoder_set_cluster.argtypes = [c.c_int]
     handle.exl3_encoder_fault_count.argtypes = [c.POINTER(c.c_uint)]
+    handle.exl3_encoder_test_cluster_wait.argtypes = [c.c_longlong, c.c_int]
     handle.exl3_encoder_cluster_capacity.argtypes = [c.c_int, c.c_int, c.POINTER(c.c_int)]
 
 
@@ -77,6 +78,60 @@ def encoder_fault_count() -> int:
     v = ctypes.c_uint(0)
     _check(lib().exl3_encoder_fault_count(ctypes.byref(v)))
     return int(v.value)
+
+
+class EncoderFault(RuntimeError):
+    """An encoder CTA gave up a bounded inter-CTA wait while the call ran, so
+    the call's trellis states and reconstructions are not valid."""
+
+
+def set_cluster_wait_test_hook(wait_limit_ns: int, stop_sends_at_step: int) -> None:
+    """Test hook of the cluster encoder's error path
+    (``exl3_encoder_test_cluster_wait``): from ``stop_sends_at_step`` on,
+    every CTA stops sending, so the next waits run out after
+    ``wait_limit_ns``. ``(0, -1)`` restores normal operation."""
+    _check(lib().exl3_encoder_test_cluster_wait(int(wait_limit_ns), int(stop_sends_at_step)))
+
+
+class encoder_fault_check:
+    """Context manager that raises :class:`EncoderFault` when the encoder's
+    fault count on ``device`` grew inside the block. Reading the count
+    synchronizes the device (at entry and at exit); a block that raised
+    already is left alone. ``delta()`` reads the growth so far, for callers
+    that combine it across ranks before raising."""
+
+    def __init__(self, device=None):
+        import torch
+
+        self.device = torch.device(device) if device is not None else None
+        self.start = 0
+
+    def _count(self) -> int:
+        import torch
+
+        if self.device is None or self.device.type != "cuda":
+            return 0
+        with torch.cuda.device(self.device):
+            return encoder_fault_count()
+
+    def delta(self) -> int:
+        return self._count() - self.start
+
+    def __enter__(self):
+        self.start = self._count()
+        return self
+
+    def __exit__(self, exc_type, exc, tb):
+        if exc_type is None:
+            raise_on_faults(self.delta())
+        return False
+
+
+def raise_on_faults(delta: int) -> None:
+    if delta > 0:
+        raise EncoderFault(
+            f"{delta} encoder CTA(s) gave up a bounded inter-CTA wait during this call; "
+            "its trellis states and reconstructions are not valid")
 
 
 def ext():

@@ -15,15 +15,18 @@ void set_error(const char* fmt, ...) {
 }
 
 int sm_count() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  if (dev >= 0 && dev < 64) {
+    const int c = cached[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
       sms <= 0)
     sms = 148;
-  if (dev >= 0 && dev < 64) cached[dev] = sms;
+  if (dev >= 0 && dev < 64) cached[dev].store(sms, std::memory_order_relaxed);
   return sms;
 }
 

@@ -27,9 +27,13 @@
 // kernels are shared. Tie-breaking and NaN rules are unchanged (min over
 // ascending k in registers; compare-and-select for pairs with NaN inputs).
 //
-// Every mbarrier wait is bounded (2 s, globaltimer); a CTA that times out
-// raises a CTA-wide abort flag, stops waiting and sending, runs to the end
-// and counts the fault in a device counter (exl3_encoder_fault_count).
+// Every mbarrier wait is bounded (2 s by default, globaltimer); a CTA that
+// times out raises a CTA-wide abort flag, stops waiting and sending, runs to
+// the end and counts the fault in a device counter (exl3_encoder_fault_count),
+// which the layer drivers compare before and after a call. A test hook
+// (exl3_encoder_test_cluster_wait) shortens the limit and makes every CTA
+// stop sending from one step on, so the waits after it run out while no
+// message is in flight.
 #include "common.cuh"
 #include "encoder_shared.cuh"
 
@@ -122,14 +126,15 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait for a message; false on timeout (raises *abort) or abort.
-__device__ __forceinline__ bool msg_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+__device__ __forceinline__ bool msg_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                         uint64_t wait_ns) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = gclock();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try(bar, parity)) return true;
     if ((it & 15u) == 0u) {
       if (*abort) return false;
-      if (gclock() - t0 > kClusterWaitNs) {
+      if (gclock() - t0 > wait_ns) {
         *abort = 1;
         return false;
       }
@@ -306,7 +311,8 @@ __device__ __forceinline__ void cl_pass(const uint32_t (&cbv)[CGeo<K, C>::NCB],
                                         const uint32_t* wt, uint32_t* inb, uint32_t* own,
                                         uint32_t bar0, const Links& lk, uint8_t* ckp, int L,
                                         int t, int r, int preA, int preB, uint32_t msg,
-                                        uint32_t expect, volatile int* abort) {
+                                        uint32_t expect, volatile int* abort, uint64_t wait_ns,
+                                        int stop_at) {
   using G = CGeo<K, C>;
   const int half = L / 2;
   for (int i = 0; i < L; ++i) {
@@ -314,10 +320,13 @@ __device__ __forceinline__ void cl_pass(const uint32_t (&cbv)[CGeo<K, C>::NCB],
     if (i > 0 && !aborted) {
       const uint32_t m = msg + (uint32_t)(i - 1);
       const uint32_t bar = bar0 + 8u * (m & 3u);
-      if (msg_wait(bar, (m >> 2) & 1u, abort) && t == 0) mbar_expect(bar, expect);  // message m+4
+      if (msg_wait(bar, (m >> 2) & 1u, abort, wait_ns) && t == 0)
+        mbar_expect(bar, expect);  // message m+4
     }
     const uint32_t w2 = wt[PASS == 1 ? (i < half ? i + half : i - half) : i];
-    const bool send = i < L - 1 && *abort == 0;
+    // stop_at >= 0 (test hook only): every CTA stops sending at that step,
+    // so all earlier messages were consumed and none is in flight
+    const bool send = i < L - 1 && *abort == 0 && (stop_at < 0 || i < stop_at);
     int slot = -1;
     if (PASS == 1) {
       const int rel = i - (half - 1);
@@ -348,7 +357,8 @@ template <int K, int C, int PASS>
 __global__ void __launch_bounds__(CGeo<K, C>::NT, 1)
 acs_cluster_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* __restrict__ ck,
                    size_t ck_pair_bytes, int32_t* __restrict__ best_edge,
-                   const int32_t* __restrict__ end_state, float* __restrict__ path_cost) {
+                   const int32_t* __restrict__ end_state, float* __restrict__ path_cost,
+                   uint64_t wait_ns, int stop_at) {
   using G = CGeo<K, C>;
   extern __shared__ __align__(16) uint8_t smem[];
   uint32_t* inb = reinterpret_cast<uint32_t*>(smem);  // 4 message buffers
@@ -417,9 +427,9 @@ acs_cluster_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* 
     const bool has_b = 2 * tp + 1 < n;
     if constexpr (PASS == 1) {
       if (nan)
-        cl_pass<K, C, 1, true>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, -1, -1, msg, expect, &abort_s);
+        cl_pass<K, C, 1, true>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, -1, -1, msg, expect, &abort_s, wait_ns, stop_at);
       else
-        cl_pass<K, C, 1, false>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, -1, -1, msg, expect, &abort_s);
+        cl_pass<K, C, 1, false>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, -1, -1, msg, expect, &abort_s, wait_ns, stop_at);
       // argmin over the cluster: lowest key = (cost bits + edge), finite only
       uint32_t ka = 0xFFFFFFFFu, kb = 0xFFFFFFFFu;
       for (int le = t; le < G::SL; le += G::NT) {
@@ -463,9 +473,9 @@ acs_cluster_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* 
       const int preA = end_state[ta];
       const int preB = has_b ? end_state[tb] : preA;
       if (nan)
-        cl_pass<K, C, 2, true>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, preA, preB, msg, expect, &abort_s);
+        cl_pass<K, C, 2, true>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, preA, preB, msg, expect, &abort_s, wait_ns, stop_at);
       else
-        cl_pass<K, C, 2, false>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, preA, preB, msg, expect, &abort_s);
+        cl_pass<K, C, 2, false>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, preA, preB, msg, expect, &abort_s, wait_ns, stop_at);
       if (t == 0 && path_cost) {
         if (preA / G::SL == r)
           path_cost[ta] = half_bits_to_float((uint16_t)(fin[preA - r * G::SL] & 0xFFFFu));
@@ -487,23 +497,28 @@ acs_cluster_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* 
 // Host side
 // ---------------------------------------------------------------------------
 int g_cluster_policy = 0;  // 0 automatic, 1 never, 2/4/8 forced
+std::atomic<unsigned long long> g_cluster_wait_ns{kClusterWaitNs};
+std::atomic<int> g_cluster_stop_at{-1};  // test hook: step at which sends stop
 
 template <int K, int C>
 struct ClusterKernels {
   static int setup(int dev) {
-    static uint32_t done = 0;
-    if (dev < 32 && (done & (1u << dev))) return EXL3_OK;
+    static DeviceBits done;
+    if (done.has(dev)) return EXL3_OK;
     EXL3_CUDA(cudaFuncSetAttribute(acs_cluster_kernel<K, C, 1>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)CGeo<K, C>::SMEM_LAUNCH));
     EXL3_CUDA(cudaFuncSetAttribute(acs_cluster_kernel<K, C, 2>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)CGeo<K, C>::SMEM_LAUNCH));
-    if (dev < 32) done |= 1u << dev;
+    done.set(dev);
     return EXL3_OK;
   }
   // clusters of this kernel that fit on the device at once (cached per device)
   static int max_active(int dev) {
-    static int cache[32] = {0};
-    if (dev < 32 && cache[dev]) return cache[dev];
+    static std::atomic<int> cache[64];  // 0 unknown, -1 none fit, else the count
+    if (dev >= 0 && dev < 64) {
+      const int c = cache[dev].load(std::memory_order_relaxed);
+      if (c != 0) return c > 0 ? c : 0;
+    }
     if (setup(dev) != EXL3_OK) return 0;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -521,7 +536,7 @@ struct ClusterKernels {
       cudaGetLastError();
       n = 0;
     }
-    if (dev < 32) cache[dev] = n > 0 ? n : -1;
+    if (dev >= 0 && dev < 64) cache[dev].store(n > 0 ? n : -1, std::memory_order_relaxed);
     return n;
   }
   static int launch(int pass, int clusters, cudaStream_t stream, const float* in, int n, int L,
@@ -541,10 +556,12 @@ struct ClusterKernels {
     cfg.numAttrs = 1;
     if (pass == 1)
       EXL3_CUDA(cudaLaunchKernelEx(&cfg, acs_cluster_kernel<K, C, 1>, in, n, L, cb, ck, ck_pair,
-                                   best_edge, end_state, path_cost));
+                                   best_edge, end_state, path_cost,
+                                   (uint64_t)g_cluster_wait_ns.load(), g_cluster_stop_at.load()));
     else
       EXL3_CUDA(cudaLaunchKernelEx(&cfg, acs_cluster_kernel<K, C, 2>, in, n, L, cb, ck, ck_pair,
-                                   best_edge, end_state, path_cost));
+                                   best_edge, end_state, path_cost,
+                                   (uint64_t)g_cluster_wait_ns.load(), g_cluster_stop_at.load()));
     return EXL3_OK;
   }
 };
@@ -645,6 +662,17 @@ extern "C" int exl3_encoder_set_cluster(int cluster_ctas) {
                    cluster_ctas == 8,
                "cluster size must be 0 (automatic), 1 (off), 2, 4 or 8, got %d", cluster_ctas);
   g_cluster_policy = cluster_ctas;
+  return EXL3_OK;
+}
+
+extern "C" int exl3_encoder_test_cluster_wait(long long wait_limit_ns, int stop_sends_at_step) {
+  EXL3_REQUIRE(wait_limit_ns <= 0 || (wait_limit_ns >= 100000 && wait_limit_ns <= 10000000000ll),
+               "wait limit must be <= 0 (default 2 s) or in [1e5, 1e10] ns, got %lld",
+               wait_limit_ns);
+  EXL3_REQUIRE(stop_sends_at_step == -1 || (stop_sends_at_step >= 1 && stop_sends_at_step <= 254),
+               "stop step must be -1 (off) or in [1, 254], got %d", stop_sends_at_step);
+  g_cluster_wait_ns.store(wait_limit_ns <= 0 ? kClusterWaitNs : (unsigned long long)wait_limit_ns);
+  g_cluster_stop_at.store(stop_sends_at_step);
   return EXL3_OK;
 }
 

@@ -682,17 +682,17 @@ template <int K>
 int pair_encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t* out_packed,
                        float* out_cost, int64_t n, int cb, int L, uint8_t* ws, size_t ws_bytes,
                        cudaStream_t stream) {
-  static int attr_done = 0;  // one bit per device
+  static DeviceBits attr_done;
   int dev = 0;
   EXL3_CUDA(cudaGetDevice(&dev));
-  if (!(dev < 32 && (attr_done & (1 << dev)))) {
+  if (!attr_done.has(dev)) {
     EXL3_CUDA(cudaFuncSetAttribute(acs_pair_kernel<K, 1>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)PSmem<K>::bytes));
     EXL3_CUDA(cudaFuncSetAttribute(acs_pair_kernel<K, 2>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)PSmem<K>::bytes));
-    if (dev < 32) attr_done |= (1 << dev);
+    attr_done.set(dev);
   }
   const size_t per_tile = pair_tile_ws_bytes(K, L);
   const size_t ck_pair = pair_ck_bytes(K, L);
@@ -1026,15 +1026,15 @@ single_tb2_kernel(const float* __restrict__ in, const uint8_t* __restrict__ ck,
 int single_encode(const float* in, float* out_w, int16_t* out_idx, int16_t* out_packed,
                   float* out_cost, int64_t n, int cb, int L, uint8_t* ws, size_t ws_bytes,
                   cudaStream_t stream) {
-  static int attr_done = 0;  // one bit per device
+  static DeviceBits attr_done;
   int dev = 0;
   EXL3_CUDA(cudaGetDevice(&dev));
-  if (!(dev < 32 && (attr_done & (1 << dev)))) {
+  if (!attr_done.has(dev)) {
     EXL3_CUDA(cudaFuncSetAttribute(acs_single_kernel<1>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSingleSmem));
     EXL3_CUDA(cudaFuncSetAttribute(acs_single_kernel<2>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSingleSmem));
-    if (dev < 32) attr_done |= (1 << dev);
+    attr_done.set(dev);
   }
   const size_t per_tile = single_tile_ws_bytes(L);
   const size_t ck_tile = single_ck_bytes(L);

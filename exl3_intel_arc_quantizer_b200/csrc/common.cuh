@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 
@@ -47,6 +48,23 @@ void set_error(const char* fmt, ...);
   } while (0)
 
 int sm_count();  // SMs of the current device (cached per device)
+
+// Per-device flags for one-time host set-up (kernel attributes, constant
+// tables). Several host threads may make first calls at once: each set-up
+// step is idempotent, so running it twice is harmless, and the atomic
+// fetch_or never loses another thread's device bit.
+class DeviceBits {
+ public:
+  bool has(int dev) const {
+    return dev >= 0 && dev < 64 && ((bits_.load(std::memory_order_acquire) >> dev) & 1u);
+  }
+  void set(int dev) {
+    if (dev >= 0 && dev < 64) bits_.fetch_or(uint64_t{1} << dev, std::memory_order_acq_rel);
+  }
+
+ private:
+  std::atomic<uint64_t> bits_{0};
+};
 
 // ---------------------------------------------------------------------------
 // Packed fp16x2 arithmetic with explicit IEEE round-to-nearest-even, so the

@@ -414,13 +414,13 @@ int validate(int K, int cb, int L) {
 
 template <int K>
 int set_smem_attrs() {
-  static int done_mask = 0;  // one bit per device (up to 32)
+  static DeviceBits done;
   int dev = 0;
   EXL3_CUDA(cudaGetDevice(&dev));
-  if (dev < 32 && (done_mask & (1 << dev))) return EXL3_OK;
+  if (done.has(dev)) return EXL3_OK;
   const int bytes = (int)Smem<K>::bytes;
   EXL3_CUDA(cudaFuncSetAttribute(acs_ref_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-  if (dev < 32) done_mask |= (1 << dev);
+  done.set(dev);
   return EXL3_OK;
 }
 

@@ -412,23 +412,22 @@ extern "C" int exl3_hessian_accumulate(float* H, const void* X, int dtype, int64
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   EXL3_REQUIRE(cr == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)cr);
 
-  static uint32_t attr_done[2] = {0u, 0u};  // per dtype, one bit per device
+  static DeviceBits attr_done[2];  // per dtype
   int dev = 0;
   EXL3_CUDA(cudaGetDevice(&dev));
-  const uint32_t bit = dev < 32 ? (1u << dev) : 0u;
   if (dtype == 0) {
-    if (!(attr_done[0] & bit)) {
+    if (!attr_done[0].has(dev)) {
       EXL3_CUDA(cudaFuncSetAttribute(hessian_tma_kernel<0>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-      attr_done[0] |= bit;
+      attr_done[0].set(dev);
     }
     hessian_tma_kernel<0><<<(unsigned)ntiles, kThreads, kSmemBytes, (cudaStream_t)stream>>>(
         map, T, d, H, nbi, nbj, err_flag);
   } else {
-    if (!(attr_done[1] & bit)) {
+    if (!attr_done[1].has(dev)) {
       EXL3_CUDA(cudaFuncSetAttribute(hessian_tma_kernel<1>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-      attr_done[1] |= bit;
+      attr_done[1].set(dev);
     }
     hessian_tma_kernel<1><<<(unsigned)ntiles, kThreads, kSmemBytes, (cudaStream_t)stream>>>(
         map, T, d, H, nbi, nbj, err_flag);

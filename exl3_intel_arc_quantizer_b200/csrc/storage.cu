@@ -158,15 +158,14 @@ constexpr size_t decode_smem_bytes(int K) {
 template <int K, int CB, int F32>
 int launch_decode(const uint16_t* tw, const void* su, const void* sv, float* out, float* w_hat,
                   int64_t tiles_k, int64_t tiles_n, cudaStream_t stream) {
-  static uint32_t attr_done = 0;  // one bit per device
+  static DeviceBits attr_done;
   int dev = 0;
   EXL3_CUDA(cudaGetDevice(&dev));
-  const uint32_t bit = dev < 32 ? (1u << dev) : 0u;
-  if (!(attr_done & bit)) {
+  if (!attr_done.has(dev)) {
     EXL3_CUDA(cudaFuncSetAttribute(decode_weight_kernel<K, CB, F32>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)decode_smem_bytes(K)));
-    attr_done |= bit;
+    attr_done.set(dev);
   }
   const dim3 grid((unsigned)(tiles_n / 8), (unsigned)(tiles_k / 8));
   decode_weight_kernel<K, CB, F32><<<grid, kDecThreads, decode_smem_bytes(K), stream>>>(

@@ -19,6 +19,7 @@ import torch
 import torch.nn as nn
 
 from .hadamard import HAD_DIM, blockwise_preapply_had_l_, blockwise_preapply_had_r_, weight_from_quantized
+from ._ext import encoder_fault_check, raise_on_faults
 from .ldlq import (
     DEFAULT_BLOCK_SIZE,
     DEFAULT_BUF_SIZE_K,
@@ -179,12 +180,14 @@ def quantize_linear_module(name: str, weight: torch.Tensor, H: torch.Tensor, K: 
 
         g_scale_fn = g_scale_fn_from_encoder(tile_encoder)
 
-    Hd = H.to(device=device, dtype=torch.float32)
-    reg = regularize(W, su, sv, H_diag=Hd.diagonal(), skip_g_scale=skip_g_scale,
-                     g_scale_fn=g_scale_fn, had_dim=HAD_DIM)
-    ldl, fact_res = _ldl_of(Hd, block_size)
-    res = _run_ldlq([(reg.weight, ldl.transformed)], tile_encoder, K, buf_size_k)[0]
-    return _finish(name, K, cb, W, Hd, reg, ldl, fact_res, res.weight_q, res.encoded, t0)
+    # raises EncoderFault if an encoder call of this module timed out
+    with encoder_fault_check(device):
+        Hd = H.to(device=device, dtype=torch.float32)
+        reg = regularize(W, su, sv, H_diag=Hd.diagonal(), skip_g_scale=skip_g_scale,
+                         g_scale_fn=g_scale_fn, had_dim=HAD_DIM)
+        ldl, fact_res = _ldl_of(Hd, block_size)
+        res = _run_ldlq([(reg.weight, ldl.transformed)], tile_encoder, K, buf_size_k)[0]
+        return _finish(name, K, cb, W, Hd, reg, ldl, fact_res, res.weight_q, res.encoded, t0)
 
 
 def _run_ldlq(jobs, tile_encoder, K: int, buf_size_k: int):
@@ -231,6 +234,9 @@ def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: i
     if tile_encoder is None:
         tile_encoder = _default_encoder(device, K)
     _check_encoder_k(tile_encoder, K)
+    # encoder CTAs that time out during this call are counted on the device;
+    # the count is checked once the results are final (on every rank)
+    faults = encoder_fault_check(device).__enter__()
 
     Ws, Hds, regs = {}, {}, {}
     for nm in names:
@@ -322,6 +328,7 @@ def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: i
 
     w_hats = {nm: weight_from_quantized(wq[nm], regs[nm].su, regs[nm].sv) for nm in names}
     if group is None:
+        raise_on_faults(faults.delta())
         # the arithmetic of compute_factorization_residual / _module_metrics
         fres = [float(a.item() / max(1e-12, b.item())) for a, b in res_parts]
         out = {}
@@ -340,7 +347,8 @@ def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: i
 
     # sharded: partial sums over this rank's column slice of every module,
     # fp64, one all-reduce; every rank ends with every module's metrics
-    parts = torch.zeros((len(names) * 5 + len(ldls) * 2,), dtype=torch.float64, device=device)
+    parts = torch.zeros((len(names) * 5 + len(ldls) * 2 + 1,), dtype=torch.float64, device=device)
+    parts[-1] = float(faults.delta())      # every rank raises if any rank's encoder faulted
     for idx, nm in enumerate(names):
         k, n = Ws[nm].shape
         c0, c1 = shard_range(n, ws, rank, 128)
@@ -359,6 +367,7 @@ def quantize_modules(modules: Dict[str, Tuple[torch.Tensor, torch.Tensor]], K: i
         parts[base + 2 * li + 1] = b
     dist.all_reduce(parts, group=group)
     v = parts.tolist()
+    raise_on_faults(int(v[-1]))
     fres = [math.sqrt(v[base + 2 * li]) / max(1e-12, math.sqrt(v[base + 2 * li + 1]))
             for li in range(len(ldls))]
     out = {}

@@ -28,7 +28,7 @@ from typing import Callable, List, Optional, Tuple
 import numpy as np
 
 from . import _build
-from ._ext import ext, require_cuda
+from ._ext import encoder_fault_check, ext, require_cuda
 from .memory_policy import MemoryPolicy, MemoryPressureError, capture_snapshot
 from .trellis_format import (
     CB_3INST,
@@ -399,6 +399,13 @@ class XPUTrellisEncoder:
             raise ValueError(f"Unknown traceback_mode {traceback_mode!r}")
         ext()
         dev = require_cuda(f"cuda:{self.device_index}")
+        with encoder_fault_check(dev):   # EncoderFault if a cluster wait timed out
+            return self._encode_batch_detailed(arr, num_tiles, pre_permute, requested_b,
+                                               traceback_mode, allocator_hook, dev)
+
+    def _encode_batch_detailed(self, arr, num_tiles, pre_permute, requested_b, traceback_mode,
+                               allocator_hook, dev) -> BatchEncodingBreakdown:
+        import torch
 
         t_total0 = time.perf_counter()
         perm_np = arr[:, self.perm] if pre_permute else arr

@@ -128,9 +128,12 @@ int exl3_pack_trellis(const int16_t* states, int16_t* packed, int64_t n, int K,
  * the workspace; the scratch is a fixed 64 MiB + 4 KiB __device__ array held
  * by every GPU that loads the library, shared by all calls: at most 16 tiles
  * per call at K=2, L=256 (more at larger K), larger calls return EXL3_EINVAL.
- * The first call on a device resolves the array's address (make it before
- * any stream capture); calls that overlap on the GPU race on the scratch.
- * Allocates nothing (no cudaMalloc/cudaFree).
+ * The first call in a CUDA context resolves the array's address (make it
+ * before any stream capture); under CUDA's default lazy module loading that
+ * first call is also what commits the array on the device, so a host whose
+ * memory pool later claims the rest of HBM makes one call first (or sets
+ * CUDA_MODULE_LOADING=EAGER). Calls that overlap on the GPU race on the
+ * scratch. Calls no cudaMalloc/cudaFree and no allocating library routine.
  */
 int exl3_quantize_tiles_noalloc(const float* in, float* out_w, int16_t* out_idx,
                                 int16_t* out_packed, float* out_cost, int64_t n, int K,
@@ -292,10 +295,23 @@ int exl3_encoder_cluster_capacity(int K, int cluster_ctas, int* clusters);
 /*
  * Number of encoder CTAs that gave up a bounded inter-CTA wait (2 s) since
  * the library loaded, on the current device; nonzero means the outputs of
- * those calls are not valid. Synchronizes the device. No counterpart in the
- * reference.
+ * those calls are not valid. Synchronizes the device. The asynchronous entry
+ * points (exl3_quantize_tiles, exl3_ldlq) cannot return this error; a caller
+ * reads the count before and after its work, as the Python layer drivers do
+ * (they raise EncoderFault when it grew). No counterpart in the reference.
  */
 int exl3_encoder_fault_count(unsigned int* count);
+
+/*
+ * Test hook for the error path above, process-wide. stop_sends_at_step in
+ * [1, 254] makes every CTA of the cluster-split ACS stop sending cost words
+ * from that step of each pass on (all CTAs at the same step, so no message is
+ * left in flight); their next waits then run out after wait_limit_ns
+ * ([1e5, 1e10] ns; <= 0 restores the 2 s default), the CTAs finish without
+ * waiting, the outputs are invalid and the fault count grows. (-1, 0)
+ * restores normal operation. No counterpart in the reference.
+ */
+int exl3_encoder_test_cluster_wait(long long wait_limit_ns, int stop_sends_at_step);
 
 /*
  * Launch timing for benchmarks (off by default). After exl3_timing_begin,

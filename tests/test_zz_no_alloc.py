@@ -65,9 +65,14 @@ def test_no_alloc_entry_point_matches_workspace_entry_point():
         ref = _outputs(n, K, dev)
         got = _outputs(n, K, dev)
         assert with_ws(_ptr(x), *map(_ptr, ref), n, K, cb, 256, _ptr(ws), ws.numel(), stream) == 0
+        torch.cuda.synchronize(dev)
+        free_before = torch.cuda.mem_get_info(dev)[0]
         assert no_alloc(_ptr(x), *map(_ptr, got), n, K, cb, 256, stream) == 0, \
             lib.exl3_last_error()
         torch.cuda.synchronize(dev)
+        if call == 1:
+            # the first call committed the scratch array; later calls take no memory
+            assert torch.cuda.mem_get_info(dev)[0] == free_before
         for a, b in zip(ref, got):
             assert torch.equal(a, b)              # bit-exact, the encoder tests' tolerance
 
