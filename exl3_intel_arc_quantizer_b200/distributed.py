@@ -31,7 +31,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import torch
 import torch.distributed as dist
 
-from .ldlq import LDLQResult, TileEncoder, ldlq
+from .ldlq import LDLQResult, TileEncoder, ldlq, ldlq_native
 
 
 def world() -> Tuple[int, int]:
@@ -108,7 +108,10 @@ def ldlq_column_sharded(weight: torch.Tensor, L: torch.Tensor, encode_tiles: Til
                         buf_size_k: int = 128, group=None, align: int = 128) -> LDLQResult:
     """LDLQ of ``weight`` (k, n) with this rank's ``align``-column slice,
     then an all-gather of the slices: the same ``LDLQResult`` as the
-    single-device loop (column slices never interact)."""
+    single-device loop (column slices never interact). With the B200
+    encoder on CUDA tensors the slice runs the native loop, whose fixed
+    per-output summation order does not depend on the slice's width, so the
+    result equals the one-device native loop bit for bit."""
     ws, rank = dist.get_world_size(group), dist.get_rank(group)
     k, n = weight.shape
     if n % align:
@@ -116,7 +119,12 @@ def ldlq_column_sharded(weight: torch.Tensor, L: torch.Tensor, encode_tiles: Til
     c0, c1 = shard_range(n, ws, rank, align)
     wq = enc = None
     if c1 > c0:
-        local = ldlq(weight[:, c0:c1].contiguous(), L, encode_tiles, buf_size_k=buf_size_k)
+        part = weight[:, c0:c1].contiguous()
+        if getattr(encode_tiles, "native_ldlq", False) and part.is_cuda:
+            local = ldlq_native([(part, L)], encode_tiles.K, getattr(encode_tiles, "cb", 2),
+                                buf_size_k)[0]
+        else:
+            local = ldlq(part, L, encode_tiles, buf_size_k=buf_size_k)
         wq, enc = local.weight_q, local.encoded
     else:  # more ranks than column blocks: this rank contributes nothing
         wq = torch.empty((k, 0), dtype=weight.dtype, device=weight.device)

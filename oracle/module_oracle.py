@@ -198,7 +198,12 @@ class ModuleOracleResult:
 
 
 def quantize_module(weight: torch.Tensor, H: torch.Tensor, K: int, cb: int = 2, buf: int = 128,
-                    encode: Optional[Callable] = None) -> ModuleOracleResult:
+                    encode: Optional[Callable] = None,
+                    ldlq_impl: Optional[Callable] = None) -> ModuleOracleResult:
+    """The module pipeline on the CPU. ``encode`` defaults to the C encoder;
+    ``ldlq_impl(weight, L, encode, buf) -> (weight_q, encoded)`` defaults to
+    :func:`ldlq` (torch CPU products, the reference's arithmetic on this host);
+    ``ldlq_oracle.ldlq_fixed_order`` swaps in the device loop's fixed order."""
     t0 = time.perf_counter()
     kd = H.shape[0]
     W = (weight.T if weight.shape[1] == kd else weight).clone().float()
@@ -207,7 +212,8 @@ def quantize_module(weight: torch.Tensor, H: torch.Tensor, K: int, cb: int = 2, 
     Hr = had_r_(had_l_(H.clone()))
     L, chol, _ = block_ldl(Hr)
     fr = float(torch.linalg.norm(Hr - chol @ chol.T).item() / max(1e-12, torch.linalg.norm(Hr).item()))
-    wq, enc = ldlq(reg.weight, L, encode if encode is not None else c_encoder(K, cb), buf)
+    wq, enc = (ldlq_impl or ldlq)(reg.weight, L, encode if encode is not None else c_encoder(K, cb),
+                                  buf)
     w_hat = weight_from_quantized(wq, reg.su, reg.sv)
     diff = W - w_hat
     mse = float(diff.pow(2).mean().item())

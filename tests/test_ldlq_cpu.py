@@ -220,3 +220,35 @@ def test_ldlq_reproduces_reference_golden_with_oracle_encoder(ldlq_golden, name)
     res = ldlq(w, L, OracleEncoder(K), buf_size_k=buf)
     assert torch.equal(res.weight_q, torch.from_numpy(ldlq_golden[f"{name}/weight_q"]))
     assert torch.equal(res.encoded, torch.from_numpy(ldlq_golden[f"{name}/encoded"]))
+
+
+@pytest.mark.parametrize("name", ["k2_32x128", "k4_64x128"])
+def test_fixed_order_ldlq_oracle_reproduces_reference_golden(ldlq_golden, name):
+    """The fixed-summation-order restatement (the order of the device loop)
+    gives the reference's own LDLQ output bit for bit on both golden cases."""
+    from oracle.ldlq_oracle import ldlq_fixed_order
+    from oracle.module_oracle import c_encoder
+
+    K, k, n, buf, seed = (int(v) for v in ldlq_golden[f"{name}/params"])
+    wq, enc = ldlq_fixed_order(torch.from_numpy(ldlq_golden[f"{name}/weight"]),
+                               torch.from_numpy(ldlq_golden[f"{name}/L"]), c_encoder(K), buf)
+    assert torch.equal(wq, torch.from_numpy(ldlq_golden[f"{name}/weight_q"]))
+    assert torch.equal(enc, torch.from_numpy(ldlq_golden[f"{name}/encoded"]))
+
+
+def test_fixed_order_ldlq_oracle_matches_the_loop_with_exact_products():
+    """With a grid encoder (no trellis), the fixed-order loop and the torch
+    loop differ only by the summation order of their products: the results
+    agree to fp32 rounding, and the fixed order is the same on every call."""
+    from oracle.ldlq_oracle import ldlq_fixed_order
+
+    g = torch.Generator().manual_seed(5)
+    w = torch.randn(256, 256, generator=g)
+    _, L = correlated_L(256, seed=3)
+    enc = GridEncoder(0.5)
+    a = ldlq(w, L, enc, buf_size_k=64)
+    b_q, b_e = ldlq_fixed_order(w, L, enc, buf=64)
+    c_q, _ = ldlq_fixed_order(w, L, enc, buf=64)
+    assert torch.equal(b_q, c_q)
+    assert float((a.weight_q - b_q).abs().max()) <= 0.5 + 1e-6      # at most one grid step
+    assert float((a.weight_q - b_q).norm() / a.weight_q.norm()) < 0.05

@@ -4,11 +4,15 @@ with fewer than 2 GPUs.
 * token-sharded Hessian: per-rank tcgen05 accumulation + NCCL all-reduce
   equals one GPU accumulating every token within the Hessian tolerance
   (max rel 1e-4: the tensor-core accumulation chains are split differently);
-* column-sharded LDLQ with the B200 encoder: close to the single-GPU loop
-  (rel Frobenius <= 1e-2; cuBLAS may round a narrower product differently,
-  which can move a tile's path);
+* column-sharded LDLQ with the B200 encoder: bit-identical to the
+  single-GPU native loop (its fixed per-output summation order does not
+  depend on the slice's width);
 * module-sharded layer quantization: every rank ends with every module's
   result, bit-identical to what its owner computed;
+* convert_layer with one calibration batch per rank (Hessian all-reduce,
+  column-sharded quantization, local re-forward) equals one GPU converting
+  both batches bit for bit: every module's w_hat and trellis states and the
+  next hidden states;
 * column-sharded batched modules: each module's metrics (and each distinct
   Hessian's factorization residual), summed over every rank's column slice
   and all-reduced, match what any rank recomputes whole from its gathered
@@ -49,7 +53,7 @@ def _worker(rank, ws, port, q):
     try:
         from exl3_intel_arc_quantizer_b200 import distributed as xd
         from exl3_intel_arc_quantizer_b200.calibration import hessian_accumulate_
-        from exl3_intel_arc_quantizer_b200.ldlq import block_ldl, ldlq, make_xpu_tile_encoder
+        from exl3_intel_arc_quantizer_b200.ldlq import block_ldl, ldlq_native, make_xpu_tile_encoder
         from exl3_intel_arc_quantizer_b200.layer_quant import quantize_linear_module
 
         # 1. token-sharded Hessian
@@ -71,7 +75,7 @@ def _worker(rank, ws, port, q):
         L = block_ldl(A @ A.T / 32 + 0.1 * torch.eye(256, device=dev)).transformed
         enc = make_xpu_tile_encoder(K=2, device_index=rank)
         sh = xd.ldlq_column_sharded(W, L, enc, buf_size_k=128)
-        ref = ldlq(W, L, enc, buf_size_k=128)
+        ref = ldlq_native([(W, L)], K=2, buf_size_k=128)[0]
         out["ldlq_rel"] = float(torch.linalg.norm(sh.weight_q - ref.weight_q)
                                 / torch.linalg.norm(ref.weight_q))
         out["ldlq_same"] = float((sh.encoded == ref.encoded).all(-1).float().mean())
@@ -114,6 +118,36 @@ def _worker(rank, ws, port, q):
             redo[2] = mt.tile_distortion   # needs weight_q, which results do not keep
             again[m] = tuple(redo) + (_ldl_of(mods[m][1].float(), 16)[1],)
         out.update(mod_metrics=met, mod_again=again)
+
+        # 5. the same modules on one GPU: sharded == unsharded, bit for bit
+        one = quantize_modules(mods, K=2, tile_encoder=enc)
+        out["qm_equal"] = {m: bool(torch.equal(qm[m].w_hat, one[m].w_hat)
+                                   and torch.equal(qm[m].encoded, one[m].encoded)) for m in mods}
+
+        # 6. convert_layer: one calibration batch per rank (Hessian all-reduce
+        #    of the two partial sums), column-sharded quantization, local
+        #    re-forward; against one GPU converting both batches
+        import copy
+
+        from exl3_intel_arc_quantizer_b200.calibration import TransformerDecoderLayer
+        from exl3_intel_arc_quantizer_b200.converter import convert_layer
+
+        torch.manual_seed(0)
+        layer = TransformerDecoderLayer(256, 512, 4, 2)
+        for prm in layer.parameters():
+            if prm.dim() == 2:
+                torch.nn.init.normal_(prm, std=0.02)
+        layer1 = copy.deepcopy(layer)
+        gh = torch.Generator(device="cpu").manual_seed(4)
+        hs = [torch.randn(2, 64, 256, generator=gh).half().to(dev) for _ in range(ws)]
+        res, nxt, tm = convert_layer(layer, [hs[rank]], K=2, device=dev, group=dist.group.WORLD)
+        full, nxt1, _ = convert_layer(layer1, hs, K=2, device=dev)
+        out["cl_equal"] = {m: bool(torch.equal(res[m].w_hat, full[m].w_hat)
+                                   and torch.equal(res[m].encoded, full[m].encoded)) for m in res}
+        out["cl_next_equal"] = bool(torch.equal(nxt[0], nxt1[rank]))
+        out["cl_metric"] = {m: (res[m].metrics.relative_frobenius_error,
+                                full[m].metrics.relative_frobenius_error) for m in res}
+        out["cl_tokens"] = tm.local_tokens
         torch.cuda.synchronize()
     except Exception as e:  # pragma: no cover
         out = e
@@ -139,7 +173,8 @@ def test_two_gpu_sharded_paths():
     print(a, b)
     assert a["count"] == b["count"] == 8192
     assert a["hess_rel"] <= 1e-4 and b["hess_rel"] <= 1e-4
-    assert a["ldlq_rel"] <= 1e-2 and b["ldlq_rel"] == a["ldlq_rel"]
+    assert a["ldlq_rel"] == 0.0 and b["ldlq_rel"] == 0.0
+    assert a["ldlq_same"] == 1.0 and b["ldlq_same"] == 1.0
     assert a["owners"] == b["owners"] and set(a["owners"].values()) == {0, 1}
     assert a["digest"] == b["digest"]
     assert all(v == 0.0 for v in list(a["local"].values()) + list(b["local"].values()))
@@ -152,3 +187,13 @@ def test_two_gpu_sharded_paths():
             # the factorization residual measures fp32 rounding of L L^T itself,
             # so a column-sliced product only has to agree in size
             assert vals[5] <= 1e-5 and again[5] <= 1e-5 and 0.5 <= vals[5] / again[5] <= 2.0
+    for r in (a, b):
+        assert all(r["qm_equal"].values()), r["qm_equal"]
+        # convert_layer over 2 GPUs == one GPU: identical Hessians (each rank's
+        # one batch is one exact partial sum; the all-reduce adds the two),
+        # identical quantized modules, identical next hidden states
+        assert r["cl_tokens"] == 128
+        assert all(r["cl_equal"].values()), r["cl_equal"]
+        assert r["cl_next_equal"]
+        for m, (got, want) in r["cl_metric"].items():
+            assert abs(got - want) <= 1e-4 * want, (m, got, want)
