@@ -53,6 +53,7 @@ def parse():
     ap.add_argument("--no-layer", action="store_true")
     ap.add_argument("--no-decoder-layer", action="store_true")
     ap.add_argument("--no-k-sweep", action="store_true")
+    ap.add_argument("--no-hessian", action="store_true")
     ap.add_argument("--model-only", action="store_true",
                     help="convert the config-5 model (32 decoder layers, K=4) on all ranks and exit")
     ap.add_argument("--model-layers", type=int, default=32)
@@ -191,13 +192,114 @@ def cpu_baseline(K, threads=None, seconds_target=12.0, impl_tag="port"):
                       f"reference encoder (oracle/trellis_oracle.c), {dt:.1f}s"}
 
 
+_REF_ENCODER = None
+
+
+def _ref_worker_init(import_path, K):
+    """Pool worker set-up: the reference's own encoder from the byte-compiled
+    reference package (oracle/_ref)."""
+    global _REF_ENCODER
+    sys.path.insert(0, import_path)
+    from exl3_quant.reference_encoder import ReferenceTrellisEncoder
+
+    _REF_ENCODER = ReferenceTrellisEncoder(K=K, cb=2)
+
+
+def _ref_worker_encode(tile):
+    return _REF_ENCODER.encode_tile(tile, pre_permute=False).end_state
+
+
+class ReferenceEncoderPool:
+    """The reference's CPU encoder (ReferenceTrellisEncoder.encode_tile,
+    exl3_quant/reference_encoder.py:253-324, its NumPy code byte-compiled into
+    oracle/_ref) in one spawned process per host core with OMP_NUM_THREADS=1,
+    one tile per task. None when oracle/_ref was not built."""
+
+    def __new__(cls, K, procs=None):
+        from oracle import build_ref
+
+        if not build_ref.available():
+            return None
+        return super().__new__(cls)
+
+    def __init__(self, K, procs=None):
+        import multiprocessing as mp
+
+        from oracle import build_ref
+
+        self.procs = procs or os.cpu_count() or 1
+        old = os.environ.get("OMP_NUM_THREADS")
+        os.environ["OMP_NUM_THREADS"] = "1"          # inherited by the spawned workers
+        try:
+            self.pool = mp.get_context("spawn").Pool(
+                self.procs, initializer=_ref_worker_init, initargs=(build_ref.import_path(), K))
+        finally:
+            if old is None:
+                os.environ.pop("OMP_NUM_THREADS", None)
+            else:
+                os.environ["OMP_NUM_THREADS"] = old
+
+    def encode(self, tiles):
+        return self.pool.map(_ref_worker_encode, list(tiles), chunksize=1)
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+
+
+def reference_cpu_baseline(K, tiles_per_core=2):
+    """The reference's own CPU encoder on every host core (the line the
+    reference's CPU path gives), on a bounded sample of the workload."""
+    pool = ReferenceEncoderPool(K)
+    if pool is None:
+        return None
+    try:
+        pool.encode(make_tiles(pool.procs, 98, "cpu").numpy())       # imports, tables
+        n = pool.procs * tiles_per_core
+        tiles = make_tiles(n, 7, "cpu").numpy()
+        t0 = time.perf_counter()
+        pool.encode(tiles)
+        dt = time.perf_counter() - t0
+    finally:
+        pool.close()
+    return {"value": n / dt, "unit": "tiles/s", "cores": pool.procs, "kind": "reference",
+            "sample": f"{n} tiles of the config-2 distribution, K={K}: the reference's "
+                      "ReferenceTrellisEncoder.encode_tile (reference_encoder.py:253-324, "
+                      f"byte-compiled), {pool.procs} spawned processes, OMP_NUM_THREADS=1, "
+                      f"{dt:.1f}s"}
+
+
 def run_reference(args):
-    """Reference arm: the reference encoder's algorithm on the host cores
-    (C restatement in oracle/, every host thread), bounded samples."""
+    """Reference arm: the reference's own CPU encoder on every host core
+    (ReferenceEncoderPool); the C restatement of oracle/ only when the
+    compiled reference package is absent. Bounded samples per step."""
     world, rank, local = dist_env()
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
+    pool = ReferenceEncoderPool(args.K)
+    if pool is not None:
+        try:
+            per_step = pool.procs
+            tiles = make_tiles(per_step, 7, "cpu").numpy()
+            for _ in range(args.warmup):
+                pool.encode(tiles)
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                pool.encode(tiles)
+            dt = time.perf_counter() - t0
+        finally:
+            pool.close()
+        value = per_step * args.steps / dt
+        base = {"value": value, "unit": "tiles/s", "cores": pool.procs, "kind": "reference",
+                "sample": f"{per_step} tiles/step x {args.steps} steps: the reference's "
+                          "ReferenceTrellisEncoder.encode_tile (reference_encoder.py:253-324, "
+                          "byte-compiled from its sources), one spawned process per core, "
+                          "OMP_NUM_THREADS=1"}
+        line = _reference_line(args, value, dt, per_step, base)
+        line["cpu_baseline_port"] = cpu_baseline(args.K, seconds_target=6.0)
+        print(json.dumps(line), flush=True)
+        return 0
     from oracle.trellis_oracle import COracle
 
     o = COracle(args.K, 2)
@@ -210,23 +312,25 @@ def run_reference(args):
         r = o.encode_batch(tiles, threads=threads)
     dt = time.perf_counter() - t0
     value = per_step * args.steps / dt
-    line = {
+    base = {"value": value, "unit": "tiles/s", "cores": int(r["threads"]), "kind": "port",
+            "sample": f"{per_step} tiles/step x {args.steps} steps, C restatement of the "
+                      "reference encoder (the compiled reference package is absent)"}
+    print(json.dumps(_reference_line(args, value, dt, per_step, base)), flush=True)
+    return 0
+
+
+def _reference_line(args, value, dt, per_step, cpu):
+    return {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tiles/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
         "config": {"workload": f"encoder sweep (config 2) K={args.K} mul1 L=256, "
                                f"{per_step} tiles per step (bounded sample)", "K": args.K},
-        "cpu_baseline": {"value": value, "unit": "tiles/s", "cores": int(r["threads"]),
-                         "kind": "port",
-                         "sample": f"{per_step} tiles/step x {args.steps} steps, C restatement "
-                                   "of the reference encoder (reference is Python/SYCL; its "
-                                   "checkout is not on the GPU host)"},
+        "cpu_baseline": cpu,
         "e2e": {"value": value, "unit": "tiles/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
-    return 0
 
 
 def layer_config3(device, seed=0):
@@ -888,9 +992,10 @@ def run_b200(args):
 
     # the headline encoder's workspace is not used by the sections below
     enc.arena.release()
-    cpu = None
+    cpu = cpu_port = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(K)
+        cpu_port = cpu_baseline(K)
+        cpu = reference_cpu_baseline(K) or cpu_port
     small = run_small_calls(device) if rank == 0 else None
     storage = run_storage(device) if rank == 0 else None
     layer = layer2 = None
@@ -907,6 +1012,9 @@ def run_b200(args):
     declayer = None
     if not args.no_decoder_layer:
         declayer = [run_decoder_layer(device, world, rank, k) for k in (2, 4)]
+    hessian = None
+    if rank == 0 and not args.no_hessian:
+        hessian = run_hessian(device)
 
     if rank == 0:
         line = {
@@ -930,17 +1038,50 @@ def run_b200(args):
             "small_calls": small,
             "storage": storage,
             "roofline": roofline,
+            "hessian": hessian,
             "cpu_baseline": cpu,
+            "cpu_baseline_port": cpu_port,
             "e2e": e2e,
             "gpu_launches": int(total_n.value),
             "clocks": clk,
         }
+        # last key: a short digest of the sections above, so that the end of
+        # the line (what a log tail keeps) carries the layer-level numbers
+        line["summary"] = summarize(line)
         print(json.dumps(line), flush=True)
     enc.arena.release()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def summarize(line):
+    def r(v, nd=4):
+        return None if v is None else float(f"{v:.{nd}g}")
+
+    out = {"encoder_k2_tiles_per_s": r(line["value"], 6),
+           "e2e_tiles_per_s": r((line.get("e2e") or {}).get("value"), 6),
+           "acs_roofline_frac": r((line.get("roofline") or {}).get("frac"), 3)}
+    if line.get("layer"):
+        out["config3_layer_k4_s"] = r(line["layer"]["seconds_per_layer"])
+    if line.get("layer_k2_gss"):
+        out["config3_layer_k2_gss_s"] = r(line["layer_k2_gss"]["seconds_per_layer"])
+    if line.get("layer_sharded"):
+        out["config3_layer_sharded_s"] = r(line["layer_sharded"].get("seconds_per_layer"))
+    for d in line.get("decoder_layer") or []:
+        out[f"config4_layer_k{d['K']}_s"] = r(d["seconds_per_layer"])
+        out[f"config4_layer_k{d['K']}_phases_s"] = {k: r(v, 3) for k, v in d["phases_s"].items()}
+    for g in (line.get("hessian") or {}).get("groups", []):
+        out[f"hessian_d{g['d']}_ms"] = r(g["ms"])
+        out[f"hessian_d{g['d']}_frac_bf16"] = r(g["frac_mma_of_measured_bf16"], 3)
+    for key, tag in (("cpu_baseline", "cpu_reference"), ("cpu_baseline_port", "cpu_port")):
+        c = line.get(key)
+        if c:
+            out[f"{tag}_tiles_per_s"] = r(c["value"])
+            out[f"{tag}_cores"] = c["cores"]
+    out["n_gpus"] = line["n_gpus"]
+    return out
 
 
 def main():

@@ -122,13 +122,35 @@ def regularize(W: torch.Tensor, H_diag: torch.Tensor) -> Regularized:
     return Regularized(work, su, sv, apply_out)
 
 
+def blocked_cholesky(A: torch.Tensor, nb: int = 128) -> torch.Tensor:
+    """Right-looking blocked Cholesky in fp32 with torch CPU ops: each
+    diagonal block by ``torch.linalg.cholesky``, the panel under it by a
+    triangular solve, the trailing matrix by one GEMM update. A valid fp32
+    factorization whose rounding differs from a single LAPACK call; raises
+    ``torch.linalg.LinAlgError`` like it on a non-positive pivot."""
+    n = A.shape[0]
+    work = A.clone()
+    for j in range(0, n, nb):
+        e = min(j + nb, n)
+        ljj = torch.linalg.cholesky(work[j:e, j:e])
+        work[j:e, j:e] = ljj
+        if e < n:
+            panel = torch.linalg.solve_triangular(ljj, work[e:, j:e].T.contiguous(),
+                                                  upper=False).T
+            work[e:, j:e] = panel
+            work[e:, e:] -= panel @ panel.T
+    return torch.tril(work)
+
+
 def block_ldl(H: torch.Tensor, block: int = 16, sigma: float = 0.025,
-              retries: int = 10) -> Tuple[torch.Tensor, torch.Tensor, int]:
-    """(transformed L, Cholesky factor, retries used)."""
+              retries: int = 10, cholesky: Optional[Callable] = None
+              ) -> Tuple[torch.Tensor, torch.Tensor, int]:
+    """(transformed L, Cholesky factor, retries used). ``cholesky`` defaults
+    to ``torch.linalg.cholesky`` (the reference's call)."""
     work = H.clone()
     for attempt in range(retries + 1):
         try:
-            chol = torch.linalg.cholesky(work)
+            chol = (cholesky or torch.linalg.cholesky)(work)
             break
         except torch.linalg.LinAlgError:
             if attempt == retries:
@@ -199,18 +221,20 @@ class ModuleOracleResult:
 
 def quantize_module(weight: torch.Tensor, H: torch.Tensor, K: int, cb: int = 2, buf: int = 128,
                     encode: Optional[Callable] = None,
-                    ldlq_impl: Optional[Callable] = None) -> ModuleOracleResult:
+                    ldlq_impl: Optional[Callable] = None,
+                    cholesky: Optional[Callable] = None) -> ModuleOracleResult:
     """The module pipeline on the CPU. ``encode`` defaults to the C encoder;
     ``ldlq_impl(weight, L, encode, buf) -> (weight_q, encoded)`` defaults to
     :func:`ldlq` (torch CPU products, the reference's arithmetic on this host);
-    ``ldlq_oracle.ldlq_fixed_order`` swaps in the device loop's fixed order."""
+    ``ldlq_oracle.ldlq_fixed_order`` swaps in the device loop's fixed order;
+    ``cholesky`` (e.g. :func:`blocked_cholesky`) replaces the LAPACK call."""
     t0 = time.perf_counter()
     kd = H.shape[0]
     W = (weight.T if weight.shape[1] == kd else weight).clone().float()
     H = H.float()
     reg = regularize(W, H.diagonal())
     Hr = had_r_(had_l_(H.clone()))
-    L, chol, _ = block_ldl(Hr)
+    L, chol, _ = block_ldl(Hr, cholesky=cholesky)
     fr = float(torch.linalg.norm(Hr - chol @ chol.T).item() / max(1e-12, torch.linalg.norm(Hr).item()))
     wq, enc = (ldlq_impl or ldlq)(reg.weight, L, encode if encode is not None else c_encoder(K, cb),
                                   buf)

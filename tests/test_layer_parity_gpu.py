@@ -14,14 +14,17 @@ the same 16 columns. The parity bar therefore has three parts:
   bit for bit (weight_q and every trellis state);
 * every floating-point stage against the reference's arithmetic on the CPU
   (``oracle/module_oracle.py``, torch CPU ops): relative Frobenius error
-  <= 1e-3 (north_star's floating-point bar; the measured values are printed
-  and gated tighter);
-* the whole module against the reference pipeline run on the CPU with the
-  B200 encoder as its callback, which is the reference's own result bit for
-  bit, since that encoder is pinned bit-exact to the reference's. The
-  distance of w_hat is gated against the distance between two valid CPU runs
-  of the reference's algorithm that differ only in the summation order of the
-  LDLQ products, and the quality metrics must agree.
+  <= 1e-3 (north_star's floating-point bar) for the Cholesky factor and L
+  (measured 6e-5 and 1.3e-4), <= 1e-5 for the rest (measured ~3e-7);
+* bit-exact mode: the device loop fed the reference's own float-stage
+  outputs reproduces the reference's CPU run (with the B200 encoder as its
+  callback, which is the reference's own result bit for bit since that
+  encoder is pinned bit-exact to the reference's): every trellis state, and
+  w_hat to 1e-6;
+* device-native mode: the whole module on the device against that reference
+  run. Its w_hat distance is gated against a second valid CPU run of the
+  reference's algorithm that differs only in its fp32 Cholesky, and the
+  quality metrics must agree within 1%.
 
 Lines starting with ``PARITY`` print the measured values.
 """
@@ -141,8 +144,9 @@ def test_float_stages_match_reference_arithmetic_at_config3_size(config3, stages
     w_ref = mo.weight_from_quantized(nat.weight_q.cpu(), reg.su.cpu(), reg.sv.cpu())
     rels["w_hat from weight_q"] = _rel(w_dev, w_ref)
     print("PARITY float stages config3: " + ", ".join(f"{k} {v:.3e}" for k, v in rels.items()))
+    gates = {"cholesky": 1e-3, "L": 1e-3}     # LAPACK vs cuSOLVER rounding, amplified by cond(H)
     for name, v in rels.items():
-        assert v <= 1e-3, (name, v)
+        assert v <= gates.get(name, 1e-5), (name, v)
 
 
 def _metrics_line(tag, m):
@@ -166,22 +170,50 @@ def test_module_on_config3_corner_matches_cpu_oracle(config3):
           m.normalized_proxy_loss)
     print(f"PARITY corner512 K={K}: w_hat rel frob {rel:.3e}, identical tiles {same:.4f}; "
           + _metrics_line("device", dm) + "; " + _metrics_line("oracle", ref.metrics))
-    assert abs(m.relative_frobenius_error - ref.metrics[1]) <= 0.02 * ref.metrics[1]
-    assert rel <= 0.2
+    assert abs(m.relative_frobenius_error - ref.metrics[1]) <= 0.01 * ref.metrics[1]
+    assert abs(m.proxy_loss - ref.metrics[3]) <= 0.01 * abs(ref.metrics[3])
+    assert rel <= 0.05 and same >= 0.9
 
 
-def test_module_at_config3_size_against_reference_pipeline(config3):
-    """The full config-3 module on the device against the reference's own
-    pipeline on the CPU (torch CPU float stages and LDLQ products, the B200
-    encoder as callback). The noise floor is a second valid CPU run of the
-    same algorithm whose LDLQ products use the device loop's fixed summation
-    order instead of the host BLAS's."""
+@pytest.fixture(scope="module")
+def reference_run(config3):
+    """The reference's pipeline on the CPU (torch CPU float stages and LDLQ
+    products) with the B200 encoder as its tile callback: the reference's own
+    result on this host, bit for bit."""
     W, _, H = config3
-    enc = _device_encoder_callback(K)
+    return mo.quantize_module(W.cpu(), H.cpu(), K=K, buf=128, encode=_device_encoder_callback(K))
+
+
+def test_bit_exact_mode_at_config3_size(reference_run):
+    """The device LDLQ loop and reconstruction, fed the reference's own
+    regularized weight, scales and block-LDL factor, reproduce the
+    reference's trellis states bit for bit and its w_hat to fp32 rounding of
+    the reconstruction, over the full 4096 x 4096 matrix."""
+    ref = reference_run
+    nat = ldlq_native([(ref.reg_weight.to(DEV), ref.L.to(DEV))], K=K, buf_size_k=128)[0]
+    w_hat = weight_from_quantized(nat.weight_q, ref.su.to(DEV), ref.sv.to(DEV))
+    same = _same_tiles(nat.encoded, ref.encoded)
+    rel = _rel(w_hat, ref.w_hat)
+    print(f"PARITY bit-exact mode config3 K={K}: identical tiles {same:.6f}, w_hat rel frob "
+          f"{rel:.3e}")
+    assert torch.equal(nat.encoded.cpu(), ref.encoded)
+    assert rel <= 1e-6
+
+
+def test_module_at_config3_size_against_reference_pipeline(config3, reference_run):
+    """The device-native module (its own regularize, FWHT, cuSOLVER Cholesky,
+    native LDLQ) against the reference's CPU run. The float stages differ at
+    fp32 rounding (the Cholesky factor by ~1e-4), and the encoder's argmin
+    turns that into different, equally good trellis paths. The noise floor is
+    a second valid CPU run of the reference's algorithm that differs only in
+    its fp32 Cholesky (blocked, torch ops, instead of one LAPACK call): the
+    device's w_hat must be no farther from the reference than that run is,
+    and the quality metrics must agree within 1%."""
+    W, _, H = config3
+    ref = reference_run
     dev = quantize_linear_module("o_proj", W, H, K=K, skip_g_scale=True, buf_size_k=128)
-    ref = mo.quantize_module(W.cpu(), H.cpu(), K=K, buf=128, encode=enc)
-    alt = mo.quantize_module(W.cpu(), H.cpu(), K=K, buf=128, encode=enc,
-                             ldlq_impl=ldlq_fixed_order)
+    alt = mo.quantize_module(W.cpu(), H.cpu(), K=K, buf=128, encode=_device_encoder_callback(K),
+                             cholesky=mo.blocked_cholesky)
     rel_dev = _rel(dev.w_hat, ref.w_hat)
     rel_alt = _rel(alt.w_hat, ref.w_hat)
     same_dev = _same_tiles(dev.encoded, ref.encoded)
@@ -190,9 +222,11 @@ def test_module_at_config3_size_against_reference_pipeline(config3):
     dm = (m.mse, m.relative_frobenius_error, m.tile_distortion, m.proxy_loss,
           m.normalized_proxy_loss)
     print(f"PARITY config3 module K={K}: device vs reference w_hat rel frob {rel_dev:.3e} "
-          f"(identical tiles {same_dev:.4f}); noise floor (CPU, fixed-order products) "
-          f"{rel_alt:.3e} (identical tiles {same_alt:.4f}); "
+          f"(identical tiles {same_dev:.4f}); second CPU Cholesky vs reference {rel_alt:.3e} "
+          f"(identical tiles {same_alt:.4f}); "
           + _metrics_line("device", dm) + "; " + _metrics_line("reference", ref.metrics)
-          + "; " + _metrics_line("fixed-order", alt.metrics))
-    assert abs(m.relative_frobenius_error - ref.metrics[1]) <= 0.01 * ref.metrics[1]
-    assert rel_dev <= 2.0 * rel_alt + 1e-3
+          + "; " + _metrics_line("blocked-cholesky", alt.metrics))
+    assert rel_dev <= 1.5 * rel_alt + 0.01
+    for got, want in ((m.relative_frobenius_error, ref.metrics[1]), (m.mse, ref.metrics[0]),
+                      (m.proxy_loss, ref.metrics[3])):
+        assert abs(got - want) <= 0.01 * abs(want), (got, want)
