@@ -195,11 +195,13 @@ def cpu_baseline(K, threads=None, seconds_target=12.0, impl_tag="port"):
 _REF_ENCODER = None
 
 
-def _ref_worker_init(import_path, K):
+def _ref_worker_init(K):
     """Pool worker set-up: the reference's own encoder from the byte-compiled
     reference package (oracle/_ref)."""
     global _REF_ENCODER
-    sys.path.insert(0, import_path)
+    from oracle import build_ref
+
+    build_ref.enable()
     from exl3_quant.reference_encoder import ReferenceTrellisEncoder
 
     _REF_ENCODER = ReferenceTrellisEncoder(K=K, cb=2)
@@ -232,7 +234,7 @@ class ReferenceEncoderPool:
         os.environ["OMP_NUM_THREADS"] = "1"          # inherited by the spawned workers
         try:
             self.pool = mp.get_context("spawn").Pool(
-                self.procs, initializer=_ref_worker_init, initargs=(build_ref.import_path(), K))
+                self.procs, initializer=_ref_worker_init, initargs=(K,))
         finally:
             if old is None:
                 os.environ.pop("OMP_NUM_THREADS", None)

@@ -33,7 +33,7 @@ LIB_DIR = PKG_DIR / "_lib"
 LIB_NAME = "libexl3k.so"
 EXT_NAME = "exl3_b200_ext"
 
-CU_SOURCES = ["abi.cu", "encoder.cu", "acs_pair.cu", "acs_cluster.cu", "noalloc.cu", "linalg.cu", "hessian.cu", "storage.cu", "ldlq.cu"]
+CU_SOURCES = ["abi.cu", "encoder.cu", "acs_pair.cu", "acs_cluster.cu", "noalloc.cu", "linalg.cu", "hessian.cu", "storage.cu", "ldlq.cu", "regularize.cu"]
 EXT_SOURCES = ["torch_ext.cpp", "torch_ext_linalg.cpp"]
 
 NVCC_FLAGS = [

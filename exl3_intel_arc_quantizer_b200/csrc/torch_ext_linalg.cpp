@@ -3,6 +3,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstring>
 #include <vector>
 
 #include "../../include/exl3k.h"
@@ -151,7 +152,82 @@ void ldlq_(std::vector<at::Tensor> W, std::vector<at::Tensor> L, std::vector<at:
         "ldlq");
 }
 
+// Regularization on the device; returns (apply_out_scales, zeros, skew, mean)
+// read back once (the only host synchronisation of the stage).
+std::vector<double> regularize_(at::Tensor W, at::Tensor su_in, at::Tensor sv_in,
+                                c10::optional<at::Tensor> h_diag_src, int64_t force_out_scales,
+                                bool q_fallback, at::Tensor work, at::Tensor su_out,
+                                at::Tensor sv_out, at::Tensor out_scales, at::Tensor in_scales) {
+  check_f32_cuda_2d(W, "weight");
+  check_f32_cuda_2d(work, "work");
+  const int64_t k = W.size(0), n = W.size(1);
+  TORCH_CHECK(work.size(0) == k && work.size(1) == n, "work must match the weight's shape");
+  for (const auto* t : {&su_in, &sv_in, &su_out, &sv_out, &out_scales, &in_scales}) {
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->scalar_type() == at::kFloat,
+                "scales must be contiguous float32 CUDA tensors");
+    TORCH_CHECK(t->device() == W.device(), "all tensors must be on the weight's device");
+  }
+  TORCH_CHECK(su_in.numel() == k && su_out.numel() == k && in_scales.numel() == k,
+              "su / in_scales must have ", k, " elements");
+  TORCH_CHECK(sv_in.numel() == n && sv_out.numel() == n && out_scales.numel() == n,
+              "sv / out_scales must have ", n, " elements");
+  const float* hd = nullptr;
+  int64_t stride = 1;
+  at::Tensor hdt;
+  if (h_diag_src.has_value() && h_diag_src->defined()) {
+    hdt = *h_diag_src;
+    TORCH_CHECK(hdt.is_cuda() && hdt.scalar_type() == at::kFloat && hdt.device() == W.device(),
+                "H_diag must be a float32 tensor on the weight's device");
+    TORCH_CHECK(hdt.dim() == 1 && hdt.size(0) == k, "H_diag must have ", k, " elements");
+    stride = hdt.stride(0);
+    hd = hdt.data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(W.device());
+  const size_t bytes = exl3_regularize_ws_bytes(k, n);
+  TORCH_CHECK(bytes > 0, "both dimensions must be divisible by 128, got (", k, ", ", n, ")");
+  auto ws = at::empty({(int64_t)bytes}, W.options().dtype(at::kByte));
+  auto info = at::empty({4}, W.options().dtype(at::kInt));
+  check(exl3_regularize(W.data_ptr<float>(), su_in.data_ptr<float>(), sv_in.data_ptr<float>(), hd,
+                        stride, (int)force_out_scales, q_fallback ? 1 : 0, work.data_ptr<float>(),
+                        su_out.data_ptr<float>(), sv_out.data_ptr<float>(),
+                        out_scales.data_ptr<float>(), in_scales.data_ptr<float>(),
+                        info.data_ptr(), k, n, ws.data_ptr(), bytes, cur_stream(W)),
+        "regularize");
+  auto host = info.cpu();
+  const int32_t* iv = host.data_ptr<int32_t>();
+  float skew, mean;
+  std::memcpy(&skew, iv + 2, 4);
+  std::memcpy(&mean, iv + 3, 4);
+  return {(double)iv[0], (double)iv[1], (double)skew, (double)mean};
+}
+
+void block_ldl_fold(at::Tensor chol, at::Tensor L, c10::optional<at::Tensor> inverses) {
+  check_f32_cuda_2d(chol, "chol");
+  check_f32_cuda_2d(L, "L");
+  const int64_t n = chol.size(0);
+  TORCH_CHECK(chol.size(1) == n && L.size(0) == n && L.size(1) == n, "square (n, n) matrices");
+  TORCH_CHECK(L.device() == chol.device(), "chol and L must be on the same device");
+  float* inv = nullptr;
+  if (inverses.has_value() && inverses->defined()) {
+    TORCH_CHECK(inverses->is_cuda() && inverses->is_contiguous() &&
+                    inverses->scalar_type() == at::kFloat && inverses->numel() == n * 16,
+                "inverses must be a contiguous float32 (n/16, 16, 16) CUDA tensor");
+    inv = inverses->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(chol.device());
+  check(exl3_block_ldl_fold(chol.data_ptr<float>(), L.data_ptr<float>(), inv, n, cur_stream(chol)),
+        "block_ldl_fold");
+}
+
 void register_linalg_ops(pybind11::module& m) {
+  m.def("regularize_", &regularize_, pybind11::arg("W"), pybind11::arg("su_in"),
+        pybind11::arg("sv_in"), pybind11::arg("H_diag"), pybind11::arg("force_out_scales"),
+        pybind11::arg("q_fallback"), pybind11::arg("work"), pybind11::arg("su_out"),
+        pybind11::arg("sv_out"), pybind11::arg("out_scales"), pybind11::arg("in_scales"),
+        "Weight regularization on the device; returns (apply_out_scales, zeros, skew, mean)");
+  m.def("block_ldl_fold", &block_ldl_fold, pybind11::arg("chol"), pybind11::arg("L"),
+        pybind11::arg("inverses") = pybind11::none(),
+        "L = C D^-1 per 16-column block with identity diagonal blocks");
   m.def("ldlq_", &ldlq_, pybind11::arg("W"), pybind11::arg("L"), pybind11::arg("W_q"),
         pybind11::arg("encoded"), pybind11::arg("K"), pybind11::arg("cb"), pybind11::arg("buf"),
         "LDLQ of several matrices in lockstep with the B200 encoder");

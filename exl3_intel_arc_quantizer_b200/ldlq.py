@@ -7,8 +7,10 @@ Same API and semantics as the reference ``exl3_quant/ldlq.py``
   attempt undamped; on failure ``diag += 2 * sigma_reg * mean(diag)``, up to
   ``max_retries`` times), 16x16 diagonal-block inverses folded into their
   block columns, identity diagonal blocks. On CUDA the factorization is
-  cuSOLVER (``torch.linalg.cholesky_ex``) and the fold is one batched
-  inverse plus one batched product.
+  cuSOLVER (``torch.linalg.cholesky_ex``) and the fold one pass of the
+  libexl3k kernel (``exl3_block_ldl_fold``: forward-substitution inverses of
+  the 16x16 diagonal blocks and the block-column products); host tensors
+  take the reference's op sequence (batched inverse, batched product).
 * :func:`ldlq` — spans of ``buf_size_k`` rows bottom-up, 16-row blocks
   bottom-up inside a span; each block's target rows get the compensation
   ``L[i+bj:j, i+bi:i+bj]^T @ err_below`` added, are cut into 16x16 tiles in
@@ -80,6 +82,15 @@ def block_ldl(H: torch.Tensor, block_size: int = DEFAULT_BLOCK_SIZE,
                 f"cholesky failed after {max_retries} damping retries (info={int(info.item())})")
         work.diagonal().add_(2.0 * sigma_reg * work.diagonal().mean())
     m = n // block_size
+    if H.is_cuda and block_size == 16:
+        # the fold on the device (exl3_block_ldl_fold): one pass over the factor
+        from ._ext import ext
+
+        chol = chol.contiguous()
+        transformed = torch.empty_like(chol)
+        inverses = torch.empty((m, 16, 16), dtype=H.dtype, device=H.device)
+        ext().block_ldl_fold(chol, transformed, inverses)
+        return BlockLDLResult(transformed, chol, inverses, retries, retries > 0, n, block_size)
     cb = chol.reshape(m, block_size, m, block_size)
     diag_blocks = torch.diagonal(cb, dim1=0, dim2=2).permute(2, 0, 1).contiguous()
     inverses = torch.linalg.inv(diag_blocks)

@@ -5,8 +5,11 @@ scales into ``sv`` (optional, skew heuristic on the Hessian diagonal),
 ``W /= sv``, right Hadamard, input-channel RMS scales into
 ``su = su * rms / (-1.24371088) + 1e-10``, ``W /= su``, left Hadamard, optional
 global scale. Decoding reverses it (``hadamard.weight_from_quantized``).
-The reductions and scalings are torch ops on the device; the rotations are
-the libexl3k Walsh-Hadamard kernels.
+Everything but the optional global scale runs in the libexl3k kernels
+(``exl3_regularize``: skew heuristic, block RMS of columns and rows, the
+scale decisions, both scalings fused with the 128-block Walsh-Hadamard
+rotations), with one read of four result words at the end; CUDA tensors only.
+``block_rms`` keeps the reference's public helper (regularize.py:49-80).
 """
 
 from __future__ import annotations
@@ -16,7 +19,8 @@ from typing import Callable, Optional
 
 import torch
 
-from .hadamard import HAD_DIM, blockwise_preapply_had_l_, blockwise_preapply_had_r_
+from ._ext import ext, require_cuda
+from .hadamard import HAD_DIM
 
 CODEBOOK_SCALE = 1.24371088
 OUT_SCALE_SKEW_CUTOFF = 0.15
@@ -64,45 +68,32 @@ def regularize(weight: torch.Tensor, su: torch.Tensor, sv: torch.Tensor,
     if k % had_dim != 0 or n % had_dim != 0:
         raise ValueError(f"both dimensions must be divisible by {had_dim}, got {(k, n)}")
 
+    if had_dim != HAD_DIM:
+        raise ValueError(f"had_dim must be {HAD_DIM} (the EXL3 rotation), got {had_dim}")
+    dev = require_cuda(weight.device)
+
     args = {} if quant_args is None else quant_args
     force = args.get("apply_out_scales")
-    skew: Optional[float] = None
+    f32 = dict(device=dev, dtype=torch.float32)
+    W = weight.contiguous()
+    work = torch.empty_like(W)
+    su_out = torch.empty(k, **f32)
+    sv_out = torch.empty(n, **f32)
+    out_scales = torch.empty(n, **f32)
+    in_scales = torch.empty(k, **f32)
+    hd = None
     if not q_fallback and H_diag is not None:
-        d, _ = torch.sort(H_diag.sqrt(), descending=True)
-        cutoff = d.shape[0] // SKEW_FRACTION
-        skew = float(d[:cutoff].sum() / d.sum())
-        apply_out = (skew < OUT_SCALE_SKEW_CUTOFF) if force is None else bool(force)
-    else:
-        apply_out = True if force is None else bool(force)
-    if q_fallback:
-        apply_out = bool(force)
-
-    work = weight.clone().contiguous()
-    out_scales = block_rms(work, dim=0, keepdim=True)
-    mean = out_scales.mean().item()
-    if mean > 1e-30:
-        out_scales /= mean
-        zeros = False
-    else:
-        zeros = True
-        if force is not None:
-            apply_out = True
-    zero_out = out_scales.abs() < 1e-30
-
-    su = su.to(device=work.device, dtype=torch.float32).clone().reshape(k, 1)
-    sv = sv.to(device=work.device, dtype=torch.float32).clone().reshape(1, n)
-    if apply_out:
-        out_scales[zero_out] = ZERO_FLOOR
-        sv = (sv * out_scales + EPS).float()
-    work /= sv
-    sv[zero_out] = 0.0
-    blockwise_preapply_had_r_(work, had_dim)
-
-    in_scales = block_rms(work, dim=1, keepdim=True)
-    in_scales[in_scales.abs() < 1e-30] = ZERO_FLOOR
-    su = (su * in_scales / (-CODEBOOK_SCALE) + EPS).float()
-    work /= su
-    blockwise_preapply_had_l_(work, had_dim)
+        hd = H_diag.to(**f32)
+        if hd.dim() != 1 or hd.shape[0] != k:
+            raise ValueError(f"H_diag must have {k} elements, got shape {tuple(hd.shape)}")
+    apply_out, zeros, skew, _mean = ext().regularize_(
+        W, su.to(**f32).reshape(k).contiguous(), sv.to(**f32).reshape(n).contiguous(), hd,
+        -1 if force is None else int(bool(force)), bool(q_fallback), work, su_out, sv_out,
+        out_scales, in_scales)
+    apply_out, zeros = bool(apply_out), bool(zeros)
+    skew = None if hd is None else float(skew)
+    su = su_out.reshape(k, 1)
+    sv = sv_out.reshape(1, n)
 
     if skip_g_scale:
         g_scale = 1.0
@@ -117,5 +108,5 @@ def regularize(weight: torch.Tensor, su: torch.Tensor, sv: torch.Tensor,
     su /= g_scale
     if "zeros" in args or quant_args is not None:
         args["zeros"] = zeros
-    return RegularizeResult(bool(apply_out), work, g_scale, su, sv, out_scales, in_scales, zeros,
-                            skew)
+    return RegularizeResult(apply_out, work, g_scale, su, sv, out_scales.reshape(1, n),
+                            in_scales.reshape(k, 1), zeros, skew)

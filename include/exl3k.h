@@ -243,6 +243,39 @@ int exl3_hessian_finalize(float* H, int64_t d, int64_t count, float damping_lamb
                           float zero_floor, float* damp_out, void* scratch8,
                           exl3_stream_t stream);
 
+/*
+ * Weight regularization of a (k, n) fp32 weight, k and n multiples of 128,
+ * entirely on the device (no host round trip): the skew heuristic on
+ * sqrt(h_diag) (h_diag may be NULL: no heuristic; its elements are
+ * h_diag[i * h_diag_stride], e.g. stride k + 1 for the diagonal of H), the
+ * 32-slice block RMS of every column, the output-scale decision
+ * (force_out_scales -1 = automatic, 0 / 1 forced; q_fallback as the
+ * reference), sv, W / sv and the right 128-block Hadamard, the row RMS, su,
+ * work / su and the left 128-block Hadamard. Outputs: work (k, n), su_out
+ * (k), sv_out (n), out_scales (n), in_scales (k) and 16 bytes of `info`
+ * {int32 apply_out_scales, int32 zeros, float skew (NaN if not computed),
+ * float mean}. Replaces regularize (exl3_quant/regularize.py:83-211) except
+ * its global-scale step, which multiplies work and divides su afterwards.
+ * exl3_regularize_ws_bytes returns the workspace size (0 on invalid shapes).
+ */
+size_t exl3_regularize_ws_bytes(int64_t k, int64_t n);
+int exl3_regularize(const float* W, const float* su_in, const float* sv_in,
+                    const float* h_diag, int64_t h_diag_stride, int force_out_scales,
+                    int q_fallback, float* work, float* su_out, float* sv_out,
+                    float* out_scales, float* in_scales, void* info, int64_t k, int64_t n,
+                    void* ws, size_t ws_bytes, exl3_stream_t stream);
+
+/*
+ * Block-LDL fold: from the (n, n) lower Cholesky factor C (n % 16 == 0,
+ * 16-byte aligned), L[:, b] = C[:, b] D_b^-1 for every 16-column block b with
+ * D_b = C's 16x16 diagonal block, identity diagonal blocks and zeros above
+ * them; `inverses` (nullable) receives the (n/16, 16, 16) D_b^-1. Replaces the
+ * fold of block_ldl (exl3_quant/ldlq.py:96-117); the factorization itself
+ * stays cuSOLVER's potrf with the reference's retry schedule.
+ */
+int exl3_block_ldl_fold(const float* chol, float* L, float* inverses, int64_t n,
+                        exl3_stream_t stream);
+
 /* ------------------------------------------------------------------ */
 /* Diagnostics                                                         */
 /* ------------------------------------------------------------------ */

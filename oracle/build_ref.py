@@ -7,11 +7,13 @@ encoder ``exl3_quant.reference_encoder.ReferenceTrellisEncoder`` is the CPU
 path the benchmark times as its reference line, and its ``ldlq`` /
 ``layer_quant`` are what the drop-in tests drive with the B200 encoder. The
 reference checkout exists only in the build container, so this recipe
-compiles each module of its ``exl3_quant`` package where it lies into a
-sourceless ``.pyc`` under ``oracle/_ref/exl3_quant/``: a build output, like
-the ``.so`` of a compiled C reference, that travels with the tree (git
-ignores it). No source file is copied. Python imports a package of sourceless
-``.pyc`` files of the same interpreter version directly.
+compiles each module of its ``exl3_quant`` package where it lies into
+byte code (the ``.pyc`` format, under the suffix ``.refc`` so that tools
+which drop ``.pyc`` files from a copy of the tree keep these) in
+``oracle/_ref/exl3_quant/``: a build output, like the ``.so`` of a compiled C
+reference, that travels with the tree (git ignores it). No source file is
+copied. :func:`enable` adds an import finder that loads the package from
+there with Python's sourceless loader (same interpreter version only).
 
     python oracle/build_ref.py --reference /path/to/EXL3_Intel_Arc_quantizer
 
@@ -21,6 +23,9 @@ Only ``tests/`` and ``bench.py``'s reference leg import ``oracle/_ref``.
 from __future__ import annotations
 
 import argparse
+import importlib.abc
+import importlib.machinery
+import importlib.util
 import py_compile
 import sys
 from pathlib import Path
@@ -28,6 +33,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
 PACKAGE = "exl3_quant"
+SUFFIX = ".refc"
 
 
 def build(reference: Path, out: Path = OUT) -> Path:
@@ -39,7 +45,7 @@ def build(reference: Path, out: Path = OUT) -> Path:
     stamp = out / "VERSION"
     tag = f"{sys.version_info.major}.{sys.version_info.minor}"
     for src in sorted(src_pkg.glob("*.py")):
-        dst = dst_pkg / (src.stem + ".pyc")
+        dst = dst_pkg / (src.stem + SUFFIX)
         if dst.exists() and dst.stat().st_mtime >= src.stat().st_mtime and stamp.exists() \
                 and stamp.read_text().strip() == tag:
             continue
@@ -54,13 +60,43 @@ def available() -> bool:
     this interpreter version."""
     stamp = OUT / "VERSION"
     tag = f"{sys.version_info.major}.{sys.version_info.minor}"
-    return ((OUT / PACKAGE / "__init__.pyc").is_file() and stamp.is_file()
+    return ((OUT / PACKAGE / ("__init__" + SUFFIX)).is_file() and stamp.is_file()
             and stamp.read_text().strip() == tag)
 
 
-def import_path() -> str:
-    """The directory to put on ``sys.path`` to import ``exl3_quant``."""
-    return str(OUT)
+class _Finder(importlib.abc.MetaPathFinder):
+    """Finds ``exl3_quant`` and its modules among the compiled files."""
+
+    def find_spec(self, fullname, path=None, target=None):
+        parts = fullname.split(".")
+        if parts[0] != PACKAGE or len(parts) > 2:
+            return None
+        pkg_dir = OUT / PACKAGE
+        if len(parts) == 1:
+            f = pkg_dir / ("__init__" + SUFFIX)
+            return importlib.util.spec_from_file_location(
+                fullname, str(f), loader=importlib.machinery.SourcelessFileLoader(fullname, str(f)),
+                submodule_search_locations=[str(pkg_dir)])
+        f = pkg_dir / (parts[1] + SUFFIX)
+        if not f.is_file():
+            return None
+        return importlib.util.spec_from_file_location(
+            fullname, str(f), loader=importlib.machinery.SourcelessFileLoader(fullname, str(f)))
+
+
+_FINDER = _Finder()
+
+
+def enable() -> None:
+    """Make ``import exl3_quant`` load the compiled reference package (ahead
+    of any other ``exl3_quant`` on ``sys.path``)."""
+    if _FINDER not in sys.meta_path:
+        sys.meta_path.insert(0, _FINDER)
+
+
+def disable() -> None:
+    if _FINDER in sys.meta_path:
+        sys.meta_path.remove(_FINDER)
 
 
 if __name__ == "__main__":

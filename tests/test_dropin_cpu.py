@@ -8,8 +8,6 @@ this package's encoder; no GPU work runs here.
 
 from __future__ import annotations
 
-import sys
-
 import pytest
 
 from oracle import build_ref
@@ -20,7 +18,7 @@ pytestmark = pytest.mark.skipif(not build_ref.available(),
 
 @pytest.fixture()
 def reference():
-    sys.path.insert(0, build_ref.import_path())
+    build_ref.enable()
     from exl3_intel_arc_quantizer_b200 import dropin
 
     pkg = dropin.install()
@@ -28,7 +26,7 @@ def reference():
         yield pkg
     finally:
         dropin.uninstall()
-        sys.path.remove(build_ref.import_path())
+        build_ref.disable()
 
 
 def test_reference_factories_bind_the_b200_encoder(reference):

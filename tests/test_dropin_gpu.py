@@ -12,8 +12,6 @@ tolerance (max relative error 1e-4).
 
 from __future__ import annotations
 
-import sys
-
 import numpy as np
 import pytest
 
@@ -29,7 +27,7 @@ DEV = torch.device("cuda", 0)
 
 @pytest.fixture(scope="module")
 def reference():
-    sys.path.insert(0, build_ref.import_path())
+    build_ref.enable()
     from exl3_intel_arc_quantizer_b200 import dropin
 
     pkg = dropin.install()
@@ -37,7 +35,7 @@ def reference():
         yield pkg
     finally:
         dropin.uninstall()
-        sys.path.remove(build_ref.import_path())
+        build_ref.disable()
 
 
 @pytest.mark.parametrize("name", ["k2_32x128", "k4_64x128"])
