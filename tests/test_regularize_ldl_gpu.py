@@ -149,7 +149,7 @@ def test_block_ldl_fold_equals_the_torch_fold_on_the_same_factor():
     n = 4096
     g = torch.Generator(device=DEV).manual_seed(3)
     a = torch.randn(n, 2048, generator=g, device=DEV)
-    chol = torch.linalg.cholesky(a @ a.T / 2048 + 0.01 * torch.eye(n, device=DEV))
+    chol = torch.linalg.cholesky(a @ a.T / 2048 + 0.01 * torch.eye(n, device=DEV)).contiguous()
     L = torch.empty_like(chol)
     inv = torch.empty((n // 16, 16, 16), device=DEV)
     ext().block_ldl_fold(chol, L, inv)
