@@ -440,7 +440,8 @@ def layer_cpu_baseline(K=4, crop=512, threads=None):
 def run_storage(device, K=4, shapes=((4096, 4096), (12288, 4096)), reps=5):
     """Storage side on config-4/5 module shapes: pack (states -> container),
     unpack (container -> states) and the one-pass weight decode (container ->
-    codebook -> both rotations -> fp32 weight). Each launch timed alone with
+    codebook -> both rotations -> fp32 weight), and the HBM-bound float
+    stages on the same shapes (Hadamards, regularization, block-LDL fold). Each launch timed alone with
     CUDA events, L2 flushed before it (512 MiB write); bandwidth from the
     algorithmic bytes: decode K/8 B read + 4 B written per weight, pack
     2 B read + K/8 B written, unpack K/8 B read + 2 B written."""
@@ -487,12 +488,36 @@ def run_storage(device, K=4, shapes=((4096, 4096), (12288, 4096)), reps=5):
                                                   unpacked.view(tk, tn, 256), K))
         t_dec = timed(lambda: e.decode_weight(packed.view(tk, tn, 16 * K), su, sv, w, None, K, 2))
         assert torch.equal(packed, container) and torch.equal(unpacked, states)
+        # the floating-point stages on the same shape: in-place 128-block
+        # Hadamards (8 B per weight), the device regularization (20 B per
+        # weight: column sums, W/sv + right FWHT, work/su + left FWHT) and the
+        # block-LDL fold of a (k, k) factor (4 B written per element, 4 B read
+        # below the diagonal)
+        t_hl = timed(lambda: e.had128_left_(w))
+        t_hr = timed(lambda: e.had128_right_(w))
+        W0 = torch.randn((k, n), generator=g, device=device) * 0.02
+        ones_k = torch.ones(k, device=device)
+        ones_n = torch.ones(n, device=device)
+        hd = torch.rand(k, generator=g, device=device) + 0.5
+        regs = [torch.empty_like(W0), torch.empty(k, device=device), torch.empty(n, device=device),
+                torch.empty(n, device=device), torch.empty(k, device=device)]
+        t_reg = timed(lambda: e.regularize_(W0, ones_k, ones_n, hd, -1, False, *regs))
+        a = torch.randn((k, k // 2), generator=g, device=device)
+        chol = torch.linalg.cholesky(a @ a.T / k + 0.05 * torch.eye(k, device=device)).contiguous()
+        L = torch.empty_like(chol)
+        del a
+        t_fold = timed(lambda: e.block_ldl_fold(chol, L, None))
+        del W0, regs, chol, L
         wts = k * n
         row = {"shape": [k, n], "K": K,
                "pack_ms": t_pack, "pack_gbs": wts * (2 + K / 8) / t_pack / 1e6,
                "unpack_ms": t_unpack, "unpack_gbs": wts * (K / 8 + 2) / t_unpack / 1e6,
-               "decode_ms": t_dec, "decode_gbs": wts * (K / 8 + 4) / t_dec / 1e6}
-        for key in ("pack", "unpack", "decode"):
+               "decode_ms": t_dec, "decode_gbs": wts * (K / 8 + 4) / t_dec / 1e6,
+               "had_left_ms": t_hl, "had_left_gbs": wts * 8 / t_hl / 1e6,
+               "had_right_ms": t_hr, "had_right_gbs": wts * 8 / t_hr / 1e6,
+               "regularize_ms": t_reg, "regularize_gbs": wts * 20 / t_reg / 1e6,
+               "ldl_fold_ms": t_fold, "ldl_fold_gbs": k * k * 6 / t_fold / 1e6}
+        for key in ("pack", "unpack", "decode", "had_left", "had_right", "regularize", "ldl_fold"):
             row[f"{key}_frac_of_measured_hbm"] = row[f"{key}_gbs"] / hbm
         out.append(row)
     del flush
@@ -1074,6 +1099,11 @@ def summarize(line):
     for d in line.get("decoder_layer") or []:
         out[f"config4_layer_k{d['K']}_s"] = r(d["seconds_per_layer"])
         out[f"config4_layer_k{d['K']}_phases_s"] = {k: r(v, 3) for k, v in d["phases_s"].items()}
+    for row in (line.get("storage") or {}).get("kernels", [])[-1:]:   # the largest shape
+        tag = "x".join(str(v) for v in row["shape"])
+        for key in ("decode", "had_left", "regularize", "ldl_fold"):
+            if f"{key}_frac_of_measured_hbm" in row:
+                out[f"{key}_{tag}_frac_hbm"] = r(row[f"{key}_frac_of_measured_hbm"], 3)
     for g in (line.get("hessian") or {}).get("groups", []):
         out[f"hessian_d{g['d']}_ms"] = r(g["ms"])
         out[f"hessian_d{g['d']}_frac_bf16"] = r(g["frac_mma_of_measured_bf16"], 3)

@@ -26,7 +26,6 @@ namespace exl3 {
 namespace {
 
 constexpr int kDB = 128;          // block edge
-constexpr int kDPitch = kDB + 1;  // padded row pitch (conflict-free column walks)
 constexpr int kDThreads = 256;   // unpack
 constexpr int kDecThreads = 256; // decode: four spans per thread
 constexpr int kUTiles = 16;       // tiles per unpack CTA (two per warp)
@@ -66,29 +65,49 @@ __device__ __forceinline__ float load_scale(const void* p, int64_t i) {
 
 // decode_weight_kernel: one CTA per 128x128 block of the (k, n) weight (8x8
 // tiles). The block's container words are read once; each thread decodes
-// four spans (16 states each, fixed tile positions) into a padded fp32
-// shared tile; the left rotation (columns, then x su) and the right rotation
-// (rows, then x sv) run in shared memory and the block is written once:
-// HBM traffic = K/8 B read + 4 B written per weight.
+// four spans (16 states each, fixed tile positions) into an fp32 shared
+// tile; the left rotation runs on columns, the right one on rows, and the
+// block is written once: HBM traffic = K/8 B read + 4 B written per weight.
+//
+// Both rotations give each thread 64 elements of one column (or row) - the
+// elements of one parity, its partner lane holding the other - so the
+// stride-1 butterfly is one shuffle and the six wider ones run in registers
+// (one shuffle per element per rotation instead of five). The shared tile is
+// stored with the rows XOR-swizzled (column c of row r at c ^ dswz(r)) so
+// that both thread mappings and the row-wise float4 copy-out are free of bank
+// conflicts. Per element the steps and their roundings are those of
+// hadamard.weight_from_quantized: butterflies in the order of strides
+// 1, 2, ..., 64 (lower + upper, lower - upper), x 1/sqrt(128), x su, the row
+// butterflies, x 1/sqrt(128), x sv.
+__device__ __forceinline__ int dswz(int r) { return 2 * (((r & 1) << 3) | ((r >> 1) & 7)); }
+__device__ __forceinline__ int dpos(int r, int c) { return r * kDB + (c ^ dswz(r)); }
+
+// in-register butterflies of strides 1..32 over v[0..63] (element stride 2h in
+// the block: the caller's stride-1 partner is another lane)
+__device__ __forceinline__ void fwht64_regs(float (&v)[64]) {
+#pragma unroll
+  for (int h = 1; h < 64; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      if (i & h) continue;
+      const float lo = v[i], hi = v[i + h];
+      v[i] = lo + hi;
+      v[i + h] = lo - hi;
+    }
+  }
+}
+
 template <int K, int CB, int SCALE_F32>
-__global__ void __launch_bounds__(kDecThreads)
+__global__ void __launch_bounds__(kDecThreads, 2)
 decode_weight_kernel(const uint16_t* __restrict__ trellis, const void* __restrict__ su,
                      const void* __restrict__ sv, float* __restrict__ out,
                      float* __restrict__ out_w_hat, int64_t tiles_n, int64_t n) {
   extern __shared__ __align__(16) uint8_t dsmem[];
-  float* blk = reinterpret_cast<float*>(dsmem);                       // 128 x 129 fp32
-  uint16_t* words = reinterpret_cast<uint16_t*>(blk + kDB * kDPitch);  // 64 tiles x 16K
+  float* blk = reinterpret_cast<float*>(dsmem);                     // 128 x 128 fp32, swizzled
+  uint16_t* words = reinterpret_cast<uint16_t*>(blk + kDB * kDB);   // 64 tiles x 16K
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t rb = blockIdx.y, cbk = blockIdx.x;
   constexpr int wpt = 16 * K;  // storage words per tile
-
-  // scales of this block's rows and columns, four per lane
-  float su_r[4], sv_c[4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    su_r[q] = load_scale<SCALE_F32>(su, rb * kDB + lane + 32 * q);
-    sv_c[q] = load_scale<SCALE_F32>(sv, cbk * kDB + lane + 32 * q);
-  }
 
   // 1. container words: each tile row of the block is one contiguous run of
   //    8 tiles (8 * 32K bytes), copied as 32-bit words
@@ -111,48 +130,70 @@ decode_weight_kernel(const uint16_t* __restrict__ trellis, const void* __restric
     const uint16_t* tw = words + tt * wpt;
     uint32_t st[16];
     span_states<K>([&](int j) { return (uint32_t)tw[j ^ 1]; }, s, st);
-    float* base = blk + ((tt >> 3) * 16 + 4 * (s & 1)) * kDPitch + (tt & 7) * 16 + (s >> 1);
+    const int r0 = (tt >> 3) * 16 + 4 * (s & 1), c0 = (tt & 7) * 16 + (s >> 1);
 #pragma unroll
     for (int u = 0; u < 16; ++u) {
       const int dr = 2 * (u >> 3) + (u & 1) + 8 * ((u >> 1) & 1);
       const int dc = 8 * ((u >> 2) & 1);
-      base[dr * kDPitch + dc] = __half2float(__ushort_as_half(cb_state_bits(CB, st[u])));
+      blk[dpos(r0 + dr, c0 + dc)] = __half2float(__ushort_as_half(cb_state_bits(CB, st[u])));
     }
   }
   __syncthreads();
 
   if (out_w_hat) {  // transformed-basis reconstruction, before the rotations
-    for (int i = tid; i < kDB * kDB; i += kDecThreads) {
-      const int r = i >> 7, c = i & 127;
-      out_w_hat[(rb * kDB + r) * n + cbk * kDB + c] = blk[r * kDPitch + c];
+    for (int r = warp; r < kDB; r += kDecThreads / 32) {
+      const int f = dswz(r);
+      const float4 p = *reinterpret_cast<const float4*>(blk + r * kDB + ((4 * lane) ^ (f & ~3)));
+      const float4 o = (f & 2) ? make_float4(p.z, p.w, p.x, p.y) : p;
+      *reinterpret_cast<float4*>(out_w_hat + (rb * kDB + r) * n + cbk * kDB + 4 * lane) = o;
     }
   }
 
-  // 3. H_l on every column, then x su (per row)
-  for (int c = warp; c < kDB; c += kDecThreads / 32) {
-    float v[4];
+  float v[64];
+  const int b = tid & 1;
+  const float sign = b ? -1.0f : 1.0f;
+  // 3. H_l on every column (thread pair per column: rows 2i + b), x 1/sqrt(128)
+  {
+    const int c = tid >> 1;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) v[q] = blk[(lane + 32 * q) * kDPitch + c];
-    fwht128_warp(v, lane);
+    for (int i = 0; i < 64; ++i) v[i] = blk[dpos(2 * i + b, c)];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) blk[(lane + 32 * q) * kDPitch + c] = (v[q] * kHad128Scale) * su_r[q];
+    for (int i = 0; i < 64; ++i) v[i] = had_bfly(v[i], __shfl_xor_sync(0xFFFFFFFFu, v[i], 1), sign);
+    fwht64_regs(v);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) blk[dpos(2 * i + b, c)] = v[i] * kHad128Scale;
   }
   __syncthreads();
-
-  // 4. H_r on every row, then x sv (per column), written straight out
+  // 4. x su, then H_r on every row (thread pair per row: columns 2i + b),
+  //    x 1/sqrt(128)
+  {
+    const int r = tid >> 1;
+    const float sur = load_scale<SCALE_F32>(su, rb * kDB + r);
+    const int f = dswz(r);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = blk[r * kDB + ((2 * i + b) ^ f)] * sur;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = had_bfly(v[i], __shfl_xor_sync(0xFFFFFFFFu, v[i], 1), sign);
+    fwht64_regs(v);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) blk[r * kDB + ((2 * i + b) ^ f)] = v[i] * kHad128Scale;
+  }
+  __syncthreads();
+  // 5. x sv (per column) and the block written row by row with float4 stores
+  float svc[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) svc[e] = load_scale<SCALE_F32>(sv, cbk * kDB + 4 * lane + e);
   for (int r = warp; r < kDB; r += kDecThreads / 32) {
-    float v[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) v[q] = blk[r * kDPitch + lane + 32 * q];
-    fwht128_warp(v, lane);
-    float* dst = out + (rb * kDB + r) * n + cbk * kDB;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) dst[lane + 32 * q] = (v[q] * kHad128Scale) * sv_c[q];
+    const int f = dswz(r);
+    const float4 p = *reinterpret_cast<const float4*>(blk + r * kDB + ((4 * lane) ^ (f & ~3)));
+    const float4 o = (f & 2) ? make_float4(p.z, p.w, p.x, p.y) : p;
+    *reinterpret_cast<float4*>(out + (rb * kDB + r) * n + cbk * kDB + 4 * lane) =
+        make_float4(o.x * svc[0], o.y * svc[1], o.z * svc[2], o.w * svc[3]);
   }
 }
 
 constexpr size_t decode_smem_bytes(int K) {
-  return (size_t)kDB * kDPitch * 4 + (size_t)64 * 16 * K * 2;
+  return (size_t)kDB * kDB * 4 + (size_t)64 * 16 * K * 2;
 }
 
 template <int K, int CB, int F32>
