@@ -44,6 +44,7 @@ def _declare(handle: ctypes.CDLL) -> None:
     handle.exl3_quantize_tiles_ws_bytes.restype = c.c_size_t
     handle.exl3_quantize_tiles_ws_bytes.argtypes = [c.c_int64, c.c_int, c.c_int]
     handle.exl3_encoder_set_cluster.argtypes = [c.c_int]
+    handle.exl3_encoder_set_cluster_pairs.argtypes = [c.c_int]
     handle.exl3_encoder_fault_count.argtypes = [c.POINTER(c.c_uint)]
     handle.exl3_encoder_test_cluster_wait.argtypes = [c.c_longlong, c.c_int]
     handle.exl3_encoder_cluster_capacity.argtypes = [c.c_int, c.c_int, c.POINTER(c.c_int)]
@@ -60,6 +61,14 @@ def set_encoder_cluster(cluster_ctas: int) -> None:
     0 automatic, 1 never, 2 / 4 / 8 always that many CTAs per tile pair.
     Process-wide; outputs are bit-identical for every setting."""
     _check(lib().exl3_encoder_set_cluster(int(cluster_ctas)))
+
+
+def set_encoder_cluster_pairs(pairs_per_cluster: int) -> None:
+    """Tile pairs per cluster of the cluster-split ACS
+    (``exl3_encoder_set_cluster_pairs``): 0 automatic, 1 / 2 / 4 forced (2 and
+    4 exist for clusters of 8 CTAs). Process-wide; outputs are bit-identical
+    for every setting."""
+    _check(lib().exl3_encoder_set_cluster_pairs(int(pairs_per_cluster)))
 
 
 def encoder_cluster_capacity(K: int, cluster_ctas: int) -> int:

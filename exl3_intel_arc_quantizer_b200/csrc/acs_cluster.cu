@@ -64,10 +64,6 @@ struct CGeo {
   static constexpr int R = ck_stride(K);              // checkpoint stride (as acs_pair.cu)
   static constexpr int CKB = S * 4;
   static constexpr int NCB = E * Q / 2;              // codebook registers
-  static constexpr size_t SMEM = (size_t)6 * SL * 4 + 256 * 4;  // 4 in + 2 own + weights
-  // launched with at least 116 KiB so two CTAs never share an SM: the split
-  // only pays when every CTA of a cluster has an SM of its own
-  static constexpr size_t SMEM_LAUNCH = SMEM > 118784 ? SMEM : 118784;
   static_assert(C == 2 || C == 4 || C == 8, "cluster of 2, 4 or 8 CTAs");
   static_assert(K >= 2 && K <= 6, "cluster split needs 2^GB >= C");
   static_assert(GL >= CE && GL >= 1, "a chunk must land in one consumer");
@@ -305,14 +301,27 @@ __device__ __forceinline__ void ckc_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
-// One pass over a pair: L steps, messages msg .. msg+L-2.
-template <int K, int C, int PASS, bool EXACT>
+// Shared memory of a cluster CTA serving P tile pairs at once: four rotating
+// input buffers and two own slices of P x S/C words each, and the P pairs'
+// weights. Launched with at least 116 KiB so two CTAs never share an SM: the
+// split only pays when every CTA of a cluster has an SM of its own.
+template <int K, int C, int P>
+struct CSmem {
+  static constexpr size_t bytes = (size_t)6 * P * CGeo<K, C>::SL * 4 + (size_t)P * 256 * 4;
+  static constexpr size_t launch = bytes > 118784 ? bytes : 118784;
+  static_assert(bytes <= 227 * 1024, "shared memory of a cluster CTA");
+};
+
+// One pass over P tile pairs at once: L steps, messages msg .. msg+L-2, each
+// message carrying every pair's words (one mbarrier phase per step for all
+// of them). Pair p's words live in slot (m * P + p) of the message buffers.
+template <int K, int C, int P, int PASS, bool EXACT>
 __device__ __forceinline__ void cl_pass(const uint32_t (&cbv)[CGeo<K, C>::NCB],
                                         const uint32_t* wt, uint32_t* inb, uint32_t* own,
-                                        uint32_t bar0, const Links& lk, uint8_t* ckp, int L,
-                                        int t, int r, int preA, int preB, uint32_t msg,
-                                        uint32_t expect, volatile int* abort, uint64_t wait_ns,
-                                        int stop_at) {
+                                        uint32_t bar0, const Links& lk, uint8_t* const (&ckp)[P],
+                                        int L, int t, int r, const int (&preA)[P],
+                                        const int (&preB)[P], uint32_t msg, uint32_t expect,
+                                        volatile int* abort, uint64_t wait_ns, int stop_at) {
   using G = CGeo<K, C>;
   const int half = L / 2;
   for (int i = 0; i < L; ++i) {
@@ -323,7 +332,6 @@ __device__ __forceinline__ void cl_pass(const uint32_t (&cbv)[CGeo<K, C>::NCB],
       if (msg_wait(bar, (m >> 2) & 1u, abort, wait_ns) && t == 0)
         mbar_expect(bar, expect);  // message m+4
     }
-    const uint32_t w2 = wt[PASS == 1 ? (i < half ? i + half : i - half) : i];
     // stop_at >= 0 (test hook only): every CTA stops sending at that step,
     // so all earlier messages were consumed and none is in flight
     const bool send = i < L - 1 && *abort == 0 && (stop_at < 0 || i < stop_at);
@@ -335,25 +343,36 @@ __device__ __forceinline__ void cl_pass(const uint32_t (&cbv)[CGeo<K, C>::NCB],
       if ((i + 1) % G::R == 0 && i <= L - 2) slot = (i + 1) / G::R - 1;
     }
     const bool own_w = slot >= 0 || i == L - 1;
-    uint32_t* ob = own + (i & 1) * G::SL;
     const int mb = (int)((msg + (uint32_t)i) & 3u);
-    if (i == 0) {
-      cl_step<K, C, true, EXACT>(cbv, w2, nullptr, inb, ob, lk, mb, send, own_w, t, r,
-                                 PASS == 2 ? preA : -1, PASS == 2 ? preB : -1);
-    } else {
-      const uint32_t* cin = inb + ((msg + (uint32_t)(i - 1)) & 3u) * G::SL;
-      cl_step<K, C, false, EXACT>(cbv, w2, cin, inb, ob, lk, mb, send, own_w, t, r, -1, -1);
+    const int wi = PASS == 1 ? (i < half ? i + half : i - half) : i;
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      const uint32_t w2 = wt[p * 256 + wi];
+      uint32_t* ob = own + ((i & 1) * P + p) * G::SL;
+      if (i == 0) {
+        cl_step<K, C, true, EXACT>(cbv, w2, nullptr, inb, ob, lk, mb * P + p, send, own_w, t, r,
+                                   PASS == 2 ? preA[p] : -1, PASS == 2 ? preB[p] : -1);
+      } else {
+        const uint32_t* cin = inb + (((msg + (uint32_t)(i - 1)) & 3u) * P + p) * G::SL;
+        cl_step<K, C, false, EXACT>(cbv, w2, cin, inb, ob, lk, mb * P + p, send, own_w, t, r,
+                                    -1, -1);
+      }
     }
     if (slot >= 0) ckc_fence();
     if (t == 0) ckc_wait_read();  // the copy of step i-1 read the slice step i+1 rewrites
     __syncthreads();
-    if (slot >= 0 && t == 0)
-      ckc_issue(ckp + (size_t)slot * G::CKB + (size_t)r * G::SL * 4, ob, G::SL * 4);
+    if (slot >= 0 && t == 0) {
+#pragma unroll
+      for (int p = 0; p < P; ++p)
+        if (ckp[p])
+          ckc_issue(ckp[p] + (size_t)slot * G::CKB + (size_t)r * G::SL * 4,
+                    own + ((i & 1) * P + p) * G::SL, G::SL * 4);
+    }
   }
   if (t == 0) ckc_wait_read();
 }
 
-template <int K, int C, int PASS>
+template <int K, int C, int P, int PASS>
 __global__ void __launch_bounds__(CGeo<K, C>::NT, 1)
 acs_cluster_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* __restrict__ ck,
                    size_t ck_pair_bytes, int32_t* __restrict__ best_edge,
@@ -361,19 +380,19 @@ acs_cluster_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* 
                    uint64_t wait_ns, int stop_at) {
   using G = CGeo<K, C>;
   extern __shared__ __align__(16) uint8_t smem[];
-  uint32_t* inb = reinterpret_cast<uint32_t*>(smem);  // 4 message buffers
-  uint32_t* own = inb + 4 * G::SL;                     // 2 slices of own results
-  uint32_t* wt = own + 2 * G::SL;                      // {w_A, w_B} per step
+  uint32_t* inb = reinterpret_cast<uint32_t*>(smem);  // 4 x P message slots of S/C words
+  uint32_t* own = inb + 4 * P * G::SL;                 // 2 x P slices of own results
+  uint32_t* wt = own + 2 * P * G::SL;                  // {w_A, w_B} per step, per pair
   __shared__ __align__(8) uint64_t bars[4];
-  __shared__ uint32_t red[64];
-  __shared__ uint32_t ckeys[2 * C];  // rank 0: per-CTA argmin keys
+  __shared__ uint32_t red[P][64];
+  __shared__ uint32_t ckeys[P][2 * C];  // rank 0: per-CTA argmin keys
   __shared__ int abort_s;
   __shared__ int self_words;
   const int t = threadIdx.x;
   const int r = (int)cluster_rank();
   const uint32_t bar0 = smem_addr(&bars[0]);
 
-  // where each chunk's words go
+  // where each chunk's words go (the same for every pair: pair p adds p * S/C)
   Links lk;
   int mine = 0;
 #pragma unroll
@@ -397,7 +416,7 @@ acs_cluster_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* 
   __syncthreads();
   if (mine) atomicAdd(&self_words, mine);
   __syncthreads();
-  const uint32_t expect = (uint32_t)(G::SL - self_words) * 4u;
+  const uint32_t expect = (uint32_t)(G::SL - self_words) * 4u * (uint32_t)P;
   if (t == 0) {
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
@@ -411,76 +430,121 @@ acs_cluster_kernel(const float* __restrict__ in, int n, int L, int cb, uint8_t* 
   uint32_t cbv[G::NCB];
   cl_init_codebook<K, C>(cbv, cb, t, r);
   const int npairs = (n + 1) / 2;
+  const int ngroups = (npairs + P - 1) / P;
   uint32_t msg = 0;
-  for (int tp = (int)cluster_id(); tp < npairs; tp += (int)cluster_count()) {
-    const int ta = 2 * tp, tb = (2 * tp + 1 < n) ? 2 * tp + 1 : 2 * tp;
+  for (int tg = (int)cluster_id(); tg < ngroups; tg += (int)cluster_count()) {
+    // pairs of the group; a missing last one repeats the group's first pair
+    // (its words travel like the others', its outputs are not written)
+    int ta[P], tb[P];
+    bool valid[P], has_b[P];
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      const int tp = tg * P + p;
+      valid[p] = tp < npairs;
+      const int tq = valid[p] ? tp : tg * P;
+      ta[p] = 2 * tq;
+      tb[p] = (2 * tq + 1 < n) ? 2 * tq + 1 : 2 * tq;
+      has_b[p] = valid[p] && 2 * tq + 1 < n;
+    }
     int nan = 0;
-    for (int i = t; i < L; i += G::NT) {
-      const __half a = __float2half_rn(in[(size_t)ta * L + i]);
-      const __half b = __float2half_rn(in[(size_t)tb * L + i]);
-      nan |= (__hisnan(a) || __hisnan(b)) ? 1 : 0;
-      wt[i] = (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      for (int i = t; i < L; i += G::NT) {
+        const __half a = __float2half_rn(in[(size_t)ta[p] * L + i]);
+        const __half b = __float2half_rn(in[(size_t)tb[p] * L + i]);
+        nan |= (__hisnan(a) || __hisnan(b)) ? 1 : 0;
+        wt[p * 256 + i] = (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+      }
     }
     nan = __syncthreads_or(nan);
-    uint8_t* pck = ck + (size_t)tp * ck_pair_bytes;
-    const uint32_t* fin = own + ((L - 1) & 1) * G::SL;
-    const bool has_b = 2 * tp + 1 < n;
+    uint8_t* pck[P];
+#pragma unroll
+    for (int p = 0; p < P; ++p)
+      pck[p] = valid[p] ? ck + (size_t)(tg * P + p) * ck_pair_bytes : nullptr;
+    const uint32_t* fin = own + ((L - 1) & 1) * P * G::SL;
     if constexpr (PASS == 1) {
+      int neg[P];
+#pragma unroll
+      for (int p = 0; p < P; ++p) neg[p] = -1;
       if (nan)
-        cl_pass<K, C, 1, true>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, -1, -1, msg, expect, &abort_s, wait_ns, stop_at);
+        cl_pass<K, C, P, 1, true>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, neg, neg, msg, expect,
+                                  &abort_s, wait_ns, stop_at);
       else
-        cl_pass<K, C, 1, false>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, -1, -1, msg, expect, &abort_s, wait_ns, stop_at);
+        cl_pass<K, C, P, 1, false>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, neg, neg, msg,
+                                   expect, &abort_s, wait_ns, stop_at);
       // argmin over the cluster: lowest key = (cost bits + edge), finite only
-      uint32_t ka = 0xFFFFFFFFu, kb = 0xFFFFFFFFu;
-      for (int le = t; le < G::SL; le += G::NT) {
-        const uint32_t w = fin[le];
-        const uint32_t e = (uint32_t)(r * G::SL + le);
-        const uint32_t a = w & 0xFFFFu, b = w >> 16;
-        if ((a & 0x7C00u) != 0x7C00u) ka = min(ka, (a << 16) | e);
-        if ((b & 0x7C00u) != 0x7C00u) kb = min(kb, (b << 16) | e);
-      }
-      ka = __reduce_min_sync(0xFFFFFFFFu, ka);
-      kb = __reduce_min_sync(0xFFFFFFFFu, kb);
-      if ((t & 31) == 0) {
-        red[t >> 5] = ka;
-        red[32 + (t >> 5)] = kb;
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+        uint32_t ka = 0xFFFFFFFFu, kb = 0xFFFFFFFFu;
+        for (int le = t; le < G::SL; le += G::NT) {
+          const uint32_t w = fin[p * G::SL + le];
+          const uint32_t e = (uint32_t)(r * G::SL + le);
+          const uint32_t a = w & 0xFFFFu, b = w >> 16;
+          if ((a & 0x7C00u) != 0x7C00u) ka = min(ka, (a << 16) | e);
+          if ((b & 0x7C00u) != 0x7C00u) kb = min(kb, (b << 16) | e);
+        }
+        ka = __reduce_min_sync(0xFFFFFFFFu, ka);
+        kb = __reduce_min_sync(0xFFFFFFFFu, kb);
+        if ((t & 31) == 0) {
+          red[p][t >> 5] = ka;
+          red[p][32 + (t >> 5)] = kb;
+        }
       }
       __syncthreads();
       if (t < 32) {
-        uint32_t va = (t < G::NT / 32) ? red[t] : 0xFFFFFFFFu;
-        uint32_t vb = (t < G::NT / 32) ? red[32 + t] : 0xFFFFFFFFu;
-        va = __reduce_min_sync(0xFFFFFFFFu, va);
-        vb = __reduce_min_sync(0xFFFFFFFFu, vb);
-        if (t == 0) {
-          const uint32_t dst = map_rank(smem_addr(&ckeys[0]), 0u);
-          asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(dst + 4u * r), "r"(va) : "memory");
-          asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(dst + 4u * (C + r)), "r"(vb)
-                       : "memory");
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+          uint32_t va = (t < G::NT / 32) ? red[p][t] : 0xFFFFFFFFu;
+          uint32_t vb = (t < G::NT / 32) ? red[p][32 + t] : 0xFFFFFFFFu;
+          va = __reduce_min_sync(0xFFFFFFFFu, va);
+          vb = __reduce_min_sync(0xFFFFFFFFu, vb);
+          if (t == 0) {
+            const uint32_t dst = map_rank(smem_addr(&ckeys[p][0]), 0u);
+            asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(dst + 4u * r), "r"(va)
+                         : "memory");
+            asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(dst + 4u * (C + r)), "r"(vb)
+                         : "memory");
+          }
         }
       }
       cluster_sync_all();
       if (r == 0 && t == 0) {
-        uint32_t va = 0xFFFFFFFFu, vb = 0xFFFFFFFFu;
 #pragma unroll
-        for (int q = 0; q < C; ++q) {
-          va = min(va, ckeys[q]);
-          vb = min(vb, ckeys[C + q]);
+        for (int p = 0; p < P; ++p) {
+          if (!valid[p]) continue;
+          uint32_t va = 0xFFFFFFFFu, vb = 0xFFFFFFFFu;
+#pragma unroll
+          for (int q = 0; q < C; ++q) {
+            va = min(va, ckeys[p][q]);
+            vb = min(vb, ckeys[p][C + q]);
+          }
+          best_edge[ta[p]] = va == 0xFFFFFFFFu ? 0 : (int)(va & 0xFFFFu);
+          if (has_b[p]) best_edge[tb[p]] = vb == 0xFFFFFFFFu ? 0 : (int)(vb & 0xFFFFu);
         }
-        best_edge[ta] = va == 0xFFFFFFFFu ? 0 : (int)(va & 0xFFFFu);
-        if (has_b) best_edge[tb] = vb == 0xFFFFFFFFu ? 0 : (int)(vb & 0xFFFFu);
       }
     } else {
-      const int preA = end_state[ta];
-      const int preB = has_b ? end_state[tb] : preA;
+      int preA[P], preB[P];
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+        preA[p] = end_state[ta[p]];
+        preB[p] = (2 * (ta[p] >> 1) + 1 < n) ? end_state[tb[p]] : preA[p];
+      }
       if (nan)
-        cl_pass<K, C, 2, true>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, preA, preB, msg, expect, &abort_s, wait_ns, stop_at);
+        cl_pass<K, C, P, 2, true>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, preA, preB, msg,
+                                  expect, &abort_s, wait_ns, stop_at);
       else
-        cl_pass<K, C, 2, false>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, preA, preB, msg, expect, &abort_s, wait_ns, stop_at);
+        cl_pass<K, C, P, 2, false>(cbv, wt, inb, own, bar0, lk, pck, L, t, r, preA, preB, msg,
+                                   expect, &abort_s, wait_ns, stop_at);
       if (t == 0 && path_cost) {
-        if (preA / G::SL == r)
-          path_cost[ta] = half_bits_to_float((uint16_t)(fin[preA - r * G::SL] & 0xFFFFu));
-        if (has_b && preB / G::SL == r)
-          path_cost[tb] = half_bits_to_float((uint16_t)(fin[preB - r * G::SL] >> 16));
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+          if (!valid[p]) continue;
+          const uint32_t* f = fin + p * G::SL;
+          if (preA[p] / G::SL == r)
+            path_cost[ta[p]] = half_bits_to_float((uint16_t)(f[preA[p] - r * G::SL] & 0xFFFFu));
+          if (has_b[p] && preB[p] / G::SL == r)
+            path_cost[tb[p]] = half_bits_to_float((uint16_t)(f[preB[p] - r * G::SL] >> 16));
+        }
       }
     }
     msg += (uint32_t)(L - 1);
@@ -500,15 +564,18 @@ int g_cluster_policy = 0;  // 0 automatic, 1 never, 2/4/8 forced
 std::atomic<unsigned long long> g_cluster_wait_ns{kClusterWaitNs};
 std::atomic<int> g_cluster_stop_at{-1};  // test hook: step at which sends stop
 
-template <int K, int C>
+std::atomic<int> g_cluster_pairs{0};  // 0 automatic, 1 / 2 / 4 forced
+
+template <int K, int C, int P>
 struct ClusterKernels {
+  using Sm = CSmem<K, C, P>;
   static int setup(int dev) {
     static DeviceBits done;
     if (done.has(dev)) return EXL3_OK;
-    EXL3_CUDA(cudaFuncSetAttribute(acs_cluster_kernel<K, C, 1>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)CGeo<K, C>::SMEM_LAUNCH));
-    EXL3_CUDA(cudaFuncSetAttribute(acs_cluster_kernel<K, C, 2>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)CGeo<K, C>::SMEM_LAUNCH));
+    EXL3_CUDA(cudaFuncSetAttribute(acs_cluster_kernel<K, C, P, 1>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Sm::launch));
+    EXL3_CUDA(cudaFuncSetAttribute(acs_cluster_kernel<K, C, P, 2>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Sm::launch));
     done.set(dev);
     return EXL3_OK;
   }
@@ -528,11 +595,12 @@ struct ClusterKernels {
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3(C * 16, 1, 1);
     cfg.blockDim = dim3(CGeo<K, C>::NT, 1, 1);
-    cfg.dynamicSmemBytes = CGeo<K, C>::SMEM_LAUNCH;
+    cfg.dynamicSmemBytes = Sm::launch;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, (void*)acs_cluster_kernel<K, C, 1>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, (void*)acs_cluster_kernel<K, C, P, 1>, &cfg) !=
+        cudaSuccess) {
       cudaGetLastError();
       n = 0;
     }
@@ -550,103 +618,146 @@ struct ClusterKernels {
     attr[0].val.clusterDim.z = 1;
     cfg.gridDim = dim3((unsigned)(clusters * C), 1, 1);
     cfg.blockDim = dim3(CGeo<K, C>::NT, 1, 1);
-    cfg.dynamicSmemBytes = CGeo<K, C>::SMEM_LAUNCH;
+    cfg.dynamicSmemBytes = Sm::launch;
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    const uint64_t wait_ns = (uint64_t)g_cluster_wait_ns.load();
+    const int stop_at = g_cluster_stop_at.load();
     if (pass == 1)
-      EXL3_CUDA(cudaLaunchKernelEx(&cfg, acs_cluster_kernel<K, C, 1>, in, n, L, cb, ck, ck_pair,
-                                   best_edge, end_state, path_cost,
-                                   (uint64_t)g_cluster_wait_ns.load(), g_cluster_stop_at.load()));
+      EXL3_CUDA(cudaLaunchKernelEx(&cfg, acs_cluster_kernel<K, C, P, 1>, in, n, L, cb, ck,
+                                   ck_pair, best_edge, end_state, path_cost, wait_ns, stop_at));
     else
-      EXL3_CUDA(cudaLaunchKernelEx(&cfg, acs_cluster_kernel<K, C, 2>, in, n, L, cb, ck, ck_pair,
-                                   best_edge, end_state, path_cost,
-                                   (uint64_t)g_cluster_wait_ns.load(), g_cluster_stop_at.load()));
+      EXL3_CUDA(cudaLaunchKernelEx(&cfg, acs_cluster_kernel<K, C, P, 2>, in, n, L, cb, ck,
+                                   ck_pair, best_edge, end_state, path_cost, wait_ns, stop_at));
     return EXL3_OK;
   }
 };
 
-template <int K>
-int max_active_for(int C, int dev) {
+// The (C, P) combinations built: one pair per cluster of 2, 4 or 8 CTAs, and
+// 2 or 4 pairs per cluster of 8 CTAs (a cluster of 8 at K >= 3 has one or
+// two edges per thread and step, so extra pairs add little to a step whose
+// time is mostly its barrier and exchange).
+template <int K, class F>
+int with_kernels(int C, int P, F&& f) {
   if constexpr (K >= 2 && K <= 6) {
-    switch (C) {
-      case 2: return ClusterKernels<K, 2>::max_active(dev);
-      case 4: return ClusterKernels<K, 4>::max_active(dev);
-      case 8: return ClusterKernels<K, 8>::max_active(dev);
-    }
+    if (C == 2 && P == 1) return f(ClusterKernels<K, 2, 1>{});
+    if (C == 4 && P == 1) return f(ClusterKernels<K, 4, 1>{});
+    if (C == 8 && P == 1) return f(ClusterKernels<K, 8, 1>{});
+    if (C == 8 && P == 2) return f(ClusterKernels<K, 8, 2>{});
+    if (C == 8 && P == 4) return f(ClusterKernels<K, 8, 4>{});
   }
-  return 0;
+  return -1;
 }
 
 template <int K>
-int choose(int pairs, int sms, int dev) {
-  if (K < 2 || K > 6 || g_cluster_policy == 1) return 1;
-  if (g_cluster_policy >= 2) return max_active_for<K>(g_cluster_policy, dev) > 0 ? g_cluster_policy : 1;
-  // K = 2 with 2 CTAs moves 16 KiB per CTA and step through DSMEM, which
-  // costs as much as the halved arithmetic saves (measured): not used
-  for (int C = 8; C >= (K == 2 ? 4 : 2); C >>= 1) {
-    if ((int64_t)pairs * C > sms) continue;
-    if (max_active_for<K>(C, dev) >= pairs) return C;
+int max_active_for(int C, int P, int dev) {
+  const int v = with_kernels<K>(C, P, [&](auto tag) { return decltype(tag)::max_active(dev); });
+  return v > 0 ? v : 0;
+}
+
+// Automatic choice for a call of `pairs` tile pairs (C = 1: no split): every
+// group of P pairs must fit on the device at once, and C * groups SMs must
+// not exceed the device's. Preference, measured: one pair per cluster of 8;
+// then 2 pairs per cluster of 8 (one exchange round for both) over one pair
+// per cluster of 4; then 4 pairs per cluster of 8; then one pair per
+// cluster of 2 (K >= 3: at K = 2 a CTA pair exchanges 16 KiB per CTA and
+// step, which costs as much as the halved arithmetic saves).
+template <int K>
+void choose(int pairs, int sms, int dev, int* C_out, int* P_out) {
+  *C_out = 1;
+  *P_out = 1;
+  if (K < 2 || K > 6 || g_cluster_policy == 1) return;
+  const int forced_p = g_cluster_pairs.load();
+  auto fits = [&](int C, int P) {
+    const int groups = (pairs + P - 1) / P;
+    return (int64_t)groups * C <= sms && max_active_for<K>(C, P, dev) >= groups;
+  };
+  static constexpr int kOrder[5][2] = {{8, 1}, {8, 2}, {4, 1}, {8, 4}, {2, 1}};
+  for (const auto& o : kOrder) {
+    const int C = o[0], P = o[1];
+    if (g_cluster_policy >= 2 && C != g_cluster_policy) continue;
+    if (forced_p > 0 && P != forced_p) continue;
+    if (K == 2 && C == 2 && g_cluster_policy != 2) continue;
+    if (fits(C, P)) {
+      *C_out = C;
+      *P_out = P;
+      return;
+    }
   }
-  return 1;
+  if (g_cluster_policy >= 2) {  // forced size: its smallest P that the device holds at all
+    for (int P : {1, 2, 4}) {
+      if (forced_p > 0 && P != forced_p) continue;
+      if (max_active_for<K>(g_cluster_policy, P, dev) > 0) {
+        *C_out = g_cluster_policy;
+        *P_out = P;
+        return;
+      }
+    }
+  }
 }
 
 }  // namespace
 
-int cluster_size_for(int K, int pairs) {
+void cluster_choice(int K, int pairs, int* C, int* P) {
+  *C = 1;
+  *P = 1;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
     cudaGetLastError();
-    return 1;
+    return;
   }
   const int sms = sm_count();
   switch (K) {
-    case 2: return choose<2>(pairs, sms, dev);
-    case 3: return choose<3>(pairs, sms, dev);
-    case 4: return choose<4>(pairs, sms, dev);
-    case 5: return choose<5>(pairs, sms, dev);
-    case 6: return choose<6>(pairs, sms, dev);
-    default: return 1;
+    case 2: choose<2>(pairs, sms, dev, C, P); break;
+    case 3: choose<3>(pairs, sms, dev, C, P); break;
+    case 4: choose<4>(pairs, sms, dev, C, P); break;
+    case 5: choose<5>(pairs, sms, dev, C, P); break;
+    case 6: choose<6>(pairs, sms, dev, C, P); break;
+    default: break;
   }
+}
+
+int cluster_size_for(int K, int pairs) {
+  int C, P;
+  cluster_choice(K, pairs, &C, &P);
+  return C;
 }
 
 template <int K>
-static int launch_k(int C, int pass, int pairs, cudaStream_t stream, const float* in, int n,
-                    int L, int cb, uint8_t* ck, size_t ck_pair, int32_t* best_edge,
+static int launch_k(int C, int P, int pass, int pairs, cudaStream_t stream, const float* in,
+                    int n, int L, int cb, uint8_t* ck, size_t ck_pair, int32_t* best_edge,
                     const int32_t* end_state, float* path_cost) {
-  if constexpr (K >= 2 && K <= 6) {
-    int dev = 0;
-    EXL3_CUDA(cudaGetDevice(&dev));
-    auto go = [&](auto tag) -> int {
-      using KK = decltype(tag);
-      int rc = KK::setup(dev);
-      if (rc) return rc;
-      const int cap = KK::max_active(dev);
-      EXL3_REQUIRE(cap > 0, "no cluster of %d CTAs fits on this device", C);
-      const int clusters = pairs < cap ? pairs : cap;
-      return KK::launch(pass, clusters, stream, in, n, L, cb, ck, ck_pair, best_edge, end_state,
-                        path_cost);
-    };
-    switch (C) {
-      case 2: return go(ClusterKernels<K, 2>{});
-      case 4: return go(ClusterKernels<K, 4>{});
-      case 8: return go(ClusterKernels<K, 8>{});
-    }
+  int dev = 0;
+  EXL3_CUDA(cudaGetDevice(&dev));
+  const int rc = with_kernels<K>(C, P, [&](auto tag) -> int {
+    using KK = decltype(tag);
+    int r = KK::setup(dev);
+    if (r) return r;
+    const int cap = KK::max_active(dev);
+    EXL3_REQUIRE(cap > 0, "no cluster of %d CTAs fits on this device", C);
+    const int groups = (pairs + P - 1) / P;
+    const int clusters = groups < cap ? groups : cap;
+    return KK::launch(pass, clusters, stream, in, n, L, cb, ck, ck_pair, best_edge, end_state,
+                      path_cost);
+  });
+  if (rc == -1) {
+    set_error("no cluster ACS for K=%d, C=%d, %d pairs per cluster", K, C, P);
+    return EXL3_EINVAL;
   }
-  set_error("no cluster ACS for K=%d, C=%d", K, C);
-  return EXL3_EINVAL;
+  return rc;
 }
 
-int cluster_acs_pass(int K, int C, int pass, cudaStream_t stream, const float* in, int n, int L,
-                     int cb, uint8_t* ck, size_t ck_pair, int32_t* best_edge,
+int cluster_acs_pass(int K, int C, int P, int pass, cudaStream_t stream, const float* in, int n,
+                     int L, int cb, uint8_t* ck, size_t ck_pair, int32_t* best_edge,
                      const int32_t* end_state, float* path_cost) {
   const int pairs = (n + 1) / 2;
   switch (K) {
-    case 2: return launch_k<2>(C, pass, pairs, stream, in, n, L, cb, ck, ck_pair, best_edge, end_state, path_cost);
-    case 3: return launch_k<3>(C, pass, pairs, stream, in, n, L, cb, ck, ck_pair, best_edge, end_state, path_cost);
-    case 4: return launch_k<4>(C, pass, pairs, stream, in, n, L, cb, ck, ck_pair, best_edge, end_state, path_cost);
-    case 5: return launch_k<5>(C, pass, pairs, stream, in, n, L, cb, ck, ck_pair, best_edge, end_state, path_cost);
-    case 6: return launch_k<6>(C, pass, pairs, stream, in, n, L, cb, ck, ck_pair, best_edge, end_state, path_cost);
+    case 2: return launch_k<2>(C, P, pass, pairs, stream, in, n, L, cb, ck, ck_pair, best_edge, end_state, path_cost);
+    case 3: return launch_k<3>(C, P, pass, pairs, stream, in, n, L, cb, ck, ck_pair, best_edge, end_state, path_cost);
+    case 4: return launch_k<4>(C, P, pass, pairs, stream, in, n, L, cb, ck, ck_pair, best_edge, end_state, path_cost);
+    case 5: return launch_k<5>(C, P, pass, pairs, stream, in, n, L, cb, ck, ck_pair, best_edge, end_state, path_cost);
+    case 6: return launch_k<6>(C, P, pass, pairs, stream, in, n, L, cb, ck, ck_pair, best_edge, end_state, path_cost);
     default:
       set_error("no cluster ACS for K=%d", K);
       return EXL3_EINVAL;
@@ -662,6 +773,14 @@ extern "C" int exl3_encoder_set_cluster(int cluster_ctas) {
                    cluster_ctas == 8,
                "cluster size must be 0 (automatic), 1 (off), 2, 4 or 8, got %d", cluster_ctas);
   g_cluster_policy = cluster_ctas;
+  return EXL3_OK;
+}
+
+extern "C" int exl3_encoder_set_cluster_pairs(int pairs_per_cluster) {
+  EXL3_REQUIRE(pairs_per_cluster == 0 || pairs_per_cluster == 1 || pairs_per_cluster == 2 ||
+                   pairs_per_cluster == 4,
+               "pairs per cluster must be 0 (automatic), 1, 2 or 4, got %d", pairs_per_cluster);
+  g_cluster_pairs.store(pairs_per_cluster);
   return EXL3_OK;
 }
 
@@ -685,11 +804,11 @@ extern "C" int exl3_encoder_cluster_capacity(int K, int cluster_ctas, int* clust
   EXL3_CUDA(cudaGetDevice(&dev));
   int n = 0;
   switch (K) {
-    case 2: n = max_active_for<2>(cluster_ctas, dev); break;
-    case 3: n = max_active_for<3>(cluster_ctas, dev); break;
-    case 4: n = max_active_for<4>(cluster_ctas, dev); break;
-    case 5: n = max_active_for<5>(cluster_ctas, dev); break;
-    case 6: n = max_active_for<6>(cluster_ctas, dev); break;
+    case 2: n = max_active_for<2>(cluster_ctas, 1, dev); break;
+    case 3: n = max_active_for<3>(cluster_ctas, 1, dev); break;
+    case 4: n = max_active_for<4>(cluster_ctas, 1, dev); break;
+    case 5: n = max_active_for<5>(cluster_ctas, 1, dev); break;
+    case 6: n = max_active_for<6>(cluster_ctas, 1, dev); break;
     default: n = 0;
   }
   *clusters = n > 0 ? n : 0;

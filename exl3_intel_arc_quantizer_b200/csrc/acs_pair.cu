@@ -714,10 +714,11 @@ int pair_encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t*
     // waves one pair per CTA, and the last partial wave, if it is small
     // enough, split over clusters (it would otherwise leave most SMs idle
     // for a whole wave)
-    const int csize = cluster_size_for(K, pairs);
-    int bulk = pairs, tail = 0, tail_c = 1;
+    int csize = 1, cpairs = 1;
+    cluster_choice(K, pairs, &csize, &cpairs);
+    int bulk = pairs, tail = 0, tail_c = 1, tail_p = 1;
     if (csize == 1 && pairs > sms && pairs % sms) {
-      tail_c = cluster_size_for(K, pairs % sms);
+      cluster_choice(K, pairs % sms, &tail_c, &tail_p);
       if (tail_c > 1) {
         tail = pairs % sms;
         bulk = pairs - tail;
@@ -740,8 +741,9 @@ int pair_encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t*
       int32_t* be = pass == 1 ? best_edge : nullptr;
       const int32_t* es = pass == 2 ? end_state : nullptr;
       float* pc = (pass == 2 && out_cost) ? out_cost + start : nullptr;
-      if (csize > 1) return cluster_acs_pass(K, csize, pass, stream, cin, m, L, cb, ck, ck_pair, be,
-                                              es, pc);
+      if (csize > 1)
+        return cluster_acs_pass(K, csize, cpairs, pass, stream, cin, m, L, cb, ck, ck_pair, be, es,
+                                pc);
       const int g = bulk < sms ? bulk : sms;
       if (pass == 1)
         acs_pair_kernel<K, 1><<<g, kPairNT, PSmem<K>::bytes, stream>>>(cin, mb, L, cb, ck, ck_pair,
@@ -751,7 +753,7 @@ int pair_encode_chunks(const float* in, float* out_w, int16_t* out_idx, int16_t*
                                                                       be, es, pc);
       EXL3_LAUNCHED();
       if (!tail) return EXL3_OK;
-      return cluster_acs_pass(K, tail_c, pass, stream, cin + (size_t)mb * L, m - mb, L, cb,
+      return cluster_acs_pass(K, tail_c, tail_p, pass, stream, cin + (size_t)mb * L, m - mb, L, cb,
                               ck + (size_t)bulk * ck_pair, ck_pair, be ? be + mb : nullptr,
                               es ? es + mb : nullptr, pc ? pc + mb : nullptr);
     };

@@ -83,9 +83,12 @@ int single_encode(const float* in, float* out_w, int16_t* out_idx, int16_t* out_
 // cluster-split ACS passes for few tile pairs (acs_cluster.cu): the cluster
 // size to use for `pairs` pairs at K (1 = the one-CTA-per-pair kernel), and
 // one pass (1 or 2) with the tile-pair kernel's arguments and checkpoints
+// Cluster split of a call of `pairs` tile pairs: C CTAs per group of P pairs
+// (C = 1: no split); cluster_size_for returns its C.
+void cluster_choice(int K, int pairs, int* C, int* P);
 int cluster_size_for(int K, int pairs);
-int cluster_acs_pass(int K, int C, int pass, cudaStream_t stream, const float* in, int n, int L,
-                     int cb, uint8_t* ck, size_t ck_pair, int32_t* best_edge,
+int cluster_acs_pass(int K, int C, int P, int pass, cudaStream_t stream, const float* in, int n,
+                     int L, int cb, uint8_t* ck, size_t ck_pair, int32_t* best_edge,
                      const int32_t* end_state, float* path_cost);
 int pair_encode(int K, const float* in, float* out_w, int16_t* out_idx, int16_t* out_packed,
                 float* out_cost, int64_t n, int cb, int L, uint8_t* ws, size_t ws_bytes,

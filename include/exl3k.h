@@ -318,6 +318,16 @@ int exl3_probe_hfma(const uint16_t* dh, const uint16_t* cost, uint16_t* out, int
 int exl3_encoder_set_cluster(int cluster_ctas);
 
 /*
+ * Tile pairs per cluster of the cluster-split ACS: 0 = automatic (one pair
+ * per cluster while the clusters fit; then 2 or 4 pairs per cluster of 8
+ * CTAs, which share one exchange round per step), 1 / 2 / 4 = always that
+ * many (tests, benchmarks; 2 and 4 exist for clusters of 8 CTAs). Outputs are
+ * bit-identical for every setting. Process-wide. No counterpart in the
+ * reference.
+ */
+int exl3_encoder_set_cluster_pairs(int pairs_per_cluster);
+
+/*
  * How many clusters of `cluster_ctas` CTAs (2, 4, 8) of the K-bit cluster
  * encoder the current device runs at once (0: that split is not available
  * for K, e.g. K = 1, 7, 8). Tile pairs beyond it take another wave. No

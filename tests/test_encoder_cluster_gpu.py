@@ -17,6 +17,7 @@ from exl3_intel_arc_quantizer_b200._ext import (  # noqa: E402
     encoder_cluster_capacity,
     encoder_fault_count,
     set_encoder_cluster,
+    set_encoder_cluster_pairs,
 )
 from exl3_intel_arc_quantizer_b200.xpu_quantizer import XPUTrellisEncoder  # noqa: E402
 from oracle.trellis_oracle import COracle  # noqa: E402
@@ -33,8 +34,9 @@ def _tiles(n, seed, L=256):
     return base * scale
 
 
-def _encode(K, cb, tiles, cluster, L=256):
+def _encode(K, cb, tiles, cluster, L=256, pairs=0):
     set_encoder_cluster(cluster)
+    set_encoder_cluster_pairs(pairs)
     try:
         enc = XPUTrellisEncoder(K=K, cb=cb, tile_len=L)
         w, i, packed, cost = enc.encode_device(torch.from_numpy(tiles).to(DEV),
@@ -45,6 +47,7 @@ def _encode(K, cb, tiles, cluster, L=256):
         return out
     finally:
         set_encoder_cluster(0)
+        set_encoder_cluster_pairs(0)
 
 
 def _same_cost(got, want, msg):
@@ -147,3 +150,45 @@ def test_last_partial_wave_split_matches_off(K):
         np.testing.assert_array_equal(a, b, err_msg=what)
     ref = COracle(K, tf.CB_MUL1).encode_batch(tiles[-24:])   # the tail pairs, checked whole
     np.testing.assert_array_equal(auto[0][-24:], ref["indices"])
+
+
+@pytest.mark.parametrize("K", [2, 3, 4, 5, 6])
+@pytest.mark.parametrize("pairs", [2, 4])
+def test_several_pairs_per_cluster_match_c_oracle(K, pairs):
+    """Clusters of 8 CTAs serving 2 or 4 tile pairs per exchange round; 11
+    tiles: the last group repeats its first pair (and the last pair is a
+    lone tile), so groups with missing pairs and odd tile counts are covered."""
+    n = 11
+    tiles = _tiles(n, 7700 + 10 * K + pairs)
+    tiles[3, 40] = np.nan            # a NaN pair inside a group: compare-and-select
+    ref = COracle(K, tf.CB_MUL1).encode_batch(tiles)
+    idx, packed, cost, recon = _encode(K, tf.CB_MUL1, tiles, 8, pairs=pairs)
+    np.testing.assert_array_equal(idx, ref["indices"])
+    np.testing.assert_array_equal(packed.view(np.uint16), ref["packed"])
+    _same_cost(cost, ref["path_cost"].view(np.uint16), f"{pairs} pairs per cluster")
+
+
+@pytest.mark.parametrize("K", [2, 4])
+def test_several_pairs_per_cluster_more_groups_than_clusters(K):
+    """200 pairs in groups of 2 and 4 over the resident clusters of 8 CTAs
+    (the clusters loop over groups): identical to one pair per CTA."""
+    tiles = _tiles(400, 7800 + K)
+    base = _encode(K, tf.CB_MUL1, tiles, 1)
+    for pairs in (2, 4):
+        got = _encode(K, tf.CB_MUL1, tiles, 8, pairs=pairs)
+        for a, b, what in zip(got, base, ("indices", "packed", "cost", "recon")):
+            np.testing.assert_array_equal(a, b, err_msg=f"{pairs} pairs {what}")
+
+
+def test_automatic_policy_with_several_pairs_matches_off():
+    """Call sizes whose pairs exceed the resident clusters of 8 CTAs (the
+    automatic choice then groups pairs): identical to no split."""
+    for K in (2, 4):
+        for n in (32, 40, 64, 96):
+            tiles = _tiles(n, 7900 + n + K)
+            off = _encode(K, tf.CB_MUL1, tiles, 1)
+            auto = _encode(K, tf.CB_MUL1, tiles, 0)
+            for a, b in zip(auto, off):
+                np.testing.assert_array_equal(a, b)
+    with pytest.raises(RuntimeError):
+        set_encoder_cluster_pairs(3)
