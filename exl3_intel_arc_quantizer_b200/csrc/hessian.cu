@@ -148,7 +148,10 @@ __device__ __forceinline__ void red_add4(float* p, float a, float b, float c, fl
 // the ones that reach column >= row somewhere. Launch order walks groups of
 // 8 consecutive i-blocks column by column (bi fastest), so the CTAs resident
 // at one time share few A and B slabs of X in L2.
-constexpr int kRasterGroup = 8;
+#ifndef EXL3_HESS_RASTER
+#define EXL3_HESS_RASTER 8
+#endif
+constexpr int kRasterGroup = EXL3_HESS_RASTER;
 
 __device__ __forceinline__ void tile_of(int idx, int nbi, int nbj, int& bi, int& bj) {
   int g0 = 0;

@@ -17,7 +17,13 @@ the running process only:
 * ``HessianCollector._accumulate`` adds fp16/bf16 activations on a CUDA
   device with the tcgen05 kernel (``hessian_accumulate_``; products of 16-bit
   values are exact in fp32, so only the summation order differs from the
-  reference's fp32 GEMM); other inputs keep the reference's own code.
+  reference's fp32 GEMM); other inputs keep the reference's own code;
+* with ``reference_encoder=True``, the reference's CPU-encoder factory
+  ``make_reference_tile_encoder`` (ldlq.py:317-341, which its
+  ``quantize_linear_module`` and ``quantize_decoder_layer`` use on every
+  non-XPU device, so its ``convert_model`` too) also returns the B200
+  encoder: it emits the same states and reconstructions bit for bit, on
+  tiles of any device.
 
 Call it before the reference imports ``exl3_quant.layer_quant`` (which binds
 the encoder class at import time); ``ldlq.make_xpu_tile_encoder`` looks the
@@ -34,7 +40,8 @@ from typing import Optional
 REFERENCE_PACKAGE = "exl3_quant"
 
 
-def install(package: str = REFERENCE_PACKAGE, hessian: bool = True):
+def install(package: str = REFERENCE_PACKAGE, hessian: bool = True,
+            reference_encoder: bool = False):
     """Route the reference package ``package`` (importable from ``sys.path``)
     to the B200 path; returns the reference package module. Idempotent."""
     from . import xpu_quantizer
@@ -44,7 +51,33 @@ def install(package: str = REFERENCE_PACKAGE, hessian: bool = True):
     setattr(pkg, "xpu_quantizer", xpu_quantizer)
     if hessian:
         _patch_hessian(importlib.import_module(f"{package}.calibration"))
+    if reference_encoder:
+        _patch_reference_encoder(package)
     return pkg
+
+
+def _b200_reference_encoder(K: int = 2):
+    """``make_reference_tile_encoder``'s contract (MUL1 codebook; tiles on any
+    device in, reconstruction and int16 states on that device out) served by
+    the B200 encoder on the current CUDA device."""
+    import torch
+
+    from .ldlq import make_xpu_tile_encoder
+
+    return make_xpu_tile_encoder(K=K, device_index=torch.cuda.current_device())
+
+
+_b200_reference_encoder._exl3_b200 = True
+
+
+def _patch_reference_encoder(package: str) -> None:
+    for name in ("ldlq", "layer_quant"):
+        mod = importlib.import_module(f"{package}.{name}")
+        current = getattr(mod, "make_reference_tile_encoder", None)
+        if current is None or getattr(current, "_exl3_b200", False):
+            continue
+        _b200_reference_encoder.__dict__.setdefault("reference", {})[mod.__name__] = current
+        mod.make_reference_tile_encoder = _b200_reference_encoder
 
 
 def installed(package: str = REFERENCE_PACKAGE) -> bool:
@@ -93,3 +126,10 @@ def uninstall(package: str = REFERENCE_PACKAGE) -> None:
         acc = cal.HessianCollector._accumulate
         if getattr(acc, "_exl3_b200", False):
             cal.HessianCollector._accumulate = acc.reference
+    saved = _b200_reference_encoder.__dict__.get("reference", {})
+    for modname, original in list(saved.items()):
+        mod = sys.modules.get(modname)
+        if mod is not None and getattr(mod, "make_reference_tile_encoder", None) is \
+                _b200_reference_encoder:
+            mod.make_reference_tile_encoder = original
+        del saved[modname]
