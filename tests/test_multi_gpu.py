@@ -43,8 +43,13 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def _step(rank, what):
+    print(f"[rank {rank}] {what}", flush=True)
+
+
 def _worker(rank, ws, port, q):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      TORCH_NCCL_ASYNC_ERROR_HANDLING="1")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=ws, device_id=dev,
@@ -56,6 +61,7 @@ def _worker(rank, ws, port, q):
         from exl3_intel_arc_quantizer_b200.ldlq import block_ldl, ldlq_native, make_xpu_tile_encoder
         from exl3_intel_arc_quantizer_b200.layer_quant import quantize_linear_module
 
+        _step(rank, "1 token-sharded Hessian")
         # 1. token-sharded Hessian
         g = torch.Generator(device=dev).manual_seed(5)
         X = torch.randn(8192, 512, generator=g, device=dev, dtype=torch.bfloat16)
@@ -68,6 +74,7 @@ def _worker(rank, ws, port, q):
         out["hess_rel"] = float((H["g"] - Href).abs().max() / Href.abs().max())
         out["count"] = counts["g"]
 
+        _step(rank, "2 column-sharded LDLQ")
         # 2. column-sharded LDLQ with the B200 encoder
         gc = torch.Generator(device="cpu").manual_seed(9)
         W = torch.randn(256, 512, generator=gc).to(dev)
@@ -80,6 +87,7 @@ def _worker(rank, ws, port, q):
                                 / torch.linalg.norm(ref.weight_q))
         out["ldlq_same"] = float((sh.encoded == ref.encoded).all(-1).float().mean())
 
+        _step(rank, "3 module-sharded layer")
         # 3. module-sharded layer
         weights = {"a": (torch.randn(256, 128, generator=gc) * 0.02).to(dev),
                    "b": (torch.randn(128, 256, generator=gc) * 0.02).to(dev)}
@@ -99,6 +107,7 @@ def _worker(rank, ws, port, q):
                 local[m] = float(torch.linalg.norm(r.result.w_hat - r.w_hat))
         out.update(owners=own, digest=digest, local=local)
 
+        _step(rank, "4 column-sharded batched modules")
         # 4. column-sharded batched modules: metrics summed over the ranks'
         #    column slices equal the ones every rank can recompute whole
         from exl3_intel_arc_quantizer_b200.layer_quant import (
@@ -119,11 +128,13 @@ def _worker(rank, ws, port, q):
             again[m] = tuple(redo) + (_ldl_of(mods[m][1].float(), 16)[1],)
         out.update(mod_metrics=met, mod_again=again)
 
+        _step(rank, "5 the same modules on one GPU")
         # 5. the same modules on one GPU: sharded == unsharded, bit for bit
         one = quantize_modules(mods, K=2, tile_encoder=enc)
         out["qm_equal"] = {m: bool(torch.equal(qm[m].w_hat, one[m].w_hat)
                                    and torch.equal(qm[m].encoded, one[m].encoded)) for m in mods}
 
+        _step(rank, "6 convert_layer")
         # 6. convert_layer: one calibration batch per rank (Hessian all-reduce
         #    of the two partial sums), column-sharded quantization, local
         #    re-forward; against one GPU converting both batches
@@ -149,7 +160,11 @@ def _worker(rank, ws, port, q):
                                 full[m].metrics.relative_frobenius_error) for m in res}
         out["cl_tokens"] = tm.local_tokens
         torch.cuda.synchronize()
+        _step(rank, "done")
     except Exception as e:  # pragma: no cover
+        import traceback
+
+        traceback.print_exc()
         out = e
     finally:
         dist.destroy_process_group()
@@ -163,9 +178,18 @@ def test_two_gpu_sharded_paths():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=600) for _ in range(2))
+    import queue
+
+    try:
+        res = dict(q.get(timeout=240) for _ in range(2))
+    except queue.Empty:
+        for p in procs:
+            p.terminate()
+        raise AssertionError("a rank did not report within 240 s (see its progress lines)")
     for p in procs:
-        p.join(timeout=120)
+        p.join(timeout=60)
+        if p.is_alive():
+            p.terminate()
     for r, v in res.items():
         if isinstance(v, Exception):
             raise v
