@@ -217,13 +217,15 @@ struct Links {
 };
 
 // One step over the thread's chunks: candidates, minimum, then the chunk's
-// words go to its consumer (message buffer `mb`) and, when `own_w`, to the
+// words go to its consumer (message `mb`: its mbarrier; `slot`: the buffer
+// slot of this pair's words in that message) and, when `own_w`, to the
 // CTA's own slice `ob` (checkpoints, final costs).
 template <int K, int C, bool FIRST, bool EXACT>
 __device__ __forceinline__ void cl_step(const uint32_t (&cbv)[CGeo<K, C>::NCB], uint32_t w2,
                                         const uint32_t* __restrict__ cin, uint32_t* inb,
                                         uint32_t* __restrict__ ob, const Links& lk, int mb,
-                                        bool send, bool own_w, int t, int r, int preA, int preB) {
+                                        int slot, bool send, bool own_w, int t, int r, int preA,
+                                        int preB) {
   using G = CGeo<K, C>;
 #pragma unroll
   for (int c = 0; c < G::NCH; ++c) {
@@ -277,9 +279,9 @@ __device__ __forceinline__ void cl_step(const uint32_t (&cbv)[CGeo<K, C>::NCB], 
     }
     if (send) {
       if (lk.data[c] != 0u)
-        st_remote<G::CE>(lk.data[c] + (uint32_t)(mb * G::SL * 4), lk.bar[c] + 8u * mb, best);
+        st_remote<G::CE>(lk.data[c] + (uint32_t)(slot * G::SL * 4), lk.bar[c] + 8u * mb, best);
       else
-        st_words<G::CE>(inb + mb * G::SL + lk.pos[c], best);
+        st_words<G::CE>(inb + slot * G::SL + lk.pos[c], best);
     }
     if (own_w) st_words<G::CE>(ob + le0, best);
   }
@@ -350,12 +352,12 @@ __device__ __forceinline__ void cl_pass(const uint32_t (&cbv)[CGeo<K, C>::NCB],
       const uint32_t w2 = wt[p * 256 + wi];
       uint32_t* ob = own + ((i & 1) * P + p) * G::SL;
       if (i == 0) {
-        cl_step<K, C, true, EXACT>(cbv, w2, nullptr, inb, ob, lk, mb * P + p, send, own_w, t, r,
-                                   PASS == 2 ? preA[p] : -1, PASS == 2 ? preB[p] : -1);
+        cl_step<K, C, true, EXACT>(cbv, w2, nullptr, inb, ob, lk, mb, mb * P + p, send, own_w, t,
+                                   r, PASS == 2 ? preA[p] : -1, PASS == 2 ? preB[p] : -1);
       } else {
         const uint32_t* cin = inb + (((msg + (uint32_t)(i - 1)) & 3u) * P + p) * G::SL;
-        cl_step<K, C, false, EXACT>(cbv, w2, cin, inb, ob, lk, mb * P + p, send, own_w, t, r,
-                                    -1, -1);
+        cl_step<K, C, false, EXACT>(cbv, w2, cin, inb, ob, lk, mb, mb * P + p, send, own_w, t,
+                                    r, -1, -1);
       }
     }
     if (slot >= 0) ckc_fence();
