@@ -26,7 +26,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _run(rank, ws, port, fn, q):
+def _run(rank, ws, port, fn, q, received):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import datetime
 
@@ -39,18 +39,27 @@ def _run(rank, ws, port, fn, q):
     finally:
         if dist.is_initialized():
             dist.destroy_process_group()
+        # tensors cross the queue as shared-memory handles of this process:
+        # stay alive until the parent has received them
+        received.wait(timeout=120)
 
 
 def _spawn_once(fn, ws):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
+    received = ctx.Event()
     port = _free_port()
-    procs = [ctx.Process(target=_run, args=(r, ws, port, fn, q)) for r in range(ws)]
+    procs = [ctx.Process(target=_run, args=(r, ws, port, fn, q, received)) for r in range(ws)]
     for p in procs:
         p.start()
-    out = dict(q.get(timeout=120) for _ in range(ws))
+    try:
+        out = dict(q.get(timeout=120) for _ in range(ws))
+    finally:
+        received.set()
     for p in procs:
         p.join(timeout=60)
+        if p.is_alive():
+            p.terminate()
     return out
 
 
