@@ -65,9 +65,9 @@ def set_encoder_cluster(cluster_ctas: int) -> None:
 
 def set_encoder_cluster_pairs(pairs_per_cluster: int) -> None:
     """Tile pairs per cluster of the cluster-split ACS
-    (``exl3_encoder_set_cluster_pairs``): 0 automatic, 1 / 2 / 4 forced (2 and
-    4 exist for clusters of 8 CTAs). Process-wide; outputs are bit-identical
-    for every setting."""
+    (``exl3_encoder_set_cluster_pairs``): 0 automatic, 1 / 2 forced (2 exists
+    for clusters of 8 CTAs). Process-wide; outputs are bit-identical for every
+    setting."""
     _check(lib().exl3_encoder_set_cluster_pairs(int(pairs_per_cluster)))
 
 

@@ -566,7 +566,7 @@ int g_cluster_policy = 0;  // 0 automatic, 1 never, 2/4/8 forced
 std::atomic<unsigned long long> g_cluster_wait_ns{kClusterWaitNs};
 std::atomic<int> g_cluster_stop_at{-1};  // test hook: step at which sends stop
 
-std::atomic<int> g_cluster_pairs{0};  // 0 automatic, 1 / 2 / 4 forced
+std::atomic<int> g_cluster_pairs{0};  // 0 automatic, 1 / 2 forced
 
 template <int K, int C, int P>
 struct ClusterKernels {
@@ -637,9 +637,7 @@ struct ClusterKernels {
 };
 
 // The (C, P) combinations built: one pair per cluster of 2, 4 or 8 CTAs, and
-// 2 or 4 pairs per cluster of 8 CTAs (a cluster of 8 at K >= 3 has one or
-// two edges per thread and step, so extra pairs add little to a step whose
-// time is mostly its barrier and exchange).
+// 2 pairs per cluster of 8 CTAs (one exchange round per step for both).
 template <int K, class F>
 int with_kernels(int C, int P, F&& f) {
   if constexpr (K >= 2 && K <= 6) {
@@ -647,7 +645,6 @@ int with_kernels(int C, int P, F&& f) {
     if (C == 4 && P == 1) return f(ClusterKernels<K, 4, 1>{});
     if (C == 8 && P == 1) return f(ClusterKernels<K, 8, 1>{});
     if (C == 8 && P == 2) return f(ClusterKernels<K, 8, 2>{});
-    if (C == 8 && P == 4) return f(ClusterKernels<K, 8, 4>{});
   }
   return -1;
 }
@@ -660,11 +657,15 @@ int max_active_for(int C, int P, int dev) {
 
 // Automatic choice for a call of `pairs` tile pairs (C = 1: no split): every
 // group of P pairs must fit on the device at once, and C * groups SMs must
-// not exceed the device's. Preference, measured: one pair per cluster of 8;
-// then 2 pairs per cluster of 8 (one exchange round for both) over one pair
-// per cluster of 4; then 4 pairs per cluster of 8; then one pair per
-// cluster of 2 (K >= 3: at K = 2 a CTA pair exchanges 16 KiB per CTA and
-// step, which costs as much as the halved arithmetic saves).
+// not exceed the device's. Preference, measured per call (ms, 16 / 32 / 48 /
+// 64 / 96 tiles): one pair per cluster of 8 (K=2: 0.42 / - / - ; K=4: 0.51)
+// first. K = 2 then takes 2 pairs per cluster of 8 (0.58 / 0.64 at 32 / 48
+// tiles, against 0.73 / 0.79 at 4 CTAs per pair, whose CTAs exchange 16 KiB
+// each per step), then 4 CTAs per pair (0.84 at 64); a cluster of 2 at K = 2
+// exchanges 32 KiB per CTA and step and is not used. K >= 3 takes 4 CTAs per
+// pair (K=4: 0.56 / 0.57 / 0.60 at 32 / 48 / 64, against 0.62 / 0.63 for 2
+// pairs per cluster of 8), then 2 (0.78 / 0.80 at 96 / 128). Beyond those the
+// pair kernel (one pair per CTA) wins (K=2: 0.87 at 96 and 128).
 template <int K>
 void choose(int pairs, int sms, int dev, int* C_out, int* P_out) {
   *C_out = 1;
@@ -675,12 +676,15 @@ void choose(int pairs, int sms, int dev, int* C_out, int* P_out) {
     const int groups = (pairs + P - 1) / P;
     return (int64_t)groups * C <= sms && max_active_for<K>(C, P, dev) >= groups;
   };
-  static constexpr int kOrder[5][2] = {{8, 1}, {8, 2}, {4, 1}, {8, 4}, {2, 1}};
-  for (const auto& o : kOrder) {
-    const int C = o[0], P = o[1];
+  static constexpr int kOrderK2[3][2] = {{8, 1}, {8, 2}, {4, 1}};
+  static constexpr int kOrderK3[4][2] = {{8, 1}, {4, 1}, {2, 1}, {8, 2}};
+  const int(*order)[2] = K == 2 ? kOrderK2 : kOrderK3;
+  const int norder = K == 2 ? 3 : 4;
+  for (int q = 0; q < norder; ++q) {
+    const int C = order[q][0], P = order[q][1];
     if (g_cluster_policy >= 2 && C != g_cluster_policy) continue;
     if (forced_p > 0 && P != forced_p) continue;
-    if (K == 2 && C == 2 && g_cluster_policy != 2) continue;
+    if (K >= 3 && P == 2 && forced_p != 2) continue;   // only when forced
     if (fits(C, P)) {
       *C_out = C;
       *P_out = P;
@@ -688,7 +692,7 @@ void choose(int pairs, int sms, int dev, int* C_out, int* P_out) {
     }
   }
   if (g_cluster_policy >= 2) {  // forced size: its smallest P that the device holds at all
-    for (int P : {1, 2, 4}) {
+    for (int P : {1, 2}) {
       if (forced_p > 0 && P != forced_p) continue;
       if (max_active_for<K>(g_cluster_policy, P, dev) > 0) {
         *C_out = g_cluster_policy;
@@ -779,9 +783,8 @@ extern "C" int exl3_encoder_set_cluster(int cluster_ctas) {
 }
 
 extern "C" int exl3_encoder_set_cluster_pairs(int pairs_per_cluster) {
-  EXL3_REQUIRE(pairs_per_cluster == 0 || pairs_per_cluster == 1 || pairs_per_cluster == 2 ||
-                   pairs_per_cluster == 4,
-               "pairs per cluster must be 0 (automatic), 1, 2 or 4, got %d", pairs_per_cluster);
+  EXL3_REQUIRE(pairs_per_cluster == 0 || pairs_per_cluster == 1 || pairs_per_cluster == 2,
+               "pairs per cluster must be 0 (automatic), 1 or 2, got %d", pairs_per_cluster);
   g_cluster_pairs.store(pairs_per_cluster);
   return EXL3_OK;
 }

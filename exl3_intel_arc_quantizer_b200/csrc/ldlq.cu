@@ -223,9 +223,9 @@ void ws_layout(const exl3_ldlq_job* jobs, int njobs, int K, size_t* prod_off, si
 
 // Estimated device time (arbitrary units) of one LDLQ step that encodes
 // `tiles` tiles at K bits: the encoder's latency floor by cluster split for
-// few tile pairs (measured: ~0.45 at 8 CTAs per pair, 0.57-0.78 at 4, 0.8
-// at 2; estimated ~0.55 / ~0.7 at 8 CTAs per 2 / 4 pairs), one unit per wave
-// of one pair per SM beyond that.
+// few tile pairs (measured: ~0.45 at 8 CTAs per pair, ~0.6 at 8 CTAs per 2
+// pairs, 0.57-0.78 at 4, 0.8 at 2), one unit per wave of one pair per SM
+// beyond that.
 void step_costs(int K, int max_tiles, std::vector<double>& cost) {
   cost.assign((size_t)max_tiles + 1, 0.0);
   const int sms = sm_count();
@@ -237,7 +237,7 @@ void step_costs(int K, int max_tiles, std::vector<double>& cost) {
     const int pairs = (t + 1) / 2;
     int c = 1, pp = 1;
     cluster_choice(K, pairs, &c, &pp);
-    if (c == 8) cost[t] = pp == 1 ? 0.45 : (pp == 2 ? 0.55 : 0.7);
+    if (c == 8) cost[t] = pp == 1 ? 0.45 : 0.6;
     else if (c == 4) cost[t] = K == 2 ? 0.78 : 0.57;
     else if (c == 2) cost[t] = 0.8;
     else cost[t] = (double)((pairs + sms - 1) / sms);

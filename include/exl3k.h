@@ -319,9 +319,9 @@ int exl3_encoder_set_cluster(int cluster_ctas);
 
 /*
  * Tile pairs per cluster of the cluster-split ACS: 0 = automatic (one pair
- * per cluster while the clusters fit; then 2 or 4 pairs per cluster of 8
- * CTAs, which share one exchange round per step), 1 / 2 / 4 = always that
- * many (tests, benchmarks; 2 and 4 exist for clusters of 8 CTAs). Outputs are
+ * per cluster while the clusters fit; at K = 2 then 2 pairs per cluster of 8
+ * CTAs, which share one exchange round per step), 1 / 2 = always that many
+ * (tests, benchmarks; 2 exists for clusters of 8 CTAs). Outputs are
  * bit-identical for every setting. Process-wide. No counterpart in the
  * reference.
  */

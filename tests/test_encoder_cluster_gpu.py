@@ -153,9 +153,9 @@ def test_last_partial_wave_split_matches_off(K):
 
 
 @pytest.mark.parametrize("K", [2, 3, 4, 5, 6])
-@pytest.mark.parametrize("pairs", [2, 4])
+@pytest.mark.parametrize("pairs", [2])
 def test_several_pairs_per_cluster_match_c_oracle(K, pairs):
-    """Clusters of 8 CTAs serving 2 or 4 tile pairs per exchange round; 11
+    """Clusters of 8 CTAs serving 2 tile pairs per exchange round; 11
     tiles: the last group repeats its first pair (and the last pair is a
     lone tile), so groups with missing pairs and odd tile counts are covered."""
     n = 11
@@ -170,11 +170,11 @@ def test_several_pairs_per_cluster_match_c_oracle(K, pairs):
 
 @pytest.mark.parametrize("K", [2, 4])
 def test_several_pairs_per_cluster_more_groups_than_clusters(K):
-    """200 pairs in groups of 2 and 4 over the resident clusters of 8 CTAs
-    (the clusters loop over groups): identical to one pair per CTA."""
+    """200 pairs in groups of 2 over the resident clusters of 8 CTAs (the
+    clusters loop over groups): identical to one pair per CTA."""
     tiles = _tiles(400, 7800 + K)
     base = _encode(K, tf.CB_MUL1, tiles, 1)
-    for pairs in (2, 4):
+    for pairs in (2,):
         got = _encode(K, tf.CB_MUL1, tiles, 8, pairs=pairs)
         for a, b, what in zip(got, base, ("indices", "packed", "cost", "recon")):
             np.testing.assert_array_equal(a, b, err_msg=f"{pairs} pairs {what}")
@@ -191,4 +191,4 @@ def test_automatic_policy_with_several_pairs_matches_off():
             for a, b in zip(auto, off):
                 np.testing.assert_array_equal(a, b)
     with pytest.raises(RuntimeError):
-        set_encoder_cluster_pairs(3)
+        set_encoder_cluster_pairs(4)
