@@ -1,13 +1,14 @@
 // Weight regularization and the block-LDL fold on the device.
 //
 // Regularization (reference exl3_quant/regularize.py:83-211, the order of
-// upstream quantize.py:1130-1236) of a (k, n) fp32 weight W, in six launches
-// and no host round trip:
+// upstream quantize.py:1130-1236) of a (k, n) fp32 weight W, in seven
+// launches and no host round trip:
 //   reg_skew_kernel      skew = (sum of the k/50 largest sqrt(H_ii)) / (sum of
 //                        all), by a radix select over the float bits (one CTA)
 //   reg_colsq_kernel     sum of W^2 over each 32-row slice of each column
-//   reg_colfinal_kernel  column RMS (slices added in order), their mean, the
-//                        output-scale decision, sv and the column divisors
+//   reg_colrms_kernel    column RMS (slices added in order)
+//   reg_colfinal_kernel  their mean, the output-scale decision, sv and the
+//                        column divisors (one CTA)
 //   reg_right_kernel     W / sv, then the 128-column Hadamard of each row (the
 //                        shared FWHT), plus each row's sum of squares over
 //                        each 32-column slice
@@ -19,9 +20,10 @@
 //
 // Block-LDL fold (reference exl3_quant/ldlq.py:96-117): with C the Cholesky
 // factor of H and D_b its 16x16 diagonal blocks, L[:, b] = C[:, b] D_b^-1
-// and the diagonal blocks become identities. One CTA per 64 x 64 tile of L
-// inverts the (lower-triangular) D_b of its four block columns by forward
-// substitution and multiplies its rows; tiles above the diagonal are zeros.
+// and the diagonal blocks become identities. ldl_inv_kernel inverts every
+// (lower-triangular) D_b once by forward substitution; ldl_fold_kernel, one
+// CTA per 64 x 64 tile of L, multiplies its rows by the four inverses of its
+// block columns; tiles above the diagonal are zeros.
 #include "common.cuh"
 #include "hadamard.cuh"
 
@@ -126,12 +128,20 @@ __global__ void reg_colsq_kernel(const float* __restrict__ W, int64_t k, int64_t
   partial[b * n + c] = s;
 }
 
-// Column RMS (the 32-row slices added in order), their mean, the output-scale
-// decision (regularize.py:145-182), out_scales, the column divisors of W and
-// sv. One CTA of 1024 threads.
+// Column RMS: the 32-row slice sums of a column added in slice order
+__global__ void reg_colrms_kernel(const float* __restrict__ partial, int64_t nb, int64_t k,
+                                  int64_t n, float* __restrict__ out_scales) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= n) return;
+  float acc = partial[c];
+  for (int64_t b = 1; b < nb; ++b) acc = __fadd_rn(acc, partial[b * n + c]);
+  out_scales[c] = sqrtf(__fdiv_rn(acc, (float)k));
+}
+
+// The column RMS mean, the output-scale decision (regularize.py:145-182),
+// out_scales, the column divisors of W and sv. One CTA of 1024 threads.
 __global__ void __launch_bounds__(1024) reg_colfinal_kernel(
-    const float* __restrict__ partial, int64_t nb, int64_t k, int64_t n,
-    const float* __restrict__ sv_in, int force, int q_fallback, int has_skew,
+    int64_t n, const float* __restrict__ sv_in, int force, int q_fallback, int has_skew,
     RegInfo* __restrict__ info, float* __restrict__ out_scales, float* __restrict__ divisor,
     float* __restrict__ sv_out) {
   __shared__ float red[32];
@@ -139,13 +149,7 @@ __global__ void __launch_bounds__(1024) reg_colfinal_kernel(
   __shared__ float s_mean;
   const int t = threadIdx.x;
   float local = 0.f;
-  for (int64_t c = t; c < n; c += blockDim.x) {
-    float acc = partial[c];
-    for (int64_t b = 1; b < nb; ++b) acc = __fadd_rn(acc, partial[b * n + c]);
-    const float rms = sqrtf(__fdiv_rn(acc, (float)k));
-    out_scales[c] = rms;
-    local += rms;
-  }
+  for (int64_t c = t; c < n; c += blockDim.x) local += out_scales[c];
   const float sum = block_sum_f(local, red);
   if (t == 0) {
     const float mean = __fdiv_rn(sum, (float)n);
@@ -252,11 +256,41 @@ __global__ void reg_left_kernel(float* __restrict__ work, const float* __restric
   }
 }
 
+// D_b^-1 of every 16x16 diagonal block of C (lower triangular) by forward
+// substitution: one CTA per four blocks, D staged in shared memory, thread
+// (g, j) computes column j of block g's inverse.
+__global__ void __launch_bounds__(64) ldl_inv_kernel(const float* __restrict__ chol,
+                                                     float* __restrict__ inverses, int64_t m,
+                                                     int64_t n) {
+  __shared__ float D[4][16][17];
+  const int t = threadIdx.x, g = t >> 4, j = t & 15;
+  const int64_t b = (int64_t)blockIdx.x * 4 + g;
+  if (b < m) {
+    const float* src = chol + (b * 16) * n + b * 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) D[g][i][j] = src[(int64_t)i * n + j];
+  }
+  __syncthreads();
+  if (b >= m) return;
+  float x[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = 0.f;
+  x[j] = __fdiv_rn(1.f, D[g][j][j]);
+  for (int i = j + 1; i < 16; ++i) {
+    float acc = 0.f;
+    for (int p = j; p < i; ++p) acc = fmaf(D[g][i][p], x[p], acc);
+    x[i] = -__fdiv_rn(acc, D[g][i][i]);
+  }
+  float* out = inverses + b * 256;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) out[i * 16 + j] = x[i];
+}
+
 // L = C D^-1 per 16-column block, identity diagonal blocks, zeros above:
 // one CTA per 64 x 64 tile (4 block columns); n % 16 == 0.
 __global__ void __launch_bounds__(256) ldl_fold_kernel(const float* __restrict__ chol,
                                                        float* __restrict__ L,
-                                                       float* __restrict__ inverses,
+                                                       const float* __restrict__ inverses,
                                                        int64_t n) {
   __shared__ float X[4][16][17];  // D_g^-1 of the tile's block columns g = 0..3
   __shared__ float T[64][65];     // the tile of C
@@ -281,28 +315,9 @@ __global__ void __launch_bounds__(256) ldl_fold_kernel(const float* __restrict__
     T[r][c + 2] = v.z;
     T[r][c + 3] = v.w;
   }
-  if (t < 64) {  // column j of D_g^-1 by forward substitution (D lower triangular)
-    const int g = t >> 4, j = t & 15;
-    const int64_t b0 = c0 + 16 * g;
-    if (16 * g < cols) {
-      const float* D = chol + b0 * n + b0;
-      float x[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) x[i] = 0.f;
-      x[j] = __fdiv_rn(1.f, D[(int64_t)j * n + j]);
-      for (int i = j + 1; i < 16; ++i) {
-        float s = 0.f;
-        for (int p = j; p < i; ++p) s = fmaf(D[(int64_t)i * n + p], x[p], s);
-        x[i] = -__fdiv_rn(s, D[(int64_t)i * n + i]);
-      }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) X[g][i][j] = x[i];
-      if (inverses && r0 == c0) {
-        float* out = inverses + (b0 / 16) * 256;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) out[i * 16 + j] = x[i];
-      }
-    }
+  for (int i = t; i < 4 * 256; i += 256) {
+    const int g = i >> 8, e = i & 255;
+    if (16 * g < cols) X[g][e >> 4][e & 15] = inverses[((c0 >> 4) + g) * 256 + e];
   }
   __syncthreads();
   const int r = t >> 2, g = t & 3;  // row r, block column g: 16 outputs
@@ -318,10 +333,10 @@ __global__ void __launch_bounds__(256) ldl_fold_kernel(const float* __restrict__
   } else {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      float s = 0.f;
+      float acc = 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) s = fmaf(T[r][16 * g + i], X[g][i][j], s);
-      o[j] = s;
+      for (int i = 0; i < 16; ++i) acc = fmaf(T[r][16 * g + i], X[g][i][j], acc);
+      o[j] = acc;
     }
   }
   float4* dst = reinterpret_cast<float4*>(L + grow * n + c0 + 16 * g);
@@ -389,8 +404,10 @@ extern "C" int exl3_regularize(const float* W, const float* su_in, const float* 
   const int64_t nb = (k + 31) / 32;
   reg_colsq_kernel<<<dim3((unsigned)((n + 255) / 256), (unsigned)nb), 256, 0, s>>>(W, k, n, cp);
   EXL3_LAUNCHED();
-  reg_colfinal_kernel<<<1, 1024, 0, s>>>(cp, nb, k, n, sv_in, force_out_scales, q_fallback,
-                                        has_skew, inf, out_scales, dv, sv_out);
+  reg_colrms_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(cp, nb, k, n, out_scales);
+  EXL3_LAUNCHED();
+  reg_colfinal_kernel<<<1, 1024, 0, s>>>(n, sv_in, force_out_scales, q_fallback, has_skew, inf,
+                                        out_scales, dv, sv_out);
   EXL3_LAUNCHED();
   const int64_t warps = k * (n / 128);
   reg_right_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(W, dv, work, rp, k, n);
@@ -406,7 +423,7 @@ extern "C" int exl3_regularize(const float* W, const float* su_in, const float* 
 
 extern "C" int exl3_block_ldl_fold(const float* chol, float* L, float* inverses, int64_t n,
                                    exl3_stream_t stream) {
-  EXL3_REQUIRE(chol && L, "NULL pointer argument");
+  EXL3_REQUIRE(chol && L && inverses, "NULL pointer argument");
   EXL3_REQUIRE(chol != L, "L must not alias the Cholesky factor");
   EXL3_REQUIRE(n > 0 && n % 16 == 0, "n (%lld) must be a positive multiple of 16", (long long)n);
   EXL3_REQUIRE(reinterpret_cast<uintptr_t>(chol) % 16 == 0 &&
@@ -414,6 +431,9 @@ extern "C" int exl3_block_ldl_fold(const float* chol, float* L, float* inverses,
                "chol and L must be 16-byte aligned");
   const int64_t tiles = (n + 63) / 64;
   EXL3_REQUIRE(tiles < 65536, "matrix too large");
+  const int64_t m = n / 16;
+  ldl_inv_kernel<<<(unsigned)((m + 3) / 4), 64, 0, (cudaStream_t)stream>>>(chol, inverses, m, n);
+  EXL3_LAUNCHED();
   ldl_fold_kernel<<<dim3((unsigned)tiles, (unsigned)tiles), 256, 0, (cudaStream_t)stream>>>(
       chol, L, inverses, n);
   EXL3_LAUNCHED();

@@ -207,13 +207,16 @@ void block_ldl_fold(at::Tensor chol, at::Tensor L, c10::optional<at::Tensor> inv
   const int64_t n = chol.size(0);
   TORCH_CHECK(chol.size(1) == n && L.size(0) == n && L.size(1) == n, "square (n, n) matrices");
   TORCH_CHECK(L.device() == chol.device(), "chol and L must be on the same device");
-  float* inv = nullptr;
+  at::Tensor inv_t;
   if (inverses.has_value() && inverses->defined()) {
-    TORCH_CHECK(inverses->is_cuda() && inverses->is_contiguous() &&
-                    inverses->scalar_type() == at::kFloat && inverses->numel() == n * 16,
-                "inverses must be a contiguous float32 (n/16, 16, 16) CUDA tensor");
-    inv = inverses->data_ptr<float>();
+    inv_t = *inverses;
+    TORCH_CHECK(inv_t.is_cuda() && inv_t.is_contiguous() && inv_t.scalar_type() == at::kFloat &&
+                    inv_t.numel() == n * 16 && inv_t.device() == chol.device(),
+                "inverses must be a contiguous float32 (n/16, 16, 16) tensor on chol's device");
+  } else {
+    inv_t = at::empty({n / 16, 16, 16}, chol.options());
   }
+  float* inv = inv_t.data_ptr<float>();
   c10::cuda::CUDAGuard g(chol.device());
   check(exl3_block_ldl_fold(chol.data_ptr<float>(), L.data_ptr<float>(), inv, n, cur_stream(chol)),
         "block_ldl_fold");

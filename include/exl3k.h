@@ -269,7 +269,7 @@ int exl3_regularize(const float* W, const float* su_in, const float* sv_in,
  * Block-LDL fold: from the (n, n) lower Cholesky factor C (n % 16 == 0,
  * 16-byte aligned), L[:, b] = C[:, b] D_b^-1 for every 16-column block b with
  * D_b = C's 16x16 diagonal block, identity diagonal blocks and zeros above
- * them; `inverses` (nullable) receives the (n/16, 16, 16) D_b^-1. Replaces the
+ * them; `inverses` receives the (n/16, 16, 16) D_b^-1. Replaces the
  * fold of block_ldl (exl3_quant/ldlq.py:96-117); the factorization itself
  * stays cuSOLVER's potrf with the reference's retry schedule.
  */
