@@ -32,4 +32,50 @@ __device__ __forceinline__ void fwht128_warp(float (&v)[4], int lane) {
   v[3] = a1 - a3;
 }
 
+// H128 (x / su) on the columns of one 128-row block, four threads per
+// column: thread (c, q) holds rows 4i + q (i < 32) of column c in registers;
+// the butterflies of strides 1 and 2 are shuffles with the partner lanes, the
+// five wider ones run in registers (the order and roundings of
+// fwht128_warp). A warp's loads and stores cover 8 columns of four rows: four
+// full 32-byte sectors, no shared memory. DIV: divide by su[row] first (the
+// regularization's left step); else the plain rotation. Every lane of the
+// warp must call it (the shuffles are warp-wide); a lane whose column is past
+// the matrix passes valid = false and neither loads nor stores.
+template <bool DIV>
+__device__ __forceinline__ void had_left_quad_cols(float* __restrict__ col, int64_t n,
+                                                   const float* __restrict__ su, int q,
+                                                   bool valid) {
+  float v[32];
+  const int64_t step = 4 * n;
+  const float* src = col + (int64_t)q * n;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float x = valid ? *src : 0.f;
+    src += step;
+    v[i] = DIV ? __fdiv_rn(x, su[4 * i + q]) : x;
+  }
+  const float s1 = (q & 1) ? -1.0f : 1.0f, s2 = (q & 2) ? -1.0f : 1.0f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = had_bfly(v[i], __shfl_xor_sync(0xFFFFFFFFu, v[i], 1), s1);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = had_bfly(v[i], __shfl_xor_sync(0xFFFFFFFFu, v[i], 2), s2);
+#pragma unroll
+  for (int h = 1; h < 32; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (i & h) continue;
+      const float lo = v[i], hi = v[i + h];
+      v[i] = lo + hi;
+      v[i + h] = lo - hi;
+    }
+  }
+  if (!valid) return;
+  float* dst = col + (int64_t)q * n;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    *dst = __fmul_rn(v[i], kHad128Scale);
+    dst += step;
+  }
+}
+
 }  // namespace exl3

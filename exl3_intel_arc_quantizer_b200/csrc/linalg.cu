@@ -35,32 +35,15 @@ __global__ void had_right_kernel(float* __restrict__ x, int64_t k, int64_t n, fl
   for (int q = 0; q < 4; ++q) p[lane + 32 * q] = v[q] * scale;
 }
 
-// H @ x on 128-row blocks: a CTA takes a 128 x 32 tile through shared
-// memory; warp w transforms columns w, w+8, w+16, w+24 along the rows.
-__global__ void had_left_kernel(float* __restrict__ x, int64_t k, int64_t n, float scale) {
-  __shared__ float tile[128][33];
-  const int64_t rb = blockIdx.y, cb = blockIdx.x;
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  float* base = x + rb * 128 * n + cb * 32;
-  const int ncols = (int)((n - cb * 32) < 32 ? (n - cb * 32) : 32);
-  for (int i = t; i < 128 * 32; i += blockDim.x) {
-    const int r = i >> 5, c = i & 31;
-    tile[r][c] = (c < ncols) ? base[(int64_t)r * n + c] : 0.f;
-  }
-  __syncthreads();
-  for (int c = warp; c < 32; c += 8) {
-    float v[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) v[q] = tile[lane + 32 * q][c];
-    fwht128_warp(v, lane);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) tile[lane + 32 * q][c] = v[q] * scale;
-  }
-  __syncthreads();
-  for (int i = t; i < 128 * 32; i += blockDim.x) {
-    const int r = i >> 5, c = i & 31;
-    if (c < ncols) base[(int64_t)r * n + c] = tile[r][c];
-  }
+// H @ x on 128-row blocks: a CTA of 256 threads takes 64 columns of one row
+// block, four threads per column (had_left_quad_cols).
+__global__ void __launch_bounds__(256, 2) had_left_kernel(float* __restrict__ x, int64_t k,
+                                                          int64_t n) {
+  const int t = threadIdx.x;
+  const int64_t c = (int64_t)blockIdx.x * 64 + (t >> 2);
+  const bool valid = c < n;
+  had_left_quad_cols<false>(x + (int64_t)blockIdx.y * 128 * n + (valid ? c : 0), n, nullptr,
+                            t & 3, valid);
 }
 
 // diag mean of H / count (one CTA)
@@ -121,8 +104,8 @@ extern "C" int exl3_had128_left(float* x, int64_t k, int64_t n, exl3_stream_t st
   EXL3_REQUIRE(n > 0 && k > 0 && k % 128 == 0, "rows (%lld) must be a positive multiple of 128",
                (long long)k);
   EXL3_REQUIRE(k / 128 < 65536, "too many row blocks");
-  dim3 grid((unsigned)((n + 31) / 32), (unsigned)(k / 128));
-  had_left_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, k, n, 0.08838834764831845f);
+  dim3 grid((unsigned)((n + 63) / 64), (unsigned)(k / 128));
+  had_left_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, k, n);
   EXL3_LAUNCHED();
   return EXL3_OK;
 }

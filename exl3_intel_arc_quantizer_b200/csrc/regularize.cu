@@ -13,7 +13,8 @@
 //                        shared FWHT), plus each row's sum of squares over
 //                        each 32-column slice
 //   reg_rowfinal_kernel  row RMS (slices added in order) and su
-//   reg_left_kernel      work / su, then the 128-row Hadamard
+//   reg_left_kernel      work / su, then the 128-row Hadamard (four threads
+//                        per column, no shared memory)
 // The reference's sums (torch reductions) have their own order; here every
 // slice sum is one fixed order and the slices are added in the reference's
 // slice order, so results agree to fp32 rounding.
@@ -226,34 +227,16 @@ __global__ void reg_rowfinal_kernel(const float* __restrict__ rpart, int64_t ns,
   su_out[row] = __fadd_rn(__fdiv_rn(__fmul_rn(su_in[row], rms), kCodebookScale), kRegEps);
 }
 
-// work = H128 (work / su) on 128-row blocks: a CTA takes a 128 x 32 tile
-// through shared memory (the layout of had_left_kernel)
-__global__ void reg_left_kernel(float* __restrict__ work, const float* __restrict__ su,
-                                int64_t k, int64_t n) {
-  __shared__ float tile[128][33];
-  const int64_t rb = blockIdx.y, cb = blockIdx.x;
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  float* base = work + rb * 128 * n + cb * 32;
-  const float* s = su + rb * 128;
-  const int ncols = (int)((n - cb * 32) < 32 ? (n - cb * 32) : 32);
-  for (int i = t; i < 128 * 32; i += blockDim.x) {
-    const int r = i >> 5, c = i & 31;
-    tile[r][c] = (c < ncols) ? __fdiv_rn(base[(int64_t)r * n + c], s[r]) : 0.f;
-  }
-  __syncthreads();
-  for (int c = warp; c < 32; c += 8) {
-    float v[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) v[q] = tile[lane + 32 * q][c];
-    fwht128_warp(v, lane);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) tile[lane + 32 * q][c] = __fmul_rn(v[q], kHad128Scale);
-  }
-  __syncthreads();
-  for (int i = t; i < 128 * 32; i += blockDim.x) {
-    const int r = i >> 5, c = i & 31;
-    if (c < ncols) base[(int64_t)r * n + c] = tile[r][c];
-  }
+// work = H128 (work / su) on 128-row blocks: a CTA of 256 threads takes 64
+// columns of one row block, four threads per column (had_left_quad_cols)
+__global__ void __launch_bounds__(256, 2) reg_left_kernel(float* __restrict__ work,
+                                                          const float* __restrict__ su,
+                                                          int64_t k, int64_t n) {
+  const int t = threadIdx.x;
+  const int64_t c = (int64_t)blockIdx.x * 64 + (t >> 2);
+  const bool valid = c < n;
+  had_left_quad_cols<true>(work + (int64_t)blockIdx.y * 128 * n + (valid ? c : 0), n,
+                           su + (int64_t)blockIdx.y * 128, t & 3, valid);
 }
 
 // D_b^-1 of every 16x16 diagonal block of C (lower triangular) by forward
@@ -415,8 +398,8 @@ extern "C" int exl3_regularize(const float* W, const float* su_in, const float* 
   reg_rowfinal_kernel<<<(unsigned)((k + 255) / 256), 256, 0, s>>>(rp, n / 32, k, n, su_in,
                                                                    in_scales, su_out);
   EXL3_LAUNCHED();
-  reg_left_kernel<<<dim3((unsigned)((n + 31) / 32), (unsigned)(k / 128)), 256, 0, s>>>(work,
-                                                                                     su_out, k, n);
+  reg_left_kernel<<<dim3((unsigned)((n + 63) / 64), (unsigned)(k / 128)), 256, 0, s>>>(
+      work, su_out, k, n);
   EXL3_LAUNCHED();
   return EXL3_OK;
 }
