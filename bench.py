@@ -505,9 +505,10 @@ def run_storage(device, K=4, shapes=((4096, 4096), (12288, 4096)), reps=5):
         a = torch.randn((k, k // 2), generator=g, device=device)
         chol = torch.linalg.cholesky(a @ a.T / k + 0.05 * torch.eye(k, device=device)).contiguous()
         L = torch.empty_like(chol)
+        inv = torch.empty((k // 16, 16, 16), device=device)
         del a
-        t_fold = timed(lambda: e.block_ldl_fold(chol, L, None))
-        del W0, regs, chol, L
+        t_fold = timed(lambda: e.block_ldl_fold(chol, L, inv))
+        del W0, regs, chol, L, inv
         wts = k * n
         row = {"shape": [k, n], "K": K,
                "pack_ms": t_pack, "pack_gbs": wts * (2 + K / 8) / t_pack / 1e6,

@@ -45,6 +45,7 @@ def _declare(handle: ctypes.CDLL) -> None:
     handle.exl3_quantize_tiles_ws_bytes.argtypes = [c.c_int64, c.c_int, c.c_int]
     handle.exl3_encoder_set_cluster.argtypes = [c.c_int]
     handle.exl3_encoder_set_cluster_pairs.argtypes = [c.c_int]
+    handle.exl3_hessian_set_tile.argtypes = [c.c_int]
     handle.exl3_encoder_fault_count.argtypes = [c.POINTER(c.c_uint)]
     handle.exl3_encoder_test_cluster_wait.argtypes = [c.c_longlong, c.c_int]
     handle.exl3_encoder_cluster_capacity.argtypes = [c.c_int, c.c_int, c.POINTER(c.c_int)]
@@ -69,6 +70,13 @@ def set_encoder_cluster_pairs(pairs_per_cluster: int) -> None:
     for clusters of 8 CTAs). Process-wide; outputs are bit-identical for every
     setting."""
     _check(lib().exl3_encoder_set_cluster_pairs(int(pairs_per_cluster)))
+
+
+def set_hessian_tile(mode: int) -> None:
+    """Tile shape of the Hessian accumulation (``exl3_hessian_set_tile``):
+    0 chosen by width (default), 1 = 128 x 256 tiles, 2 = 256 x 256 tiles.
+    Process-wide; the sums are bit-identical for every setting."""
+    _check(lib().exl3_hessian_set_tile(int(mode)))
 
 
 def encoder_cluster_capacity(K: int, cluster_ctas: int) -> int:

@@ -5,8 +5,8 @@
 // in fp32, so tcgen05 kind::f16 MMAs with fp32 accumulation compute the same
 // sums up to summation order.
 //
-// Design (one CTA per 128 x 256 tile of H that reaches the upper triangle;
-// 6 warps with fixed roles):
+// Design (one CTA per 128 x 256 tile of H that reaches the upper triangle,
+// or per 256 x 256 tile for wide H, see HGeo; 6 warps with fixed roles):
 //   * warp 0 (one lane) streams X through TMA: per 64-token chunk, the
 //     128-column A slab X[t:t+64, i0:i0+128] and the 256-column B slab
 //     X[t:t+64, j0:j0+256] as 64 x 64 boxes with 128-byte swizzle, straight
@@ -52,6 +52,22 @@ constexpr int kBoxBytes = 64 * kBK * 2;  // one 64-column x 64-token box, 8 KiB
 constexpr int kStgPitch = 33;
 constexpr int kStgBytes = 4 * 32 * kStgPitch * 4;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait
+
+// MB = 128-row A slabs per tile. MB = 1: 128 x 256 tiles, four stages of
+// 48 KiB and two accumulator sets in TMEM (a segment drains while the next
+// one accumulates). MB = 2: 256 x 256 tiles whose two halves share the B
+// slab (64 KiB per stage for twice the MMAs: a third less L2 traffic per
+// flop), three stages, one accumulator set (the MMAs wait for each drain).
+template <int MB>
+struct HGeo {
+  static constexpr int kStagesM = MB == 1 ? 4 : 3;
+  static constexpr int kABytesM = MB * kABytes;
+  static constexpr int kStageBytesM = kABytesM + kBBytes;
+  static constexpr int kNBuf = MB == 1 ? 2 : 1;
+  static constexpr size_t kSmem = 1024 + (size_t)kStagesM * kStageBytesM + kStgBytes + 12 * 8 + 16;
+  static_assert(kStagesM <= kStages, "barrier slots");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -144,28 +160,52 @@ __device__ __forceinline__ void red_add4(float* p, float a, float b, float c, fl
                : "memory");
 }
 
-// i-block bi (128 rows) pairs with the j-blocks bj >= bi/2 (256 columns):
-// the ones that reach column >= row somewhere. Launch order walks groups of
-// 8 consecutive i-blocks column by column (bi fastest), so the CTAs resident
-// at one time share few A and B slabs of X in L2.
+// MB = 1: i-block bi (128 rows) pairs with the j-blocks bj >= bi/2 (256
+// columns): the ones that reach column >= row somewhere. MB = 2 (SQ): 256 x
+// 256 blocks with bj >= bi. Launch order walks groups of 8 consecutive
+// i-blocks column by column (bi fastest), so the CTAs resident at one time
+// share few A and B slabs of X in L2.
 #ifndef EXL3_HESS_RASTER
 #define EXL3_HESS_RASTER 8
 #endif
 constexpr int kRasterGroup = EXL3_HESS_RASTER;
+// Tile shape by waves (one CTA per SM either way): a 256 x 256 tile costs
+// about 1.8 times a 128 x 256 one (twice the MMAs, a third less L2 traffic
+// per MMA; measured 1.75-1.83 on B200 with 262,144 tokens), so the shape
+// with fewer waves x cost wins: 256 x 256 at d = 4096, 12288, 14336 and
+// 128 x 256 at d = 2048 and 5120.
+constexpr double kSquareTileCost = 1.8;
 
+template <bool SQ>
+int64_t tile_count(int64_t d) {
+  const int64_t nbi = (d + kBM * (SQ ? 2 : 1) - 1) / (kBM * (SQ ? 2 : 1));
+  const int64_t nbj = (d + kBN - 1) / kBN;
+  int64_t n = 0;
+  for (int64_t bi = 0; bi < nbi; ++bi) n += nbj - (SQ ? bi : (bi >> 1));
+  return n;
+}
+
+int choose_mb(int64_t d, int sms) {
+  const int64_t w1 = (tile_count<false>(d) + sms - 1) / sms;
+  const int64_t w2 = (tile_count<true>(d) + sms - 1) / sms;
+  return (double)w2 * kSquareTileCost < (double)w1 ? 2 : 1;
+}
+
+template <bool SQ>
 __device__ __forceinline__ void tile_of(int idx, int nbi, int nbj, int& bi, int& bj) {
   int g0 = 0;
   for (;;) {
     const int g1 = min(g0 + kRasterGroup, nbi);
     int cnt = 0;
-    for (int b = g0; b < g1; ++b) cnt += nbj - (b >> 1);
+    for (int b = g0; b < g1; ++b) cnt += nbj - (SQ ? b : (b >> 1));
     if (idx < cnt) break;
     idx -= cnt;
     g0 = g1;
   }
   const int glast = min(g0 + kRasterGroup, nbi) - 1;
-  for (int j = g0 >> 1;; ++j) {
-    const int hi = min(glast, 2 * j + 1);  // bj >= bi/2  <=>  bi <= 2*bj + 1
+  for (int j = SQ ? g0 : (g0 >> 1);; ++j) {
+    // SQ: bj >= bi; else bj >= bi/2  <=>  bi <= 2*bj + 1
+    const int hi = min(glast, SQ ? j : 2 * j + 1);
     const int cnt = hi - g0 + 1;
     if (idx < cnt) {
       bi = g0 + idx;
@@ -176,25 +216,26 @@ __device__ __forceinline__ void tile_of(int idx, int nbi, int nbj, int& bi, int&
   }
 }
 
-template <int BF16>
+template <int BF16, int MB>
 __global__ void __launch_bounds__(kThreads, 1)
 hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, int64_t d,
                    float* __restrict__ H, int nbi, int nbj, int* __restrict__ err_flag) {
+  using G = HGeo<MB>;
   extern __shared__ uint8_t dsm_raw[];
   // 1024-byte alignment for the swizzled operand tiles
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* stage_base = smem;
-  float* stg = reinterpret_cast<float*>(smem + kStages * kStageBytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kStgBytes);
+  float* stg = reinterpret_cast<float*>(smem + G::kStagesM * G::kStageBytesM);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::kStagesM * G::kStageBytesM + kStgBytes);
   // bars: full[4], empty[4], accf[2], acce[2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int bi, bj;
-  tile_of(blockIdx.x, nbi, nbj, bi, bj);
-  const int i0 = bi * kBM, j0 = bj * kBN;
+  tile_of<MB == 2>(blockIdx.x, nbi, nbj, bi, bj);
+  const int i0 = bi * kBM * MB, j0 = bj * kBN;
   const int nchunks = (int)((T_tokens + kBK - 1) / kBK);
   const int nseg = (nchunks + kSegChunks - 1) / kSegChunks;
 
@@ -204,7 +245,7 @@ hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, i
   auto acce = [&](int b) { return smem_u32(&bars[2 * kStages + 2 + b]); };
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < G::kStagesM; ++s) {
       mbar_init(full(s), 1);
       mbar_init(empty(s), 1);
     }
@@ -231,24 +272,28 @@ hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, i
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
       int issued = 0;
       for (int c = 0; c < nchunks; ++c) {
-        const int s = c % kStages, r = c / kStages;
+        const int s = c % G::kStagesM, r = c / G::kStagesM;
         if (r > 0 && !mbar_wait(empty(s), (r - 1) & 1, abort_flag, false)) break;
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(full(s)),
-                     "r"(kStageBytes)
+                     "r"(G::kStageBytesM)
                      : "memory");
-        const uint32_t a = smem_u32(stage_base + s * kStageBytes);
-        const uint32_t b = a + kABytes;
+        const uint32_t a = smem_u32(stage_base + s * G::kStageBytesM);
+        const uint32_t b = a + G::kABytesM;
         const int t0 = c * kBK;
-        tma_load_2d(a, &xmap, i0, t0, full(s));
-        tma_load_2d(a + kBoxBytes, &xmap, i0 + 64, t0, full(s));
+#pragma unroll
+        for (int m = 0; m < MB; ++m) {
+          tma_load_2d(a + m * kABytes, &xmap, i0 + 128 * m, t0, full(s));
+          tma_load_2d(a + m * kABytes + kBoxBytes, &xmap, i0 + 128 * m + 64, t0, full(s));
+        }
 #pragma unroll
         for (int q = 0; q < 4; ++q) tma_load_2d(b + q * kBoxBytes, &xmap, j0 + 64 * q, t0, full(s));
         issued = c + 1;
       }
       // stopped early: every copy in flight must land before the CTA exits
       if (issued < nchunks) {
-        const int first = issued > kStages ? issued - kStages : 0;
-        for (int c = first; c < issued; ++c) mbar_drain(full(c % kStages), (c / kStages) & 1);
+        const int first = issued > G::kStagesM ? issued - G::kStagesM : 0;
+        for (int c = first; c < issued; ++c)
+          mbar_drain(full(c % G::kStagesM), (c / G::kStagesM) & 1);
       }
     }
   } else if (warp == 1) {
@@ -257,28 +302,31 @@ hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, i
       const uint32_t idesc = make_idesc(BF16);
       int last_commit = -1;
       for (int c = 0; c < nchunks; ++c) {
-        const int s = c % kStages, r = c / kStages;
-        const int seg = c / kSegChunks, buf = seg & 1;
+        const int s = c % G::kStagesM, r = c / G::kStagesM;
+        const int seg = c / kSegChunks, buf = seg % G::kNBuf;
         const bool seg_first = (c % kSegChunks) == 0;
         const bool seg_last = (c % kSegChunks) == kSegChunks - 1 || c == nchunks - 1;
-        if (seg_first && seg >= 2) {
-          if (!mbar_wait(acce(buf), ((seg >> 1) - 1) & 1, abort_flag, false)) break;
+        if (seg_first && seg >= G::kNBuf) {
+          if (!mbar_wait(acce(buf), ((seg / G::kNBuf) - 1) & 1, abort_flag, false)) break;
         }
         if (!mbar_wait(full(s), r & 1, abort_flag, false)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a0 = smem_u32(stage_base + s * kStageBytes);
-        const uint32_t b0 = a0 + kABytes;
-        const uint32_t dacc = tmem + (uint32_t)(buf * kBN);
+        const uint32_t a0 = smem_u32(stage_base + s * G::kStageBytesM);
+        const uint32_t b0 = a0 + G::kABytesM;
 #pragma unroll
         for (int ks = 0; ks < kBK / 16; ++ks) {
-          const uint64_t da = make_desc_sw128(a0 + ks * 2 * kSBO);
           const uint64_t db = make_desc_sw128(b0 + ks * 2 * kSBO);
           const uint32_t accum = (seg_first && ks == 0) ? 0u : 1u;
-          asm volatile(
-              "{\n\t.reg .pred p;\n\t"
-              "setp.ne.b32 p, %4, 0;\n\t"
-              "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-              ::"r"(dacc), "l"(da), "l"(db), "r"(idesc), "r"(accum));
+#pragma unroll
+          for (int m = 0; m < MB; ++m) {
+            const uint64_t da = make_desc_sw128(a0 + m * kABytes + ks * 2 * kSBO);
+            const uint32_t dacc = tmem + (uint32_t)((buf * MB + m) * kBN);
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "setp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                ::"r"(dacc), "l"(da), "l"(db), "r"(idesc), "r"(accum));
+          }
         }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                      ::"r"(empty(s)) : "memory");
@@ -290,23 +338,24 @@ hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, i
       }
       // stopped early: the MMAs in flight must finish before TMEM is freed
       if (last_commit >= 0 && last_commit < nchunks - 1)
-        mbar_drain(empty(last_commit % kStages), (last_commit / kStages) & 1);
+        mbar_drain(empty(last_commit % G::kStagesM), (last_commit / G::kStagesM) & 1);
     }
   } else {
     // ---------------- epilogue: warps 2..5 ----------------
     const int quarter = warp & 3;  // this warp may read TMEM lanes 32*quarter .. +31
-    const int row_base = i0 + 32 * quarter;
     float* my_stg = stg + (warp - 2) * 32 * kStgPitch;
     for (int seg = 0; seg < nseg; ++seg) {
-      const int buf = seg & 1;
-      const bool ok = mbar_wait(accf(buf), (seg >> 1) & 1, abort_flag, true);
+      const int buf = seg % G::kNBuf;
+      const bool ok = mbar_wait(accf(buf), (seg / G::kNBuf) & 1, abort_flag, true);
       if (!__all_sync(0xFFFFFFFFu, ok)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll 1
-      for (int cb = 0; cb < kBN; cb += 32) {
+      for (int mc = 0; mc < MB * kBN; mc += 32) {
+        const int m = mc / kBN, cb = mc % kBN;
+        const int row_base = i0 + 128 * m + 32 * quarter;
         uint32_t v[32];
-        const uint32_t taddr =
-            tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(buf * kBN + cb);
+        const uint32_t taddr = tmem + ((uint32_t)(32 * quarter) << 16) +
+                               (uint32_t)((buf * MB + m) * kBN + cb);
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
             "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -365,8 +414,6 @@ hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, i
   }
 }
 
-constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + kStgBytes + 12 * 8 + 16;
-
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static std::once_flag once;
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -381,10 +428,35 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// Tile shape: 0 = by waves (choose_mb), 1 = 128 x 256,
+// 2 = 256 x 256. Set only by exl3_hessian_set_tile (tests and probes).
+std::atomic<int> g_tile_mode{0};
+
+template <int BF16, int MB>
+int launch_hessian(const CUtensorMap& map, int64_t T, int64_t d, float* H, int nbi, int nbj,
+                   int64_t ntiles, int* err_flag, int dev, exl3_stream_t stream) {
+  static DeviceBits attr_done;
+  constexpr size_t smem = HGeo<MB>::kSmem;
+  if (!attr_done.has(dev)) {
+    EXL3_CUDA(cudaFuncSetAttribute(hessian_tma_kernel<BF16, MB>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_done.set(dev);
+  }
+  hessian_tma_kernel<BF16, MB><<<(unsigned)ntiles, kThreads, smem, (cudaStream_t)stream>>>(
+      map, T, d, H, nbi, nbj, err_flag);
+  return EXL3_OK;
+}
+
 }  // namespace
 }  // namespace exl3
 
 using namespace exl3;
+
+extern "C" int exl3_hessian_set_tile(int mode) {
+  EXL3_REQUIRE(mode >= 0 && mode <= 2, "tile mode must be 0 (by d), 1 (128x256) or 2 (256x256)");
+  g_tile_mode.store(mode);
+  return EXL3_OK;
+}
 
 extern "C" int exl3_hessian_accumulate(float* H, const void* X, int dtype, int64_t T, int64_t d,
                                        int* err_flag, exl3_stream_t stream) {
@@ -396,10 +468,11 @@ extern "C" int exl3_hessian_accumulate(float* H, const void* X, int dtype, int64
   EXL3_REQUIRE(reinterpret_cast<uintptr_t>(X) % 16 == 0, "X must be 16-byte aligned");
   EXL3_REQUIRE(reinterpret_cast<uintptr_t>(H) % 16 == 0, "H must be 16-byte aligned");
   if (T == 0) return EXL3_OK;
-  const int nbi = (int)((d + kBM - 1) / kBM);
+  const int mode = g_tile_mode.load();
+  const int mb = mode == 1 ? 1 : mode == 2 ? 2 : choose_mb(d, sm_count());
+  const int nbi = (int)((d + kBM * mb - 1) / (kBM * mb));
   const int nbj = (int)((d + kBN - 1) / kBN);
-  int64_t ntiles = 0;
-  for (int bi = 0; bi < nbi; ++bi) ntiles += nbj - (bi >> 1);
+  const int64_t ntiles = mb == 2 ? tile_count<true>(d) : tile_count<false>(d);
 
   auto enc = encode_fn();
   EXL3_REQUIRE(enc != nullptr, "cuTensorMapEncodeTiled is unavailable from the driver");
@@ -415,26 +488,17 @@ extern "C" int exl3_hessian_accumulate(float* H, const void* X, int dtype, int64
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   EXL3_REQUIRE(cr == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)cr);
 
-  static DeviceBits attr_done[2];  // per dtype
   int dev = 0;
   EXL3_CUDA(cudaGetDevice(&dev));
-  if (dtype == 0) {
-    if (!attr_done[0].has(dev)) {
-      EXL3_CUDA(cudaFuncSetAttribute(hessian_tma_kernel<0>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-      attr_done[0].set(dev);
-    }
-    hessian_tma_kernel<0><<<(unsigned)ntiles, kThreads, kSmemBytes, (cudaStream_t)stream>>>(
-        map, T, d, H, nbi, nbj, err_flag);
-  } else {
-    if (!attr_done[1].has(dev)) {
-      EXL3_CUDA(cudaFuncSetAttribute(hessian_tma_kernel<1>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-      attr_done[1].set(dev);
-    }
-    hessian_tma_kernel<1><<<(unsigned)ntiles, kThreads, kSmemBytes, (cudaStream_t)stream>>>(
-        map, T, d, H, nbi, nbj, err_flag);
+  const int variant = 2 * dtype + (mb - 1);
+  int rc = EXL3_OK;
+  switch (variant) {
+    case 0: rc = launch_hessian<0, 1>(map, T, d, H, nbi, nbj, ntiles, err_flag, dev, stream); break;
+    case 1: rc = launch_hessian<0, 2>(map, T, d, H, nbi, nbj, ntiles, err_flag, dev, stream); break;
+    case 2: rc = launch_hessian<1, 1>(map, T, d, H, nbi, nbj, ntiles, err_flag, dev, stream); break;
+    default: rc = launch_hessian<1, 2>(map, T, d, H, nbi, nbj, ntiles, err_flag, dev, stream); break;
   }
+  if (rc != EXL3_OK) return rc;
   EXL3_LAUNCHED();
   return EXL3_OK;
 }

@@ -233,6 +233,15 @@ int exl3_hessian_accumulate(float* H, const void* X, int dtype, int64_t T, int64
                             int* err_flag, exl3_stream_t stream);
 
 /*
+ * Tile shape of exl3_hessian_accumulate in this process: 0 = chosen by d
+ * (256 x 256 tiles for wide H, 128 x 256 otherwise; the default), 1 = always
+ * 128 x 256, 2 = always 256 x 256. Results are bit-identical across shapes
+ * (each element is summed over the same 8192-token segments in the same
+ * order); the setting exists for tests and tuning. No reference counterpart.
+ */
+int exl3_hessian_set_tile(int mode);
+
+/*
  * Hessian finalize in place on an fp32 (d, d) sum of X^T X over `count`
  * tokens: H /= count; diag += max(1e-8, lambda * mean(diag)); diagonal
  * entries with |d| < zero_floor become zero_floor. damp_out (device, may be

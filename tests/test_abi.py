@@ -71,6 +71,9 @@ def test_argument_errors_return_status_and_message():
     g.restype = ctypes.c_int
     g.argtypes = [ctypes.c_int, P, P]
     assert g(3, dummy, None) == EINVAL
+    assert lib.exl3_hessian_set_tile(3) == EINVAL
+    assert b"tile mode" in lib.exl3_last_error()
+    assert lib.exl3_hessian_set_tile(0) == 0
 
 
 def test_torch_binding_loads_and_validates_on_cpu_tensors():

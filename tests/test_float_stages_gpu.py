@@ -129,6 +129,35 @@ def test_hessian_long_accumulation_stays_within_tolerance():
     assert torch.equal(H, H2)          # deterministic
 
 
+@pytest.mark.parametrize("d,T", [(136, 300), (520, 8200), (1032, 9000), (2048, 640)])
+def test_hessian_tile_shapes_agree_bit_for_bit(d, T):
+    """128 x 256 and 256 x 256 tiles (forced through exl3_hessian_set_tile)
+    on ragged widths and token counts past one 8192-token segment: each
+    within 1e-4 of the fp32 GEMM, and identical to each other (every element
+    is the same chain of M=128 tensor-core accumulations)."""
+    from exl3_intel_arc_quantizer_b200._ext import ext, set_hessian_tile
+
+    g = torch.Generator(device=DEV).manual_seed(d * 7 + T)
+    x = torch.randn(T, d, generator=g, device=DEV, dtype=torch.bfloat16)
+    x[:, d - 1] *= 12.0
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = {}
+    try:
+        for mode in (1, 2, 0):
+            set_hessian_tile(mode)
+            H = torch.zeros(d, d, device=DEV)
+            ext().hessian_accumulate_(H, x, err)
+            out[mode] = H
+    finally:
+        set_hessian_tile(0)
+    assert int(err.item()) == 0
+    xf = x.float()
+    assert _max_rel(out[1], xf.T @ xf) <= 1e-4
+    assert torch.equal(out[1], out[2])
+    assert torch.equal(out[0], out[1])
+    assert torch.equal(out[2], out[2].T)
+
+
 def test_collector_groups_share_hessians():
     from exl3_intel_arc_quantizer_b200.calibration import TransformerDecoderLayer, make_rotary_embeddings
 
