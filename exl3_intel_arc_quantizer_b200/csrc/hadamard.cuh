@@ -37,8 +37,8 @@ __device__ __forceinline__ void fwht128_warp(float (&v)[4], int lane) {
 // the butterflies of strides 1 and 2 are shuffles with the partner lanes, the
 // five wider ones run in registers (the order and roundings of
 // fwht128_warp). A warp's loads and stores cover 8 columns of four rows: four
-// full 32-byte sectors, no shared memory. DIV: divide by su[row] first (the
-// regularization's left step); else the plain rotation. Every lane of the
+// full 32-byte sectors. DIV: divide by su[row] first (the regularization's
+// left step; su best in shared memory); else the plain rotation. Every lane of the
 // warp must call it (the shuffles are warp-wide); a lane whose column is past
 // the matrix passes valid = false and neither loads nor stores.
 template <bool DIV>
@@ -48,11 +48,16 @@ __device__ __forceinline__ void had_left_quad_cols(float* __restrict__ col, int6
   float v[32];
   const int64_t step = 4 * n;
   const float* src = col + (int64_t)q * n;
+  // every load is issued before the first division (a division's slow path
+  // would otherwise hold back the loads behind it)
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
-    const float x = valid ? *src : 0.f;
+    v[i] = valid ? *src : 0.f;
     src += step;
-    v[i] = DIV ? __fdiv_rn(x, su[4 * i + q]) : x;
+  }
+  if (DIV) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __fdiv_rn(v[i], su[4 * i + q]);
   }
   const float s1 = (q & 1) ? -1.0f : 1.0f, s2 = (q & 2) ? -1.0f : 1.0f;
 #pragma unroll

@@ -17,14 +17,16 @@
 //     hands the finished accumulator to the epilogue and switches to the
 //     other one;
 //   * warps 2-5 drain a finished accumulator (tcgen05.ld), stage each 32x32
-//     block in shared memory and add it into H with 16-byte
-//     red.global.add.v4.f32: the element (r, c) for c >= r and its mirror
-//     (c, r) for c > r, while the MMAs of the next segment run.
+//     block in shared memory and add its elements (r, c), c >= r, into H
+//     with 16-byte red.global.add.v4.f32 (L2 evict-last, so H's lines stay
+//     cached between segments), while the MMAs of the next segment run;
+//   * hessian_mirror_kernel then copies the upper triangle to the lower one.
 // Draining every segment bounds the length of each tensor-core accumulation
-// chain (its additions are not round-to-nearest, so long chains drift) and
-// leaves H symmetric after every call. Each element of H is updated by one
-// thread in a fixed order (other tiles only add +0.0 to it), so results are
-// deterministic.
+// chain (its additions are not round-to-nearest, so long chains drift). H is
+// symmetric after every call; on entry only its upper triangle is read (the
+// lower one is rewritten from it), so H must be symmetric on entry, as any
+// sum of earlier calls is. Each element of the upper triangle is updated by
+// one thread in a fixed order, so results are deterministic.
 // Every wait is bounded by the global timer; a role that gives up records
 // the error flag and the others stop at their next wait; the CTA then waits
 // (bounded) for its own TMA copies and MMAs before it frees TMEM and exits.
@@ -154,9 +156,18 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-__device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float e) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
-               "f"(e)
+// L2 policy for H: its lines stay in L2 ahead of the streamed X slabs, so the
+// tile's next segment adds into cached lines instead of re-reading HBM
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float e,
+                                         uint64_t pol) {
+  asm volatile("red.global.add.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p),
+               "f"(a), "f"(b), "f"(c), "f"(e), "l"(pol)
                : "memory");
 }
 
@@ -343,6 +354,7 @@ hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, i
   } else {
     // ---------------- epilogue: warps 2..5 ----------------
     const int quarter = warp & 3;  // this warp may read TMEM lanes 32*quarter .. +31
+    const uint64_t hpol = l2_evict_last_policy();
     float* my_stg = stg + (warp - 2) * 32 * kStgPitch;
     for (int seg = 0; seg < nseg; ++seg) {
       const int buf = seg % G::kNBuf;
@@ -373,7 +385,8 @@ hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, i
         __syncwarp();
         const int col0 = j0 + cb;
         const int sub = lane >> 3, quad = (lane & 7) * 4;
-        // direct (r, c), c >= r: 8 lanes per row, 4 columns per lane
+        // (r, c), c >= r: 8 lanes per row, 4 columns per lane (the lower
+        // triangle is written once per call by hessian_mirror_kernel)
 #pragma unroll 2
         for (int it = 0; it < 8; ++it) {
           const int rr = it * 4 + sub;
@@ -381,18 +394,7 @@ hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, i
           if (r < d && c < d && c + 3 >= r) {
             const float* s = my_stg + rr * kStgPitch + quad;
             red_add4(H + (int64_t)r * d + c, (c >= r) ? s[0] : 0.f, (c + 1 >= r) ? s[1] : 0.f,
-                     (c + 2 >= r) ? s[2] : 0.f, s[3]);
-          }
-        }
-        // mirror (c, r), c > r: 8 lanes per column, 4 rows per lane
-#pragma unroll 2
-        for (int it = 0; it < 8; ++it) {
-          const int q = it * 4 + sub;
-          const int c = col0 + q, r = row_base + quad;
-          if (r < d && c < d && c > r) {
-            const float* s = my_stg + quad * kStgPitch + q;
-            red_add4(H + (int64_t)c * d + r, s[0], (c > r + 1) ? s[kStgPitch] : 0.f,
-                     (c > r + 2) ? s[2 * kStgPitch] : 0.f, (c > r + 3) ? s[3 * kStgPitch] : 0.f);
+                     (c + 2 >= r) ? s[2] : 0.f, s[3], hpol);
           }
         }
         __syncwarp();
@@ -426,6 +428,26 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   });
   return fn;
+}
+
+// H[c][r] = H[r][c] for c > r: the lower triangle from the upper one, one
+// CTA of 32 x 8 threads per 32 x 32 block of the upper triangle (blocks
+// below the diagonal exit at once), transposed through shared memory
+__global__ void __launch_bounds__(256) hessian_mirror_kernel(float* __restrict__ H, int64_t d) {
+  const int64_t bi = blockIdx.y, bj = blockIdx.x;
+  if (bj < bi) return;
+  __shared__ float t[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t r0 = bi * 32, c0 = bj * 32;
+  for (int k = ty; k < 32; k += 8) {
+    const int64_t r = r0 + k, c = c0 + tx;
+    if (r < d && c < d) t[k][tx] = H[r * d + c];
+  }
+  __syncthreads();
+  for (int k = ty; k < 32; k += 8) {
+    const int64_t r = c0 + k, c = r0 + tx;  // lower (r, c) takes upper (c, r)
+    if (r < d && c < d && r > c) H[r * d + c] = t[tx][k];
+  }
 }
 
 // Tile shape: 0 = by waves (choose_mb), 1 = 128 x 256,
@@ -499,6 +521,9 @@ extern "C" int exl3_hessian_accumulate(float* H, const void* X, int dtype, int64
     default: rc = launch_hessian<1, 2>(map, T, d, H, nbi, nbj, ntiles, err_flag, dev, stream); break;
   }
   if (rc != EXL3_OK) return rc;
+  EXL3_LAUNCHED();
+  const unsigned nb32 = (unsigned)((d + 31) / 32);
+  hessian_mirror_kernel<<<dim3(nb32, nb32), 256, 0, (cudaStream_t)stream>>>(H, d);
   EXL3_LAUNCHED();
   return EXL3_OK;
 }

@@ -6,25 +6,27 @@
 //   reg_skew_kernel      skew = (sum of the k/50 largest sqrt(H_ii)) / (sum of
 //                        all), by a radix select over the float bits (one CTA)
 //   reg_colsq_kernel     sum of W^2 over each 32-row slice of each column
-//   reg_colrms_kernel    column RMS (slices added in order)
+//   reg_colrms_kernel    column RMS (slice sums added in a fixed order)
 //   reg_colfinal_kernel  their mean, the output-scale decision, sv and the
 //                        column divisors (one CTA)
 //   reg_right_kernel     W / sv, then the 128-column Hadamard of each row (the
 //                        shared FWHT), plus each row's sum of squares over
 //                        each 32-column slice
-//   reg_rowfinal_kernel  row RMS (slices added in order) and su
+//   reg_rowfinal_kernel  row RMS (slice sums added in a fixed order) and su
 //   reg_left_kernel      work / su, then the 128-row Hadamard (four threads
 //                        per column, no shared memory)
 // The reference's sums (torch reductions) have their own order; here every
-// slice sum is one fixed order and the slices are added in the reference's
-// slice order, so results agree to fp32 rounding.
+// sum has one fixed order (32-element slices, then eight interleaved chains
+// of slices added in order), so results are deterministic and agree with the
+// reference to fp32 rounding.
 //
 // Block-LDL fold (reference exl3_quant/ldlq.py:96-117): with C the Cholesky
 // factor of H and D_b its 16x16 diagonal blocks, L[:, b] = C[:, b] D_b^-1
 // and the diagonal blocks become identities. ldl_inv_kernel inverts every
 // (lower-triangular) D_b once by forward substitution; ldl_fold_kernel, one
 // CTA per 64 x 64 tile of L, multiplies its rows by the four inverses of its
-// block columns; tiles above the diagonal are zeros.
+// block columns (inverse columns held in registers); tiles above the
+// diagonal are zeros.
 #include "common.cuh"
 #include "hadamard.cuh"
 
@@ -83,15 +85,35 @@ __global__ void __launch_bounds__(1024) reg_skew_kernel(const float* __restrict_
       if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
     }
     __syncthreads();
-    if (t == 0) {
-      int64_t rem = remaining;
-      int digit = 255;
-      for (; digit > 0; --digit) {
-        if ((int64_t)hist[digit] >= rem) break;
-        rem -= hist[digit];
+    if (t < 32) {
+      // the digit holding the remaining-th largest key: lane l owns digits
+      // 255 - 8l .. 248 - 8l; an exclusive scan over lanes gives the count
+      // above each lane's digits, the first lane that reaches `remaining`
+      // walks its eight (digit 0 takes whatever is left)
+      uint32_t cnt[8], own = 0u;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        cnt[u] = hist[255 - 8 * t - u];
+        own += cnt[u];
       }
-      sel[0] = (uint32_t)digit;
-      sel[1] = (uint32_t)rem;
+      uint32_t incl = own;
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (t >= o) incl += y;
+      }
+      const uint32_t above = incl - own;
+      const unsigned hit = __ballot_sync(0xFFFFFFFFu, (int64_t)incl >= remaining);
+      const int owner = hit ? __ffs(hit) - 1 : 31;
+      if (t == owner) {
+        int64_t rem = remaining - (int64_t)above;
+        int digit = 255 - 8 * t;
+        for (int u = 0; u < 7 && (int64_t)cnt[u] < rem; ++u) {
+          rem -= cnt[u];
+          --digit;
+        }
+        sel[0] = (uint32_t)digit;
+        sel[1] = (uint32_t)rem;
+      }
     }
     __syncthreads();
     prefix |= sel[0] << shift;
@@ -129,14 +151,43 @@ __global__ void reg_colsq_kernel(const float* __restrict__ W, int64_t k, int64_t
   partial[b * n + c] = s;
 }
 
-// Column RMS: the 32-row slice sums of a column added in slice order
-__global__ void reg_colrms_kernel(const float* __restrict__ partial, int64_t nb, int64_t k,
-                                  int64_t n, float* __restrict__ out_scales) {
-  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= n) return;
-  float acc = partial[c];
-  for (int64_t b = 1; b < nb; ++b) acc = __fadd_rn(acc, partial[b * n + c]);
-  out_scales[c] = sqrtf(__fdiv_rn(acc, (float)k));
+// Sum over s < ns of part[s * stride + x] for the 32 consecutive x of a CTA
+// of 32 x 8 threads: thread (x, g) adds the slices s = g, g + 8, ... in order
+// (eight loads in flight per step), then the eight chains are added in order
+// g = 0..7. Returns the sum in threads with g == 0.
+__device__ __forceinline__ float slice_sum_32x8(const float* __restrict__ part, int64_t ns,
+                                                int64_t stride, int64_t x, bool valid) {
+  __shared__ float chains[8][33];
+  const int tx = threadIdx.x & 31, g = threadIdx.x >> 5;
+  float acc = 0.f;
+  if (valid) {
+    int64_t sl = g;
+    for (; sl + 56 < ns; sl += 64) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = part[(sl + 8 * u) * stride + x];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
+    }
+    for (; sl < ns; sl += 8) acc = __fadd_rn(acc, part[sl * stride + x]);
+  }
+  chains[g][tx] = acc;
+  __syncthreads();
+  float total = 0.f;
+  if (g == 0) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) total = __fadd_rn(total, chains[u][tx]);
+  }
+  return total;
+}
+
+// Column RMS from the 32-row slice sums (CTA of 32 columns x 8 chains)
+__global__ void __launch_bounds__(256) reg_colrms_kernel(const float* __restrict__ partial,
+                                                         int64_t nb, int64_t k, int64_t n,
+                                                         float* __restrict__ out_scales) {
+  const int64_t c = (int64_t)blockIdx.x * 32 + (threadIdx.x & 31);
+  const float acc = slice_sum_32x8(partial, nb, n, c, c < n);
+  if (threadIdx.x < 32 && c < n) out_scales[c] = sqrtf(__fdiv_rn(acc, (float)k));
 }
 
 // The column RMS mean, the output-scale decision (regularize.py:145-182),
@@ -197,9 +248,14 @@ __global__ void reg_right_kernel(const float* __restrict__ W, const float* __res
   const int64_t row = warp / nb, blk = warp % nb;
   const float* src = W + row * n + blk * 128;
   const float* dv = divisor + blk * 128;
-  float v[4];
+  float v[4], d[4];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) v[q] = __fdiv_rn(src[lane + 32 * q], dv[lane + 32 * q]);
+  for (int q = 0; q < 4; ++q) {
+    v[q] = src[lane + 32 * q];
+    d[q] = dv[lane + 32 * q];
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) v[q] = __fdiv_rn(v[q], d[q]);
   fwht128_warp(v, lane);
   float* dst = work + row * n + blk * 128;
 #pragma unroll
@@ -212,15 +268,14 @@ __global__ void reg_right_kernel(const float* __restrict__ W, const float* __res
   }
 }
 
-// Row RMS (the 32-column slices added in order) and su
+// Row RMS from the 32-column slice sums (CTA of 32 rows x 8 chains) and su
 // (regularize.py:187-190): su = su_in * rms / -1.24371088 + 1e-10
-__global__ void reg_rowfinal_kernel(const float* __restrict__ rpart, int64_t ns, int64_t k,
-                                    int64_t n, const float* __restrict__ su_in,
-                                    float* __restrict__ in_scales, float* __restrict__ su_out) {
-  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= k) return;
-  float acc = rpart[row];
-  for (int64_t s = 1; s < ns; ++s) acc = __fadd_rn(acc, rpart[s * k + row]);
+__global__ void __launch_bounds__(256) reg_rowfinal_kernel(
+    const float* __restrict__ rpart, int64_t ns, int64_t k, int64_t n,
+    const float* __restrict__ su_in, float* __restrict__ in_scales, float* __restrict__ su_out) {
+  const int64_t row = (int64_t)blockIdx.x * 32 + (threadIdx.x & 31);
+  const float acc = slice_sum_32x8(rpart, ns, k, row, row < k);
+  if (threadIdx.x >= 32 || row >= k) return;
   float rms = sqrtf(__fdiv_rn(acc, (float)n));
   if (fabsf(rms) < 1e-30f) rms = kRegZeroFloor;
   in_scales[row] = rms;
@@ -232,11 +287,14 @@ __global__ void reg_rowfinal_kernel(const float* __restrict__ rpart, int64_t ns,
 __global__ void __launch_bounds__(256, 2) reg_left_kernel(float* __restrict__ work,
                                                           const float* __restrict__ su,
                                                           int64_t k, int64_t n) {
+  __shared__ float su_s[128];
   const int t = threadIdx.x;
+  if (t < 128) su_s[t] = su[(int64_t)blockIdx.y * 128 + t];
+  __syncthreads();
   const int64_t c = (int64_t)blockIdx.x * 64 + (t >> 2);
   const bool valid = c < n;
-  had_left_quad_cols<true>(work + (int64_t)blockIdx.y * 128 * n + (valid ? c : 0), n,
-                           su + (int64_t)blockIdx.y * 128, t & 3, valid);
+  had_left_quad_cols<true>(work + (int64_t)blockIdx.y * 128 * n + (valid ? c : 0), n, su_s,
+                           t & 3, valid);
 }
 
 // D_b^-1 of every 16x16 diagonal block of C (lower triangular) by forward
@@ -270,13 +328,17 @@ __global__ void __launch_bounds__(64) ldl_inv_kernel(const float* __restrict__ c
 }
 
 // L = C D^-1 per 16-column block, identity diagonal blocks, zeros above:
-// one CTA per 64 x 64 tile (4 block columns); n % 16 == 0.
+// one CTA per 64 x 64 tile (4 block columns); n % 16 == 0. Thread (g, j, q)
+// holds column j of D_g^-1 in registers and computes column 16 g + j of the
+// 16 rows of row block q: per row one chain of 16 fmaf (i = 0..15) over the
+// row's C entries, read from shared memory four at a time and shared by the
+// 16 threads of the block column. A warp stores 32 consecutive columns of one
+// row per instruction.
 __global__ void __launch_bounds__(256) ldl_fold_kernel(const float* __restrict__ chol,
                                                        float* __restrict__ L,
                                                        const float* __restrict__ inverses,
                                                        int64_t n) {
-  __shared__ float X[4][16][17];  // D_g^-1 of the tile's block columns g = 0..3
-  __shared__ float T[64][65];     // the tile of C
+  __shared__ __align__(16) float T[64][68];  // the tile of C
   const int64_t r0 = (int64_t)blockIdx.y * 64, c0 = (int64_t)blockIdx.x * 64;
   const int t = threadIdx.x;
   const int rows = (int)((n - r0) < 64 ? (n - r0) : 64);
@@ -293,38 +355,42 @@ __global__ void __launch_bounds__(256) ldl_fold_kernel(const float* __restrict__
     const int r = i >> 4, c = (i & 15) * 4;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (r < rows && c < cols) v = *reinterpret_cast<const float4*>(chol + (r0 + r) * n + c0 + c);
-    T[r][c] = v.x;
-    T[r][c + 1] = v.y;
-    T[r][c + 2] = v.z;
-    T[r][c + 3] = v.w;
-  }
-  for (int i = t; i < 4 * 256; i += 256) {
-    const int g = i >> 8, e = i & 255;
-    if (16 * g < cols) X[g][e >> 4][e & 15] = inverses[((c0 >> 4) + g) * 256 + e];
+    *reinterpret_cast<float4*>(&T[r][c]) = v;
   }
   __syncthreads();
-  const int r = t >> 2, g = t & 3;  // row r, block column g: 16 outputs
-  if (r >= rows || 16 * g >= cols) return;
-  float o[16];
-  const int64_t grow = r0 + r, gblk = (c0 >> 4) + g;
-  if ((grow >> 4) < gblk) {
+  const int lane = t & 31, w = t >> 5;
+  const int j = lane & 15, g = 2 * (w & 1) + (lane >> 4), q = w >> 1;
+  if (16 * g >= cols || 16 * q >= rows) return;
+  const int64_t gblk = (c0 >> 4) + g, rblk = (r0 >> 4) + q;
+  float* dst = L + (r0 + 16 * q) * n + c0 + 16 * g + j;
+  if (rblk < gblk) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) o[j] = 0.f;
-  } else if ((grow >> 4) == gblk) {
-#pragma unroll
-    for (int j = 0; j < 16; ++j) o[j] = (j == (int)(grow & 15)) ? 1.f : 0.f;
-  } else {
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      float acc = 0.f;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) acc = fmaf(T[r][16 * g + i], X[g][i][j], acc);
-      o[j] = acc;
-    }
+    for (int rr = 0; rr < 16; ++rr) dst[rr * n] = 0.f;
+    return;
   }
-  float4* dst = reinterpret_cast<float4*>(L + grow * n + c0 + 16 * g);
+  if (rblk == gblk) {
 #pragma unroll
-  for (int q = 0; q < 4; ++q) dst[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+    for (int rr = 0; rr < 16; ++rr) dst[rr * n] = (rr == j) ? 1.f : 0.f;
+    return;
+  }
+  float x[16];
+  const float* xs = inverses + gblk * 256 + j;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = xs[16 * i];
+#pragma unroll 4
+  for (int rr = 0; rr < 16; ++rr) {
+    const float4* tr = reinterpret_cast<const float4*>(&T[16 * q + rr][16 * g]);
+    float acc = 0.f;
+#pragma unroll
+    for (int i4 = 0; i4 < 4; ++i4) {
+      const float4 a = tr[i4];
+      acc = fmaf(a.x, x[4 * i4], acc);
+      acc = fmaf(a.y, x[4 * i4 + 1], acc);
+      acc = fmaf(a.z, x[4 * i4 + 2], acc);
+      acc = fmaf(a.w, x[4 * i4 + 3], acc);
+    }
+    dst[rr * n] = acc;
+  }
 }
 
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }
@@ -387,7 +453,7 @@ extern "C" int exl3_regularize(const float* W, const float* su_in, const float* 
   const int64_t nb = (k + 31) / 32;
   reg_colsq_kernel<<<dim3((unsigned)((n + 255) / 256), (unsigned)nb), 256, 0, s>>>(W, k, n, cp);
   EXL3_LAUNCHED();
-  reg_colrms_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(cp, nb, k, n, out_scales);
+  reg_colrms_kernel<<<(unsigned)((n + 31) / 32), 256, 0, s>>>(cp, nb, k, n, out_scales);
   EXL3_LAUNCHED();
   reg_colfinal_kernel<<<1, 1024, 0, s>>>(n, sv_in, force_out_scales, q_fallback, has_skew, inf,
                                         out_scales, dv, sv_out);
@@ -395,8 +461,8 @@ extern "C" int exl3_regularize(const float* W, const float* su_in, const float* 
   const int64_t warps = k * (n / 128);
   reg_right_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(W, dv, work, rp, k, n);
   EXL3_LAUNCHED();
-  reg_rowfinal_kernel<<<(unsigned)((k + 255) / 256), 256, 0, s>>>(rp, n / 32, k, n, su_in,
-                                                                   in_scales, su_out);
+  reg_rowfinal_kernel<<<(unsigned)((k + 31) / 32), 256, 0, s>>>(rp, n / 32, k, n, su_in,
+                                                                 in_scales, su_out);
   EXL3_LAUNCHED();
   reg_left_kernel<<<dim3((unsigned)((n + 63) / 64), (unsigned)(k / 128)), 256, 0, s>>>(
       work, su_out, k, n);

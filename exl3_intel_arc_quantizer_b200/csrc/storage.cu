@@ -12,10 +12,10 @@
 //
 // decode_weight_kernel: one CTA per 128x128 block of the (k, n) weight (8x8
 // tiles). The block's container words are read once, each element is
-// decoded into a padded fp32 shared tile at its tensor-core position, then
-// the left rotation (columns, with the row scales su) and the right
-// rotation (rows, with the column scales sv) run in shared memory and the
-// block is written once: HBM traffic = K/8 B read + 4 B written per weight.
+// decoded straight into the registers of the thread that rotates its column
+// (left rotation, then x su), the right rotation runs on rows through a
+// swizzled fp32 shared tile, and the block (x sv) is written once: HBM
+// traffic = K/8 B read + 4 B written per weight.
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -27,7 +27,7 @@ namespace {
 
 constexpr int kDB = 128;          // block edge
 constexpr int kDThreads = 256;   // unpack
-constexpr int kDecThreads = 256; // decode: four spans per thread
+constexpr int kDecThreads = 256; // decode: two threads per column
 constexpr int kUTiles = 16;       // tiles per unpack CTA (two per warp)
 
 // unpack: one thread per span. A warp stages its two tiles' container words
@@ -64,37 +64,117 @@ __device__ __forceinline__ float load_scale(const void* p, int64_t i) {
 }
 
 // decode_weight_kernel: one CTA per 128x128 block of the (k, n) weight (8x8
-// tiles). The block's container words are read once; each thread decodes
-// four spans (16 states each, fixed tile positions) into an fp32 shared
-// tile; the left rotation runs on columns, the right one on rows, and the
-// block is written once: HBM traffic = K/8 B read + 4 B written per weight.
+// tiles); HBM traffic = K/8 B read + 4 B written per weight.
 //
-// Both rotations give each thread 64 elements of one column (or row) - the
-// elements of one parity, its partner lane holding the other - so the
-// stride-1 butterfly is one shuffle and the six wider ones run in registers
-// (one shuffle per element per rotation instead of five). The shared tile is
-// stored with the rows XOR-swizzled (column c of row r at c ^ dswz(r)) so
-// that both thread mappings and the row-wise float4 copy-out are free of bank
-// conflicts. Per element the steps and their roundings are those of
+// 1. The block's container words become a table of 32-bit windows in shared
+//    memory: window m of a tile holds stream words m and m + 1 (circular), so
+//    the 16-bit state of element e is one bit-field extract of window
+//    floor((K(e+1) - 16) / 16) at bit 16 - (K(e+1) mod 16). The table index
+//    is padded per K (WinPad) so that a warp's reads spread over the banks.
+// 2. Two threads per column (c, b) decode the 64 elements of column c in rows
+//    4i + 2b and 4i + 2b + 1 straight into registers as pairs of adjacent
+//    rows (tensor-core positions of trellis_format.py:88-108: consecutive
+//    span elements u, u + 1; each tile gives a thread two spans x two pairs)
+//    and apply the left rotation: row stride 1 inside each pair, stride 2
+//    with the partner lane (one shuffle), strides 4..64 between pairs.
+// 3. x su, the right rotation on rows (two threads per row, column pairs
+//    4i + 2b, 4i + 2b + 1 read and written as 8-byte words, same scheme),
+//    x sv and a row-wise float4 copy-out, through an fp32 shared tile whose
+//    rows are XOR-swizzled (column c of row r at c ^ dswz(r)) so that the
+//    column stores, the pair accesses and the copy-out are free of bank
+//    conflicts.
+// Butterflies and scalings run as packed f32x2 operations where two
+// independent elements take the same step (each lane rounds like the scalar
+// operation). Per element the steps and their roundings are those of
 // hadamard.weight_from_quantized: butterflies in the order of strides
 // 1, 2, ..., 64 (lower + upper, lower - upper), x 1/sqrt(128), x su, the row
 // butterflies, x 1/sqrt(128), x sv.
-__device__ __forceinline__ int dswz(int r) { return 2 * (((r & 1) << 3) | ((r >> 1) & 7)); }
+__device__ __forceinline__ int dswz(int r) {
+  return 16 * ((r >> 1) & 1) + 8 * (r & 1) + 4 * ((r >> 2) & 1);
+}
 __device__ __forceinline__ int dpos(int r, int c) { return r * kDB + (c ^ dswz(r)); }
 
-// in-register butterflies of strides 1..32 over v[0..63] (element stride 2h in
-// the block: the caller's stride-1 partner is another lane)
-__device__ __forceinline__ void fwht64_regs(float (&v)[64]) {
+// window table padding: index m is stored at m + A * (m >> S); (A, S) per K
+// chosen so that a warp's reads (16 columns of one tile, both row classes)
+// hit distinct banks for K = 1, 2, 4 and at most two-way conflicts otherwise
+template <int K> struct WinPad { static constexpr int A = 0, S = 5; };
+template <> struct WinPad<3> { static constexpr int A = 5, S = 5; };
+template <> struct WinPad<4> { static constexpr int A = 4, S = 3; };
+template <> struct WinPad<5> { static constexpr int A = 3, S = 2; };
+template <> struct WinPad<7> { static constexpr int A = 1, S = 5; };
+template <> struct WinPad<8> { static constexpr int A = 1, S = 2; };
+template <int K>
+__device__ __forceinline__ int wpad(int m) { return m + WinPad<K>::A * (m >> WinPad<K>::S); }
+template <int K>
+__host__ __device__ constexpr int win_stride() {
+  return 16 * K + WinPad<K>::A * ((16 * K - 1) >> WinPad<K>::S);
+}
+
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) { return __fadd2_rn(a, b); }
+// a - b with one rounding: (-1) * b is exact
+__device__ __forceinline__ float2 f2_sub(float2 a, float2 b) {
+  return __ffma2_rn(b, make_float2(-1.0f, -1.0f), a);
+}
+
+// 128-point butterflies over a line held by two lanes as pairs of adjacent
+// elements w[p] = (v[4p + 2b], v[4p + 2b + 1]) (b = lane bit 0): stride 1
+// inside each pair, stride 2 with the partner lane (lower = mine + other,
+// upper = other - mine), strides 4..64 between pairs, x 1/sqrt(128)
+__device__ __forceinline__ void fwht128_pair_line(float2 (&w)[32], float sign) {
 #pragma unroll
-  for (int h = 1; h < 64; h <<= 1) {
+  for (int p = 0; p < 32; ++p) {
+    const float lo = w[p].x, hi = w[p].y;
+    w[p] = make_float2(lo + hi, lo - hi);
+  }
+  const float2 sg = make_float2(sign, sign);
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      if (i & h) continue;
-      const float lo = v[i], hi = v[i + h];
-      v[i] = lo + hi;
-      v[i + h] = lo - hi;
+  for (int p = 0; p < 32; ++p) {
+    const float2 o = make_float2(__shfl_xor_sync(0xFFFFFFFFu, w[p].x, 1),
+                                 __shfl_xor_sync(0xFFFFFFFFu, w[p].y, 1));
+    w[p] = __ffma2_rn(sg, w[p], o);
+  }
+#pragma unroll
+  for (int h = 1; h < 32; h <<= 1) {
+#pragma unroll
+    for (int p = 0; p < 32; ++p) {
+      if (p & h) continue;
+      const float2 lo = w[p], hi = w[p + h];
+      w[p] = f2_add(lo, hi);
+      w[p + h] = f2_sub(lo, hi);
     }
   }
+  const float2 sc = make_float2(kHad128Scale, kHad128Scale);
+#pragma unroll
+  for (int p = 0; p < 32; ++p) w[p] = __fmul2_rn(w[p], sc);
+}
+
+// two codebook values (the states' fp16 values widened to fp32)
+template <int CB>
+__device__ __forceinline__ float2 cb_decode2(uint32_t s0, uint32_t s1) {
+  if constexpr (CB == 2) {
+    // 0x6400 + byte sum of s * 0x83DCD12D (< 2^16), then h * inv + bias in
+    // fp16 for both lanes at once
+    const uint32_t h0 = __dp4a(s0 * 0x83DCD12Du, 0x01010101u, 0x6400u);
+    const uint32_t h1 = __dp4a(s1 * 0x83DCD12Du, 0x01010101u, 0x6400u);
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(h0 | (h1 << 16)), "r"(0x1EEE1EEEu),
+        "r"(0xC931C931u));
+    return __half22float2(*reinterpret_cast<const __half2*>(&r));
+  } else {
+    return make_float2(half_bits_to_float(cb_state_bits(CB, s0)),
+                       half_bits_to_float(cb_state_bits(CB, s1)));
+  }
+}
+
+__device__ __forceinline__ uint32_t bits16_at(uint32_t w, uint32_t pos) {
+  uint32_t r;
+  asm("bfe.u32 %0, %1, %2, 16;" : "=r"(r) : "r"(w), "r"(pos));
+  return r;
+}
+
+template <int K>
+constexpr size_t decode_smem_bytes() {
+  return (size_t)kDB * kDB * 4 + (size_t)64 * win_stride<K>() * 4;
 }
 
 template <int K, int CB, int SCALE_F32>
@@ -103,97 +183,118 @@ decode_weight_kernel(const uint16_t* __restrict__ trellis, const void* __restric
                      const void* __restrict__ sv, float* __restrict__ out,
                      float* __restrict__ out_w_hat, int64_t tiles_n, int64_t n) {
   extern __shared__ __align__(16) uint8_t dsmem[];
-  float* blk = reinterpret_cast<float*>(dsmem);                     // 128 x 128 fp32, swizzled
-  uint16_t* words = reinterpret_cast<uint16_t*>(blk + kDB * kDB);   // 64 tiles x 16K
+  float* blk = reinterpret_cast<float*>(dsmem);                    // 128 x 128 fp32, swizzled
+  uint32_t* win = reinterpret_cast<uint32_t*>(blk + kDB * kDB);    // 64 tiles x win_stride
+  constexpr int kW32 = 8 * K;          // 32-bit container words per tile
+  constexpr int kWS = win_stride<K>();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t rb = blockIdx.y, cbk = blockIdx.x;
-  constexpr int wpt = 16 * K;  // storage words per tile
 
-  // 1. container words: each tile row of the block is one contiguous run of
-  //    8 tiles (8 * 32K bytes), copied as 32-bit words
+  // 1. windows: each tile row of the block is one contiguous run of 8 tiles;
+  //    stored 32-bit word q is stream words 2q + 1, 2q (SWAP16), so window 2q
+  //    is the word itself and window 2q + 1 joins its low half with the next
+  //    word's high half
 #pragma unroll
   for (int tr = 0; tr < 8; ++tr) {
     const uint32_t* src = reinterpret_cast<const uint32_t*>(
-        trellis + ((rb * 8 + tr) * tiles_n + cbk * 8) * (int64_t)wpt);
-    uint32_t* dst = reinterpret_cast<uint32_t*>(words + tr * 8 * wpt);
-    for (int i = tid; i < 4 * wpt; i += kDecThreads) dst[i] = src[i];
-  }
-  __syncthreads();
-
-  // 2. decode: four spans per thread; span s of tile tt holds elements
-  //    16s..16s+15, whose tensor-core positions (trellis_format.py:88-108)
-  //    are (4(s&1) + dr(u), (s>>1) + dc(u)) with compile-time dr, dc
-#pragma unroll
-  for (int q = 0; q < 1024 / kDecThreads; ++q) {
-    const int spid = q * kDecThreads + tid;
-    const int tt = spid >> 4, s = spid & 15;
-    const uint16_t* tw = words + tt * wpt;
-    uint32_t st[16];
-    span_states<K>([&](int j) { return (uint32_t)tw[j ^ 1]; }, s, st);
-    const int r0 = (tt >> 3) * 16 + 4 * (s & 1), c0 = (tt & 7) * 16 + (s >> 1);
-#pragma unroll
-    for (int u = 0; u < 16; ++u) {
-      const int dr = 2 * (u >> 3) + (u & 1) + 8 * ((u >> 1) & 1);
-      const int dc = 8 * ((u >> 2) & 1);
-      blk[dpos(r0 + dr, c0 + dc)] = __half2float(__ushort_as_half(cb_state_bits(CB, st[u])));
+        trellis + ((rb * 8 + tr) * tiles_n + cbk * 8) * (int64_t)(16 * K));
+    for (int i = tid; i < 8 * kW32; i += kDecThreads) {
+      const int t = i / kW32, q = i - t * kW32;
+      const uint32_t a = src[i];
+      const uint32_t nx = src[t * kW32 + (q + 1 < kW32 ? q + 1 : 0)];
+      uint32_t* tw = win + (tr * 8 + t) * kWS;
+      tw[wpad<K>(2 * q)] = a;
+      tw[wpad<K>(2 * q + 1)] = (a << 16) | (nx >> 16);
     }
   }
   __syncthreads();
+
+  // 2. two threads per column: c = tid / 2, rows 4i + 2b + j. In tile row tr
+  //    the column's local index lc takes spans s = 2 (lc & 7) + sp and span
+  //    elements u = 4 (lc >> 3) + 2x + 8b + j; element e = 16 s + u sits at
+  //    local row 4 sp + 8x + 2b + j, i.e. pair index 4 tr + sp + 2x
+  const int b = tid & 1, c = tid >> 1, lc = c & 15, tcb = c >> 4;
+  int woff[8];
+  uint32_t wbit[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {  // k = 4x + 2sp + j
+    const int x = k >> 2, sp = (k >> 1) & 1, j = k & 1;
+    const int e = 32 * (lc & 7) + 16 * sp + 4 * (lc >> 3) + 2 * x + 8 * b + j;
+    const int be = K * (e + 1);  // the state is stream bits [be - 16, be)
+    int m = (be + 256 * K - 16) >> 4;
+    if (m >= 16 * K) m -= 16 * K;
+    woff[k] = wpad<K>(m);
+    wbit[k] = 16u - (uint32_t)(be & 15);
+  }
+  float2 w[32];  // w[p]: rows 4p + 2b, 4p + 2b + 1 of column c
+#pragma unroll
+  for (int tr = 0; tr < 8; ++tr) {
+    const uint32_t* tw = win + (tr * 8 + tcb) * kWS;
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+      const uint32_t s0 = bits16_at(tw[woff[k]], wbit[k]);
+      const uint32_t s1 = bits16_at(tw[woff[k + 1]], wbit[k + 1]);
+      const int x = k >> 2, sp = (k >> 1) & 1;
+      w[4 * tr + sp + 2 * x] = cb_decode2<CB>(s0, s1);
+    }
+  }
 
   if (out_w_hat) {  // transformed-basis reconstruction, before the rotations
+#pragma unroll
+    for (int p = 0; p < 32; ++p) {
+      blk[dpos(4 * p + 2 * b, c)] = w[p].x;
+      blk[dpos(4 * p + 2 * b + 1, c)] = w[p].y;
+    }
+    __syncthreads();
     for (int r = warp; r < kDB; r += kDecThreads / 32) {
-      const int f = dswz(r);
-      const float4 p = *reinterpret_cast<const float4*>(blk + r * kDB + ((4 * lane) ^ (f & ~3)));
-      const float4 o = (f & 2) ? make_float4(p.z, p.w, p.x, p.y) : p;
+      const float4 o = *reinterpret_cast<const float4*>(blk + r * kDB + ((4 * lane) ^ dswz(r)));
       *reinterpret_cast<float4*>(out_w_hat + (rb * kDB + r) * n + cbk * kDB + 4 * lane) = o;
     }
+    __syncthreads();
   }
 
-  float v[64];
-  const int b = tid & 1;
   const float sign = b ? -1.0f : 1.0f;
-  // 3. H_l on every column (thread pair per column: rows 2i + b), x 1/sqrt(128)
-  {
-    const int c = tid >> 1;
+  // left rotation on the column, x 1/sqrt(128)
+  fwht128_pair_line(w, sign);
 #pragma unroll
-    for (int i = 0; i < 64; ++i) v[i] = blk[dpos(2 * i + b, c)];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) v[i] = had_bfly(v[i], __shfl_xor_sync(0xFFFFFFFFu, v[i], 1), sign);
-    fwht64_regs(v);
-#pragma unroll
-    for (int i = 0; i < 64; ++i) blk[dpos(2 * i + b, c)] = v[i] * kHad128Scale;
+  for (int p = 0; p < 32; ++p) {
+    blk[dpos(4 * p + 2 * b, c)] = w[p].x;
+    blk[dpos(4 * p + 2 * b + 1, c)] = w[p].y;
   }
   __syncthreads();
-  // 4. x su, then H_r on every row (thread pair per row: columns 2i + b),
-  //    x 1/sqrt(128)
+  // 3. x su, then the right rotation on every row (two threads per row:
+  //    column pairs 4i + 2b, 4i + 2b + 1), x 1/sqrt(128). Column pair p =
+  //    8m + k sits at 32m + ((4k) ^ dswz(r)) + 2b: eight per-thread
+  //    pointers, the rest immediate offsets
   {
-    const int r = tid >> 1;
+    const int r = c;
     const float sur = load_scale<SCALE_F32>(su, rb * kDB + r);
+    const float2 su2 = make_float2(sur, sur);
     const int f = dswz(r);
+    float2* rp[8];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) v[i] = blk[r * kDB + ((2 * i + b) ^ f)] * sur;
+    for (int k = 0; k < 8; ++k)
+      rp[k] = reinterpret_cast<float2*>(blk + r * kDB + ((4 * k) ^ f) + 2 * b);
 #pragma unroll
-    for (int i = 0; i < 64; ++i) v[i] = had_bfly(v[i], __shfl_xor_sync(0xFFFFFFFFu, v[i], 1), sign);
-    fwht64_regs(v);
+    for (int p = 0; p < 32; ++p) w[p] = __fmul2_rn(rp[p & 7][16 * (p >> 3)], su2);
+    fwht128_pair_line(w, sign);
 #pragma unroll
-    for (int i = 0; i < 64; ++i) blk[r * kDB + ((2 * i + b) ^ f)] = v[i] * kHad128Scale;
+    for (int p = 0; p < 32; ++p) rp[p & 7][16 * (p >> 3)] = w[p];
   }
   __syncthreads();
-  // 5. x sv (per column) and the block written row by row with float4 stores
-  float svc[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) svc[e] = load_scale<SCALE_F32>(sv, cbk * kDB + 4 * lane + e);
+  // x sv (per column) and the block written row by row with float4 stores
+  float2 sv01, sv23;
+  sv01.x = load_scale<SCALE_F32>(sv, cbk * kDB + 4 * lane);
+  sv01.y = load_scale<SCALE_F32>(sv, cbk * kDB + 4 * lane + 1);
+  sv23.x = load_scale<SCALE_F32>(sv, cbk * kDB + 4 * lane + 2);
+  sv23.y = load_scale<SCALE_F32>(sv, cbk * kDB + 4 * lane + 3);
   for (int r = warp; r < kDB; r += kDecThreads / 32) {
-    const int f = dswz(r);
-    const float4 p = *reinterpret_cast<const float4*>(blk + r * kDB + ((4 * lane) ^ (f & ~3)));
-    const float4 o = (f & 2) ? make_float4(p.z, p.w, p.x, p.y) : p;
+    const float4 o = *reinterpret_cast<const float4*>(blk + r * kDB + ((4 * lane) ^ dswz(r)));
+    const float2 lo = __fmul2_rn(make_float2(o.x, o.y), sv01);
+    const float2 hi = __fmul2_rn(make_float2(o.z, o.w), sv23);
     *reinterpret_cast<float4*>(out + (rb * kDB + r) * n + cbk * kDB + 4 * lane) =
-        make_float4(o.x * svc[0], o.y * svc[1], o.z * svc[2], o.w * svc[3]);
+        make_float4(lo.x, lo.y, hi.x, hi.y);
   }
-}
-
-constexpr size_t decode_smem_bytes(int K) {
-  return (size_t)kDB * kDB * 4 + (size_t)64 * 16 * K * 2;
 }
 
 template <int K, int CB, int F32>
@@ -205,11 +306,11 @@ int launch_decode(const uint16_t* tw, const void* su, const void* sv, float* out
   if (!attr_done.has(dev)) {
     EXL3_CUDA(cudaFuncSetAttribute(decode_weight_kernel<K, CB, F32>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)decode_smem_bytes(K)));
+                                   (int)decode_smem_bytes<K>()));
     attr_done.set(dev);
   }
   const dim3 grid((unsigned)(tiles_n / 8), (unsigned)(tiles_k / 8));
-  decode_weight_kernel<K, CB, F32><<<grid, kDecThreads, decode_smem_bytes(K), stream>>>(
+  decode_weight_kernel<K, CB, F32><<<grid, kDecThreads, decode_smem_bytes<K>(), stream>>>(
       tw, su, sv, out, w_hat, tiles_n, tiles_n * 16);
   EXL3_LAUNCHED();
   return EXL3_OK;

@@ -223,8 +223,10 @@ int exl3_had128_left(float* x, int64_t k, int64_t n, exl3_stream_t stream);
 /*
  * H += X^T X on the tensor cores (tcgen05, fp32 accumulation): X is a
  * row-major (T, d) fp16 (dtype 0) or bf16 (dtype 1) matrix, 16-byte aligned,
- * d % 8 == 0; H is a row-major fp32 (d, d) matrix. Only the upper-triangle
- * 128x128 tiles are multiplied; the lower triangle is written by mirroring.
+ * d % 8 == 0; H is a row-major fp32 (d, d) matrix, symmetric on entry (as
+ * any sum of earlier calls is). Only tiles reaching the upper triangle are
+ * multiplied and added; the lower triangle is then rewritten from the upper
+ * one, so H is symmetric on return.
  * err_flag (device int) is set to 1 if a CTA gave up waiting on its own
  * tensor-core completion (it then skips its update). Replaces
  * HessianCollector._accumulate (exl3_quant/calibration.py:337-352).
