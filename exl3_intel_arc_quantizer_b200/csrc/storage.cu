@@ -129,8 +129,10 @@ __device__ __forceinline__ void fwht128_pair_line(float2 (&w)[32], float sign) {
   const float2 sg = make_float2(sign, sign);
 #pragma unroll
   for (int p = 0; p < 32; ++p) {
-    const float2 o = make_float2(__shfl_xor_sync(0xFFFFFFFFu, w[p].x, 1),
-                                 __shfl_xor_sync(0xFFFFFFFFu, w[p].y, 1));
+    // one 64-bit shuffle: both halves land in a register pair
+    const unsigned long long mine = *reinterpret_cast<const unsigned long long*>(&w[p]);
+    const unsigned long long theirs = __shfl_xor_sync(0xFFFFFFFFu, mine, 1);
+    const float2 o = *reinterpret_cast<const float2*>(&theirs);
     w[p] = __ffma2_rn(sg, w[p], o);
   }
 #pragma unroll
@@ -170,6 +172,16 @@ __device__ __forceinline__ uint32_t bits16_at(uint32_t w, uint32_t pos) {
   uint32_t r;
   asm("bfe.u32 %0, %1, %2, 16;" : "=r"(r) : "r"(w), "r"(pos));
   return r;
+}
+
+// K = 4 and K = 8: K (e + 1) mod 16 depends only on e mod 4 (K = 4: the
+// thread's 2x + j, K = 8: j), so the window bit of slot k is a constant
+template <int K>
+__device__ __forceinline__ constexpr bool const_window_bit() { return K == 4 || K == 8; }
+template <int K>
+__device__ __forceinline__ constexpr uint32_t window_bit_of_slot(int k) {
+  // slot k = 4x + 2sp + j; e = 16 * (...) + 2x + 8b + j + 4 (lc >> 3)
+  return 16u - (uint32_t)((K * (2 * (k >> 2) + (k & 1) + 1)) & 15);
 }
 
 template <int K>
@@ -232,8 +244,15 @@ decode_weight_kernel(const uint16_t* __restrict__ trellis, const void* __restric
     const uint32_t* tw = win + (tr * 8 + tcb) * kWS;
 #pragma unroll
     for (int k = 0; k < 8; k += 2) {
-      const uint32_t s0 = bits16_at(tw[woff[k]], wbit[k]);
-      const uint32_t s1 = bits16_at(tw[woff[k + 1]], wbit[k + 1]);
+      uint32_t s0, s1;
+      if constexpr (const_window_bit<K>()) {
+        constexpr uint32_t kMask = 0xFFFFu;
+        s0 = (tw[woff[k]] >> window_bit_of_slot<K>(k)) & kMask;
+        s1 = (tw[woff[k + 1]] >> window_bit_of_slot<K>(k + 1)) & kMask;
+      } else {
+        s0 = bits16_at(tw[woff[k]], wbit[k]);
+        s1 = bits16_at(tw[woff[k + 1]], wbit[k + 1]);
+      }
       const int x = k >> 2, sp = (k >> 1) & 1;
       w[4 * tr + sp + 2 * x] = cb_decode2<CB>(s0, s1);
     }
