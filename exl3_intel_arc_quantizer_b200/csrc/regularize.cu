@@ -80,9 +80,17 @@ __global__ void __launch_bounds__(1024) reg_skew_kernel(const float* __restrict_
   for (int shift = 24; shift >= 0 && want > 0; shift -= 8) {
     for (int i = t; i < 256; i += blockDim.x) hist[i] = 0u;
     __syncthreads();
-    for (int64_t i = t; i < d; i += blockDim.x) {
-      const uint32_t key = __float_as_uint(sqrtf(hdiag[i * stride]));
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+    // warp-aggregated counts: most keys share the few top-byte digits of
+    // similar magnitudes, so one atomic per distinct digit per warp
+    for (int64_t i0 = 0; i0 < d; i0 += blockDim.x) {
+      const int64_t i = i0 + t;
+      uint32_t dig = 0x100u;  // no digit
+      if (i < d) {
+        const uint32_t key = __float_as_uint(sqrtf(hdiag[i * stride]));
+        if ((key & mask) == prefix) dig = (key >> shift) & 255u;
+      }
+      const unsigned peers = __match_any_sync(0xFFFFFFFFu, dig);
+      if (dig != 0x100u && __ffs(peers) - 1 == (t & 31)) atomicAdd(&hist[dig], __popc(peers));
     }
     __syncthreads();
     if (t < 32) {
@@ -258,14 +266,30 @@ __global__ void reg_right_kernel(const float* __restrict__ W, const float* __res
   for (int q = 0; q < 4; ++q) v[q] = __fdiv_rn(v[q], d[q]);
   fwht128_warp(v, lane);
   float* dst = work + row * n + blk * 128;
+  float sq[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     v[q] = __fmul_rn(v[q], kHad128Scale);
     dst[lane + 32 * q] = v[q];
-    float s = __fmul_rn(v[q], v[q]);
-    for (int o = 16; o; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, o));
-    if (lane == 0) rpart[(blk * 4 + q) * k + row] = s;
+    sq[q] = __fmul_rn(v[q], v[q]);
   }
+  // the four slice sums by one transposed reduction: at offset 16 a lane
+  // keeps two slices (lanes < 16 slices 0, 1, the others 2, 3) and adds its
+  // partner's values of them, at offset 8 one slice, then offsets 4, 2, 1.
+  // Every slice is summed over the same pairwise tree (lane pairs 16 apart,
+  // then 8, 4, 2, 1) as a full warp reduction per slice, so the sums are
+  // bit-identical to that, with 6 shuffles instead of 20.
+  const bool h16 = lane & 16, h8 = lane & 8;
+  float a0 = h16 ? sq[2] : sq[0], a1 = h16 ? sq[3] : sq[1];
+  const float g0 = __shfl_xor_sync(0xFFFFFFFFu, h16 ? sq[0] : sq[2], 16);
+  const float g1 = __shfl_xor_sync(0xFFFFFFFFu, h16 ? sq[1] : sq[3], 16);
+  a0 = __fadd_rn(a0, g0);
+  a1 = __fadd_rn(a1, g1);
+  float t = h8 ? a1 : a0;
+  t = __fadd_rn(t, __shfl_xor_sync(0xFFFFFFFFu, h8 ? a0 : a1, 8));
+  for (int o = 4; o; o >>= 1) t = __fadd_rn(t, __shfl_xor_sync(0xFFFFFFFFu, t, o));
+  // lane 0 holds slice 0, lane 8 slice 1, lane 16 slice 2, lane 24 slice 3
+  if ((lane & 7) == 0) rpart[(blk * 4 + (lane >> 3)) * k + row] = t;
 }
 
 // Row RMS from the 32-column slice sums (CTA of 32 rows x 8 chains) and su
