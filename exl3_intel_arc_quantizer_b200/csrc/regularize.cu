@@ -80,17 +80,9 @@ __global__ void __launch_bounds__(1024) reg_skew_kernel(const float* __restrict_
   for (int shift = 24; shift >= 0 && want > 0; shift -= 8) {
     for (int i = t; i < 256; i += blockDim.x) hist[i] = 0u;
     __syncthreads();
-    // warp-aggregated counts: most keys share the few top-byte digits of
-    // similar magnitudes, so one atomic per distinct digit per warp
-    for (int64_t i0 = 0; i0 < d; i0 += blockDim.x) {
-      const int64_t i = i0 + t;
-      uint32_t dig = 0x100u;  // no digit
-      if (i < d) {
-        const uint32_t key = __float_as_uint(sqrtf(hdiag[i * stride]));
-        if ((key & mask) == prefix) dig = (key >> shift) & 255u;
-      }
-      const unsigned peers = __match_any_sync(0xFFFFFFFFu, dig);
-      if (dig != 0x100u && __ffs(peers) - 1 == (t & 31)) atomicAdd(&hist[dig], __popc(peers));
+    for (int64_t i = t; i < d; i += blockDim.x) {
+      const uint32_t key = __float_as_uint(sqrtf(hdiag[i * stride]));
+      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
     }
     __syncthreads();
     if (t < 32) {
