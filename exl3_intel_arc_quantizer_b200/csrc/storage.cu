@@ -246,9 +246,16 @@ decode_weight_kernel(const uint16_t* __restrict__ trellis, const void* __restric
     for (int k = 0; k < 8; k += 2) {
       uint32_t s0, s1;
       if constexpr (const_window_bit<K>()) {
+        // one window holds both states of the pair (they overlap in 16 - K
+        // bits; the first starts at most 16 - K bits into the window)
         constexpr uint32_t kMask = 0xFFFFu;
-        s0 = (tw[woff[k]] >> window_bit_of_slot<K>(k)) & kMask;
-        s1 = (tw[woff[k + 1]] >> window_bit_of_slot<K>(k + 1)) & kMask;
+        const uint32_t win0 = tw[woff[k]];
+        s0 = (win0 >> window_bit_of_slot<K>(k)) & kMask;
+        s1 = (win0 >> (window_bit_of_slot<K>(k) - K)) & kMask;
+      } else if constexpr (K == 1 || K == 2) {
+        const uint32_t win0 = tw[woff[k]];
+        s0 = bits16_at(win0, wbit[k]);
+        s1 = bits16_at(win0, wbit[k] - K);
       } else {
         s0 = bits16_at(tw[woff[k]], wbit[k]);
         s1 = bits16_at(tw[woff[k + 1]], wbit[k + 1]);
