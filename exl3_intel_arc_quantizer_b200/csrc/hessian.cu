@@ -6,7 +6,7 @@
 // sums up to summation order.
 //
 // Design (one CTA per 128 x 256 tile of H that reaches the upper triangle,
-// or per 256 x 256 tile for wide H, see HGeo; 6 warps with fixed roles):
+// or per 256 x 256 tile for wide H, see HGeo; 10 warps with fixed roles):
 //   * warp 0 (one lane) streams X through TMA: per 64-token chunk, the
 //     128-column A slab X[t:t+64, i0:i0+128] and the 256-column B slab
 //     X[t:t+64, j0:j0+256] as 64 x 64 boxes with 128-byte swizzle, straight
@@ -16,11 +16,13 @@
 //     tcgen05.commit frees each stage and, every 8192 tokens (a segment),
 //     hands the finished accumulator to the epilogue and switches to the
 //     other one;
-//   * warps 2-5 drain a finished accumulator (tcgen05.ld), stage each 32x32
+//   * warps 2-9 (two per TMEM lane quarter, each half of the columns) drain
+//     a finished accumulator (tcgen05.ld), stage each 32x32
 //     block in shared memory and add its elements (r, c), c >= r, into H
 //     with 16-byte red.global.add.v4.f32 (L2 evict-last, so H's lines stay
 //     cached between segments), while the MMAs of the next segment run;
 //   * hessian_mirror_kernel then copies the upper triangle to the lower one.
+// Long calls run as one launch per 65,536-token slab (kSlabTokens).
 // Draining every segment bounds the length of each tensor-core accumulation
 // chain (its additions are not round-to-nearest, so long chains drift). H is
 // symmetric after every call; on entry only its upper triangle is read (the
@@ -46,13 +48,14 @@ constexpr int kBN = 256;                 // tile columns (j)
 constexpr int kBK = 64;                  // tokens per stage
 constexpr int kStages = 4;
 constexpr int kSegChunks = 128;          // 8192 tokens per accumulator segment
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;            // two per TMEM lane quarter
+constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr int kABytes = kBM * kBK * 2;   // 16 KiB
 constexpr int kBBytes = kBN * kBK * 2;   // 32 KiB
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kBoxBytes = 64 * kBK * 2;  // one 64-column x 64-token box, 8 KiB
 constexpr int kStgPitch = 33;
-constexpr int kStgBytes = 4 * 32 * kStgPitch * 4;
+constexpr int kStgBytes = kEpiWarps * 32 * kStgPitch * 4;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait
 
 // MB = 128-row A slabs per tile. MB = 1: 128 x 256 tiles, four stages of
@@ -229,7 +232,8 @@ __device__ __forceinline__ void tile_of(int idx, int nbi, int nbj, int& bi, int&
 
 template <int BF16, int MB>
 __global__ void __launch_bounds__(kThreads, 1)
-hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, int64_t d,
+hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t t_base, int64_t T_tokens,
+                   int64_t d,
                    float* __restrict__ H, int nbi, int nbj, int* __restrict__ err_flag) {
   using G = HGeo<MB>;
   extern __shared__ uint8_t dsm_raw[];
@@ -262,7 +266,7 @@ hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, i
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf(b), 1);
-      mbar_init(acce(b), 4);
+      mbar_init(acce(b), kEpiWarps);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -290,7 +294,7 @@ hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, i
                      : "memory");
         const uint32_t a = smem_u32(stage_base + s * G::kStageBytesM);
         const uint32_t b = a + G::kABytesM;
-        const int t0 = c * kBK;
+        const int t0 = (int)(t_base + (int64_t)c * kBK);
 #pragma unroll
         for (int m = 0; m < MB; ++m) {
           tma_load_2d(a + m * kABytes, &xmap, i0 + 128 * m, t0, full(s));
@@ -352,8 +356,9 @@ hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, i
         mbar_drain(empty(last_commit % G::kStagesM), (last_commit / G::kStagesM) & 1);
     }
   } else {
-    // ---------------- epilogue: warps 2..5 ----------------
+    // ---------------- epilogue: warps 2..9 ----------------
     const int quarter = warp & 3;  // this warp may read TMEM lanes 32*quarter .. +31
+    const int half = (warp - 2) >> 2;  // and drains this half of the accumulator columns
     const uint64_t hpol = l2_evict_last_policy();
     float* my_stg = stg + (warp - 2) * 32 * kStgPitch;
     for (int seg = 0; seg < nseg; ++seg) {
@@ -362,7 +367,7 @@ hessian_tma_kernel(const __grid_constant__ CUtensorMap xmap, int64_t T_tokens, i
       if (!__all_sync(0xFFFFFFFFu, ok)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll 1
-      for (int mc = 0; mc < MB * kBN; mc += 32) {
+      for (int mc = half * (MB * kBN / 2); mc < (half + 1) * (MB * kBN / 2); mc += 32) {
         const int m = mc / kBN, cb = mc % kBN;
         const int row_base = i0 + 128 * m + 32 * quarter;
         uint32_t v[32];
@@ -454,6 +459,14 @@ __global__ void __launch_bounds__(256) hessian_mirror_kernel(float* __restrict__
 // 2 = 256 x 256. Set only by exl3_hessian_set_tile (tests and probes).
 std::atomic<int> g_tile_mode{0};
 
+// Tokens per launch: a wave of CTAs shares each X slab in L2 only while its
+// CTAs stay near the same token chunk, and over a long call they drift apart
+// (d = 12288: 262,144 tokens in one launch ran at 1,140 TFLOP/s, 65,536 at
+// 1,430). A multiple of the 8192-token segment, so the segments, and with
+// them the sums, are those of one launch.
+constexpr int64_t kSlabTokens = 65536;
+static_assert(kSlabTokens % (kSegChunks * kBK) == 0, "slabs hold whole segments");
+
 template <int BF16, int MB>
 int launch_hessian(const CUtensorMap& map, int64_t T, int64_t d, float* H, int nbi, int nbj,
                    int64_t ntiles, int* err_flag, int dev, exl3_stream_t stream) {
@@ -464,8 +477,12 @@ int launch_hessian(const CUtensorMap& map, int64_t T, int64_t d, float* H, int n
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_done.set(dev);
   }
-  hessian_tma_kernel<BF16, MB><<<(unsigned)ntiles, kThreads, smem, (cudaStream_t)stream>>>(
-      map, T, d, H, nbi, nbj, err_flag);
+  for (int64_t tb = 0; tb < T; tb += kSlabTokens) {
+    const int64_t len = T - tb < kSlabTokens ? T - tb : kSlabTokens;
+    hessian_tma_kernel<BF16, MB><<<(unsigned)ntiles, kThreads, smem, (cudaStream_t)stream>>>(
+        map, tb, len, d, H, nbi, nbj, err_flag);
+    EXL3_LAUNCHED();
+  }
   return EXL3_OK;
 }
 
