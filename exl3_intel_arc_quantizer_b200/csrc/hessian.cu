@@ -464,7 +464,10 @@ std::atomic<int> g_tile_mode{0};
 // (d = 12288: 262,144 tokens in one launch ran at 1,140 TFLOP/s, 65,536 at
 // 1,430). A multiple of the 8192-token segment, so the segments, and with
 // them the sums, are those of one launch.
-constexpr int64_t kSlabTokens = 65536;
+#ifndef EXL3_HESS_SLAB
+#define EXL3_HESS_SLAB 65536
+#endif
+constexpr int64_t kSlabTokens = EXL3_HESS_SLAB;
 static_assert(kSlabTokens % (kSegChunks * kBK) == 0, "slabs hold whole segments");
 
 template <int BF16, int MB>
