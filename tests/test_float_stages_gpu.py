@@ -129,6 +129,29 @@ def test_hessian_long_accumulation_stays_within_tolerance():
     assert torch.equal(H, H2)          # deterministic
 
 
+def test_hessian_rewrites_the_lower_triangle_from_the_upper():
+    """The accumulation adds X^T X to the upper triangle (tiles reaching it)
+    and then copies the upper triangle onto the lower one, so a symmetric H
+    stays exactly symmetric and a lower triangle that disagrees with the
+    upper one is overwritten (the documented contract: H symmetric on
+    entry). 70,000 tokens span two 65,536-token launches."""
+    from exl3_intel_arc_quantizer_b200._ext import ext
+
+    d, T = 384, 70000
+    g = torch.Generator(device=DEV).manual_seed(17)
+    x = torch.randn(T, d, generator=g, device=DEV, dtype=torch.bfloat16)
+    base = torch.randn(d, d, generator=g, device=DEV)
+    H = base.clone()
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ext().hessian_accumulate_(H, x, err)
+    assert int(err.item()) == 0
+    assert torch.equal(H, H.T)
+    xf = x.float()
+    want = torch.triu(base) + torch.triu(xf.T @ xf)
+    up = torch.triu(torch.ones(d, d, dtype=torch.bool, device=DEV))
+    assert float((H[up] - want[up]).abs().max() / want[up].abs().max()) <= 1e-4
+
+
 @pytest.mark.parametrize("d,T", [(136, 300), (520, 8200), (1032, 9000), (2048, 640)])
 def test_hessian_tile_shapes_agree_bit_for_bit(d, T):
     """128 x 256 and 256 x 256 tiles (forced through exl3_hessian_set_tile)
