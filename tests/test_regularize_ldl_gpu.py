@@ -141,15 +141,17 @@ def test_block_ldl_fold_matches_reference_function(ref, n):
     assert float(torch.triu(L, diagonal=1).abs().max()) == 0.0    # zeros above the diagonal
 
 
-def test_block_ldl_fold_equals_the_torch_fold_on_the_same_factor():
+@pytest.mark.parametrize("n", [80, 208, 4096])
+def test_block_ldl_fold_equals_the_torch_fold_on_the_same_factor(n):
     """On one device factor, the kernel's fold agrees with the reference op
-    sequence (batched inverse + batched product) run on the device."""
+    sequence (batched inverse + batched product) run on the device; 80 and
+    208 leave ragged 64 x 64 tiles at the edges."""
     from exl3_intel_arc_quantizer_b200._ext import ext
 
-    n = 4096
-    g = torch.Generator(device=DEV).manual_seed(3)
-    a = torch.randn(n, 2048, generator=g, device=DEV)
-    chol = torch.linalg.cholesky(a @ a.T / 2048 + 0.01 * torch.eye(n, device=DEV)).contiguous()
+    w = max(n // 2, 64)
+    g = torch.Generator(device=DEV).manual_seed(3 + n)
+    a = torch.randn(n, w, generator=g, device=DEV)
+    chol = torch.linalg.cholesky(a @ a.T / w + 0.01 * torch.eye(n, device=DEV)).contiguous()
     L = torch.empty_like(chol)
     inv = torch.empty((n // 16, 16, 16), device=DEV)
     ext().block_ldl_fold(chol, L, inv)
