@@ -202,21 +202,58 @@ decode_weight_kernel(const uint16_t* __restrict__ trellis, const void* __restric
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t rb = blockIdx.y, cbk = blockIdx.x;
 
-  // 1. windows: each tile row of the block is one contiguous run of 8 tiles;
-  //    stored 32-bit word q is stream words 2q + 1, 2q (SWAP16), so window 2q
-  //    is the word itself and window 2q + 1 joins its low half with the next
-  //    word's high half
+  // the scales are loaded first, so that their latency hides behind phase 1
+  const int b = tid & 1, c = tid >> 1, lc = c & 15, tcb = c >> 4;
+  const float sur = load_scale<SCALE_F32>(su, rb * kDB + c);
+  float2 sv01, sv23;
+  sv01.x = load_scale<SCALE_F32>(sv, cbk * kDB + 4 * lane);
+  sv01.y = load_scale<SCALE_F32>(sv, cbk * kDB + 4 * lane + 1);
+  sv23.x = load_scale<SCALE_F32>(sv, cbk * kDB + 4 * lane + 2);
+  sv23.y = load_scale<SCALE_F32>(sv, cbk * kDB + 4 * lane + 3);
+
+  // 1. windows. Each tile row of the block is one contiguous run of 8 tiles
+  //    (8 * kW32 words); all 2K words a thread copies are loaded at once (one
+  //    DRAM round trip per CTA, not one per tile row). Stored 32-bit word q is
+  //    stream words 2q + 1, 2q (SWAP16), so window 2q is the word itself and
+  //    window 2q + 1 joins its low half with the next word's high half; the
+  //    next word comes from a shuffle where a tile fits in a warp (K = 1, 2,
+  //    4), else from a copy staged in the fp32 tile's space (free until
+  //    phase 2 has read the windows)
+  {
+    constexpr int kRun = 8 * kW32;
+    static_assert(8 * kRun <= kDB * kDB, "the staged container must fit in the fp32 tile");
+    uint32_t* stage = reinterpret_cast<uint32_t*>(blk);  // 64 tiles x kW32, block order
+    uint32_t v[2 * K];
 #pragma unroll
-  for (int tr = 0; tr < 8; ++tr) {
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(
-        trellis + ((rb * 8 + tr) * tiles_n + cbk * 8) * (int64_t)(16 * K));
-    for (int i = tid; i < 8 * kW32; i += kDecThreads) {
-      const int t = i / kW32, q = i - t * kW32;
-      const uint32_t a = src[i];
-      const uint32_t nx = src[t * kW32 + (q + 1 < kW32 ? q + 1 : 0)];
-      uint32_t* tw = win + (tr * 8 + t) * kWS;
-      tw[wpad<K>(2 * q)] = a;
-      tw[wpad<K>(2 * q + 1)] = (a << 16) | (nx >> 16);
+    for (int it = 0; it < 2 * K; ++it) {
+      const int i = it * kDecThreads + tid, tr = i / kRun;
+      v[it] = reinterpret_cast<const uint32_t*>(
+          trellis + ((rb * 8 + tr) * tiles_n + cbk * 8) * (int64_t)(16 * K))[i - tr * kRun];
+    }
+    if constexpr (32 % kW32 == 0) {
+      // K = 1, 2, 4: a tile's words sit in kW32 consecutive lanes of one
+      // warp, so the next word (circular) is one shuffle away
+#pragma unroll
+      for (int it = 0; it < 2 * K; ++it) {
+        const int i = it * kDecThreads + tid, t = i / kW32, q = i - t * kW32;
+        const uint32_t nx = __shfl_sync(0xFFFFFFFFu, v[it], lane + 1, kW32);
+        uint32_t* tw = win + t * kWS;
+        tw[wpad<K>(2 * q)] = v[it];
+        tw[wpad<K>(2 * q + 1)] = (v[it] << 16) | (nx >> 16);
+      }
+    } else {
+#pragma unroll
+      for (int it = 0; it < 2 * K; ++it) stage[it * kDecThreads + tid] = v[it];
+      __syncthreads();
+#pragma unroll
+      for (int it = 0; it < 2 * K; ++it) {
+        const int i = it * kDecThreads + tid, t = i / kW32, q = i - t * kW32;
+        const uint32_t a = stage[i];
+        const uint32_t nx = stage[t * kW32 + (q + 1 < kW32 ? q + 1 : 0)];
+        uint32_t* tw = win + t * kWS;
+        tw[wpad<K>(2 * q)] = a;
+        tw[wpad<K>(2 * q + 1)] = (a << 16) | (nx >> 16);
+      }
     }
   }
   __syncthreads();
@@ -225,7 +262,6 @@ decode_weight_kernel(const uint16_t* __restrict__ trellis, const void* __restric
   //    the column's local index lc takes spans s = 2 (lc & 7) + sp and span
   //    elements u = 4 (lc >> 3) + 2x + 8b + j; element e = 16 s + u sits at
   //    local row 4 sp + 8x + 2b + j, i.e. pair index 4 tr + sp + 2x
-  const int b = tid & 1, c = tid >> 1, lc = c & 15, tcb = c >> 4;
   int woff[8];
   uint32_t wbit[8];
 #pragma unroll
@@ -294,7 +330,6 @@ decode_weight_kernel(const uint16_t* __restrict__ trellis, const void* __restric
   //    pointers, the rest immediate offsets
   {
     const int r = c;
-    const float sur = load_scale<SCALE_F32>(su, rb * kDB + r);
     const float2 su2 = make_float2(sur, sur);
     const int f = dswz(r);
     float2* rp[8];
@@ -309,11 +344,6 @@ decode_weight_kernel(const uint16_t* __restrict__ trellis, const void* __restric
   }
   __syncthreads();
   // x sv (per column) and the block written row by row with float4 stores
-  float2 sv01, sv23;
-  sv01.x = load_scale<SCALE_F32>(sv, cbk * kDB + 4 * lane);
-  sv01.y = load_scale<SCALE_F32>(sv, cbk * kDB + 4 * lane + 1);
-  sv23.x = load_scale<SCALE_F32>(sv, cbk * kDB + 4 * lane + 2);
-  sv23.y = load_scale<SCALE_F32>(sv, cbk * kDB + 4 * lane + 3);
   for (int r = warp; r < kDB; r += kDecThreads / 32) {
     const float4 o = *reinterpret_cast<const float4*>(blk + r * kDB + ((4 * lane) ^ dswz(r)));
     const float2 lo = __fmul2_rn(make_float2(o.x, o.y), sv01);
