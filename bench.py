@@ -521,8 +521,36 @@ def run_storage(device, K=4, shapes=((4096, 4096), (12288, 4096)), reps=5):
         for key in ("pack", "unpack", "decode", "had_left", "had_right", "regularize", "ldl_fold"):
             row[f"{key}_frac_of_measured_hbm"] = row[f"{key}_gbs"] / hbm
         out.append(row)
-    del flush
-    return {"kernels": out, "hbm_peak_gbs": hbm,
+    # the weight decode at every K on the largest shape (MUL1 codebook, fp16
+    # scales, random containers)
+    k, n = shapes[-1]
+    g = torch.Generator(device=device).manual_seed(17)
+    su = (torch.rand(k, generator=g, device=device) + 0.5).half()
+    sv = (torch.rand(n, generator=g, device=device) + 0.5).half()
+    w = torch.empty((k, n), dtype=torch.float32, device=device)
+    sweep = []
+    for kk in range(1, 9):
+        cont = torch.randint(-32768, 32767, (k // 16, n // 16, 16 * kk), generator=g,
+                             device=device, dtype=torch.int32).to(torch.int16)
+        ts = []
+        for r in range(reps + 1):
+            flush.fill_(r & 0xFF)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            e.decode_weight(cont, su, sv, w, None, kk, 2)
+            e1.record()
+            e1.synchronize()
+            if r:
+                ts.append(e0.elapsed_time(e1))
+        t = statistics.median(ts)
+        gbs = k * n * (kk / 8 + 4) / t / 1e6
+        sweep.append({"K": kk, "ms": round(t, 4), "gbs": round(gbs, 1),
+                      "frac_of_measured_hbm": round(gbs / hbm, 3)})
+        del cont
+    del flush, w
+    return {"kernels": out, "decode_k_sweep": {"shape": [k, n], "rows": sweep},
+            "hbm_peak_gbs": hbm,
             "peak_source": "MEASURED_PEAKS.json hbm_gbs (copy)" if peaks else "fallback 6650"}
 
 

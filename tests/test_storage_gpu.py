@@ -101,6 +101,29 @@ def test_full_size_roundtrip_through_encoder():
         assert float((dec16 - res.w_hat).abs().max()) <= 2e-3 * float(res.w_hat.abs().max())
 
 
+@pytest.mark.parametrize("K", range(1, 9))
+def test_decode_multi_block_every_k(K):
+    """A 384 x 256 weight (3 x 2 blocks of 128 x 128) from a random container
+    at every K and codebook: the decode kernel's w_hat equals the oracle's
+    state -> codebook -> tile placement bit for bit, and the weight equals
+    the package's own rotation of that w_hat bit for bit (fp32 scales) - so
+    the per-block container offsets, the window table and both rotations
+    are checked away from block (0, 0) for the shuffle (K = 1, 2, 4) and the
+    staged (other K) window builds alike."""
+    rng = np.random.default_rng(70 + K)
+    tk, tn = 24, 16
+    tr_np = rng.integers(-32768, 32768, size=(tk, tn, 16 * K)).astype(np.int16)
+    su = torch.from_numpy(rng.uniform(0.5, 1.5, tk * 16).astype(np.float32)).to(DEV)
+    sv = torch.from_numpy(rng.uniform(0.5, 1.5, tn * 16).astype(np.float32)).to(DEV)
+    tr = torch.from_numpy(tr_np).to(DEV)
+    for cb in (0, 1, 2):
+        dec, w_hat = ser.decode_weight_from_storage(tr, su, sv, K=K, cb=cb, return_w_hat=True)
+        assert torch.equal(w_hat.cpu(), torch.from_numpy(so.w_hat_from_trellis(tr_np, K, cb)))
+        assert torch.equal(dec, weight_from_quantized(w_hat, su, sv)), (K, cb)
+        ref = so.weight_from_quantized(w_hat.cpu().numpy(), su.cpu().numpy(), sv.cpu().numpy())
+        assert float(np.abs(dec.cpu().numpy() - ref).max()) <= 1e-5 * float(np.abs(ref).max())
+
+
 def test_validation():
     tr = torch.zeros(8, 8, 32, dtype=torch.int16, device=DEV)
     ones = torch.ones(128, dtype=torch.float16, device=DEV)
