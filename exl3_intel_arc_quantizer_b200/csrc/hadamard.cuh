@@ -83,4 +83,66 @@ __device__ __forceinline__ void had_left_quad_cols(float* __restrict__ col, int6
   }
 }
 
+// The same transform on two adjacent columns at once: thread (p, q) holds
+// rows 4i + q of columns 2p and 2p + 1 as one float2 per row, so each load,
+// store and shuffle moves both columns and every butterfly and the scale are
+// one packed f32x2 operation (each lane rounds as the scalar operation does:
+// fma with a +-1 factor for the shuffle strides, add and fma(hi, -1, lo) for
+// the register strides, the order of had_left_quad_cols). A warp covers 16
+// columns of four rows per access (64-byte row segments). `col` points at
+// column 2p of the block's first row and must be 8-byte aligned with n even.
+template <bool DIV>
+__device__ __forceinline__ void had_left_pair_cols(float* __restrict__ col, int64_t n,
+                                                   const float* __restrict__ su, int q,
+                                                   bool valid) {
+  float2 v[32];
+  const int64_t step = 4 * n;
+  const float* src = col + (int64_t)q * n;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    v[i] = valid ? *reinterpret_cast<const float2*>(src) : make_float2(0.f, 0.f);
+    src += step;
+  }
+  if (DIV) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float s = su[4 * i + q];
+      v[i] = make_float2(__fdiv_rn(v[i].x, s), __fdiv_rn(v[i].y, s));
+    }
+  }
+#pragma unroll
+  for (int b = 1; b <= 2; b <<= 1) {
+    const float sg = (q & b) ? -1.0f : 1.0f;
+    const float2 sg2 = make_float2(sg, sg);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const unsigned long long mine = *reinterpret_cast<const unsigned long long*>(&v[i]);
+      const unsigned long long theirs = __shfl_xor_sync(0xFFFFFFFFu, mine, b);
+      v[i] = __ffma2_rn(sg2, v[i], *reinterpret_cast<const float2*>(&theirs));
+    }
+  }
+  const float2 neg = make_float2(-1.0f, -1.0f);
+#pragma unroll
+  for (int h = 1; h < 32; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (i & h) continue;
+      const float2 lo = v[i], hi = v[i + h];
+      v[i] = __fadd2_rn(lo, hi);
+      v[i + h] = __ffma2_rn(hi, neg, lo);
+    }
+  }
+  if (!valid) return;
+  float* dst = col + (int64_t)q * n;
+  // an opaque copy of the pointer: the store addresses are stepped afresh
+  // instead of 32 load addresses being held through the butterflies
+  asm volatile("" : "+l"(dst));
+  const float2 sc = make_float2(kHad128Scale, kHad128Scale);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    *reinterpret_cast<float2*>(dst) = __fmul2_rn(v[i], sc);
+    dst += step;
+  }
+}
+
 }  // namespace exl3

@@ -46,6 +46,17 @@ __global__ void __launch_bounds__(256, 2) had_left_kernel(float* __restrict__ x,
                             t & 3, valid);
 }
 
+// The same with two adjacent columns per thread (had_left_pair_cols; n even,
+// x 8-byte aligned): a CTA of 256 threads takes 128 columns of one row block.
+__global__ void __launch_bounds__(256, 2) had_left_pair_kernel(float* __restrict__ x, int64_t k,
+                                                               int64_t n) {
+  const int t = threadIdx.x;
+  const int64_t c = (int64_t)blockIdx.x * 128 + 2 * (t >> 2);
+  const bool valid = c < n;
+  had_left_pair_cols<false>(x + (int64_t)blockIdx.y * 128 * n + (valid ? c : 0), n, nullptr,
+                            t & 3, valid);
+}
+
 // diag mean of H / count (one CTA)
 __global__ void hess_diag_mean_kernel(const float* __restrict__ H, int64_t d, double inv_count,
                                       double* __restrict__ out) {
@@ -104,8 +115,13 @@ extern "C" int exl3_had128_left(float* x, int64_t k, int64_t n, exl3_stream_t st
   EXL3_REQUIRE(n > 0 && k > 0 && k % 128 == 0, "rows (%lld) must be a positive multiple of 128",
                (long long)k);
   EXL3_REQUIRE(k / 128 < 65536, "too many row blocks");
-  dim3 grid((unsigned)((n + 63) / 64), (unsigned)(k / 128));
-  had_left_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, k, n);
+  if (n % 2 == 0 && reinterpret_cast<uintptr_t>(x) % 8 == 0) {
+    const dim3 grid((unsigned)((n + 127) / 128), (unsigned)(k / 128));
+    had_left_pair_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, k, n);
+  } else {
+    const dim3 grid((unsigned)((n + 63) / 64), (unsigned)(k / 128));
+    had_left_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, k, n);
+  }
   EXL3_LAUNCHED();
   return EXL3_OK;
 }

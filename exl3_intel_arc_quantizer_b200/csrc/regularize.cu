@@ -313,6 +313,21 @@ __global__ void __launch_bounds__(256, 2) reg_left_kernel(float* __restrict__ wo
                            t & 3, valid);
 }
 
+// the same with two adjacent columns per thread (had_left_pair_cols; work
+// 8-byte aligned): a CTA takes 128 columns of one row block
+__global__ void __launch_bounds__(256, 2) reg_left_pair_kernel(float* __restrict__ work,
+                                                               const float* __restrict__ su,
+                                                               int64_t k, int64_t n) {
+  __shared__ float su_s[128];
+  const int t = threadIdx.x;
+  if (t < 128) su_s[t] = su[(int64_t)blockIdx.y * 128 + t];
+  __syncthreads();
+  const int64_t c = (int64_t)blockIdx.x * 128 + 2 * (t >> 2);
+  const bool valid = c < n;
+  had_left_pair_cols<true>(work + (int64_t)blockIdx.y * 128 * n + (valid ? c : 0), n, su_s,
+                           t & 3, valid);
+}
+
 // D_b^-1 of every 16x16 diagonal block of C (lower triangular) by forward
 // substitution: one CTA per four blocks, D staged in shared memory, thread
 // (g, j) computes column j of block g's inverse.
@@ -480,8 +495,13 @@ extern "C" int exl3_regularize(const float* W, const float* su_in, const float* 
   reg_rowfinal_kernel<<<(unsigned)((k + 31) / 32), 256, 0, s>>>(rp, n / 32, k, n, su_in,
                                                                  in_scales, su_out);
   EXL3_LAUNCHED();
-  reg_left_kernel<<<dim3((unsigned)((n + 63) / 64), (unsigned)(k / 128)), 256, 0, s>>>(
-      work, su_out, k, n);
+  if (reinterpret_cast<uintptr_t>(work) % 8 == 0) {  // n is a multiple of 128
+    reg_left_pair_kernel<<<dim3((unsigned)(n / 128), (unsigned)(k / 128)), 256, 0, s>>>(
+        work, su_out, k, n);
+  } else {
+    reg_left_kernel<<<dim3((unsigned)((n + 63) / 64), (unsigned)(k / 128)), 256, 0, s>>>(
+        work, su_out, k, n);
+  }
   EXL3_LAUNCHED();
   return EXL3_OK;
 }

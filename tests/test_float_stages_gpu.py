@@ -54,6 +54,48 @@ def test_hadamard_matches_reference(float_golden):
         hd.preapply_had_l(torch.zeros(100, 128, device=DEV))
 
 
+def test_left_rotation_two_column_and_four_thread_kernels_agree_bit_for_bit():
+    """The left H128 runs two adjacent columns per thread (packed f32x2) when
+    the column count is even and the buffer 8-byte aligned, else four
+    threads per column. Both take the same butterflies in the same order with
+    the same roundings, so an odd column count or a buffer at a 4-byte offset
+    (the four-thread kernels) gives the same bits as the aligned even case.
+    Checked for the plain rotation and for the regularization's left step
+    (work / su, then the rotation)."""
+    from exl3_intel_arc_quantizer_b200._ext import ext
+
+    g = torch.Generator(device="cpu").manual_seed(11)
+    k, n = 384, 130
+    x = torch.randn(k, n, generator=g).to(DEV)
+    a = x.clone()
+    ext().had128_left_(a)
+    odd = torch.randn(k, n + 1, generator=g).to(DEV)
+    odd[:, :n] = x
+    ext().had128_left_(odd)
+    assert torch.equal(a, odd[:, :n])
+    flat = torch.empty(k * n + 1, device=DEV)
+    c = flat[1:].view(k, n)
+    c.copy_(x)
+    ext().had128_left_(c)
+    assert torch.equal(a, c)
+
+    n = 256
+    W = (torch.randn(k, n, generator=g) * 0.02).to(DEV)
+    hdiag = (torch.rand(k, generator=g) + 0.5).to(DEV)
+    su = torch.where(torch.rand(k, generator=g) < 0.5, -1.0, 1.0).to(DEV)
+    sv = torch.where(torch.rand(n, generator=g) < 0.5, -1.0, 1.0).to(DEV)
+    outs = []
+    for offset in (0, 1):
+        buf = torch.empty(k * n + 1, device=DEV)
+        work = buf[offset:offset + k * n].view(k, n)
+        vecs = [torch.empty(k, device=DEV), torch.empty(n, device=DEV),
+                torch.empty(n, device=DEV), torch.empty(k, device=DEV)]
+        ext().regularize_(W, su, sv, hdiag, -1, False, work, *vecs)
+        outs.append([work.clone()] + vecs)
+    for got, want in zip(outs[1], outs[0]):
+        assert torch.equal(got, want)
+
+
 def test_regularize_matches_reference(float_golden):
     w = torch.from_numpy(float_golden["reg/w"]).to(DEV)
     su = torch.from_numpy(float_golden["reg/su_in"]).to(DEV)
