@@ -18,21 +18,33 @@ namespace exl3 {
 
 namespace {
 
-// x @ H on 128-column blocks: one warp per (row, block); lane l holds
-// elements l, l+32, l+64, l+96 of the block.
+// x @ H on 128-column blocks: two (row, block) tasks per warp, both tasks'
+// loads issued first; lane l holds elements l, l+32, l+64, l+96 of a block.
+constexpr int kRightTasks = 2;
 __global__ void had_right_kernel(float* __restrict__ x, int64_t k, int64_t n, float scale) {
   const int64_t warp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  const int64_t nb = n >> 7;
-  if (warp >= k * nb) return;
-  const int64_t row = warp / nb, blk = warp % nb;
-  float* p = x + row * n + blk * 128;
-  float v[4];
+  const int64_t nb = n >> 7, total = k * nb;
+  if (warp * kRightTasks >= total) return;
+  float v[kRightTasks][4];
+  float* p[kRightTasks];
+  bool ok[kRightTasks];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) v[q] = p[lane + 32 * q];
-  fwht128_warp(v, lane);
+  for (int j = 0; j < kRightTasks; ++j) {
+    const int64_t task = warp * kRightTasks + j;
+    ok[j] = task < total;  // the same for every lane of the warp
+    p[j] = x + (ok[j] ? (task / nb) * n + (task % nb) * 128 : 0);
 #pragma unroll
-  for (int q = 0; q < 4; ++q) p[lane + 32 * q] = v[q] * scale;
+    for (int q = 0; q < 4; ++q) v[j][q] = ok[j] ? p[j][lane + 32 * q] : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < kRightTasks; ++j) fwht128_warp(v[j], lane);
+#pragma unroll
+  for (int j = 0; j < kRightTasks; ++j) {
+    if (!ok[j]) continue;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) p[j][lane + 32 * q] = v[j][q] * scale;
+  }
 }
 
 // H @ x on 128-row blocks: a CTA of 256 threads takes 64 columns of one row
@@ -100,7 +112,7 @@ extern "C" int exl3_had128_right(float* x, int64_t k, int64_t n, exl3_stream_t s
   EXL3_REQUIRE(x != nullptr, "x is NULL");
   EXL3_REQUIRE(k > 0 && n > 0 && n % 128 == 0, "columns (%lld) must be a positive multiple of 128",
                (long long)n);
-  const int64_t warps = k * (n / 128);
+  const int64_t warps = (k * (n / 128) + kRightTasks - 1) / kRightTasks;
   const int threads = 256;
   const int64_t blocks = (warps + 7) / 8;
   EXL3_REQUIRE(blocks < (1ll << 31), "matrix too large");

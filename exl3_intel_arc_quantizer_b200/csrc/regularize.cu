@@ -13,8 +13,9 @@
 //                        shared FWHT), plus each row's sum of squares over
 //                        each 32-column slice
 //   reg_rowfinal_kernel  row RMS (slice sums added in a fixed order) and su
-//   reg_left_kernel      work / su, then the 128-row Hadamard (four threads
-//                        per column, no shared memory)
+//   reg_left_kernel      work / su, then the 128-row Hadamard (two adjacent
+//                        columns per thread; four threads per column when
+//                        work is not 8-byte aligned; no shared memory)
 // The reference's sums (torch reductions) have their own order; here every
 // sum has one fixed order (32-element slices, then eight interleaved chains
 // of slices added in order), so results are deterministic and agree with the

@@ -96,6 +96,27 @@ def test_left_rotation_two_column_and_four_thread_kernels_agree_bit_for_bit():
         assert torch.equal(got, want)
 
 
+def test_right_rotation_two_tasks_per_warp_ragged():
+    """The right H128 gives each warp two (row, 128-column block) tasks; with
+    an odd task count (5 rows x 3 blocks) the last warp has one. Every row
+    rotated in one call equals the row rotated alone (3 tasks: one warp with
+    two, one with one), and the product with the block-diagonal H128 to fp32
+    rounding."""
+    from exl3_intel_arc_quantizer_b200._ext import ext
+
+    g = torch.Generator(device="cpu").manual_seed(12)
+    x = torch.randn(5, 384, generator=g).to(DEV)
+    a = x.clone()
+    ext().had128_right_(a)
+    for r in range(5):
+        row = x[r:r + 1].clone()
+        ext().had128_right_(row)
+        assert torch.equal(row[0], a[r])
+    h = hd.hadamard(128, torch.float32, device=DEV)
+    ref = (x.view(5, 3, 128) @ h).view(5, 384)
+    assert (a - ref).abs().max() <= 1e-5 * x.abs().max()
+
+
 def test_regularize_matches_reference(float_golden):
     w = torch.from_numpy(float_golden["reg/w"]).to(DEV)
     su = torch.from_numpy(float_golden["reg/su_in"]).to(DEV)
