@@ -1,10 +1,13 @@
 // 128-point fast Walsh-Hadamard transform held by one warp: lane l holds
 // elements l, l+32, l+64, l+96 in v[0..3]. Sylvester order (the partner of
 // element i at stride h is i ^ h; the lower index keeps the sum), strides
-// 1..16 across lanes by shuffles, 32 and 64 inside the thread. Every kernel
-// that applies the 128-block rotation uses this one function so that the
-// rotation rounds identically wherever it runs (reference
-// exl3_quant/hadamard.py:94-140 multiplies by H128/sqrt(128) as a GEMM).
+// 1..16 across lanes by shuffles, 32 and 64 inside the thread. Every helper
+// here (and the weight decode's pair-line transform) takes the same
+// butterflies in the same order, strides 1, 2, ..., 64, the lower element
+// keeping lower + upper, each rounded once, then one scale by 1/sqrt(128),
+// so the rotation rounds identically whichever kernel and data layout runs
+// it (reference exl3_quant/hadamard.py:94-140 multiplies by H128/sqrt(128)
+// as a GEMM).
 #pragma once
 
 namespace exl3 {

@@ -48,7 +48,8 @@ __global__ void had_right_kernel(float* __restrict__ x, int64_t k, int64_t n, fl
 }
 
 // H @ x on 128-row blocks: a CTA of 256 threads takes 64 columns of one row
-// block, four threads per column (had_left_quad_cols).
+// block, four threads per column (had_left_quad_cols). Used when n is odd or
+// x is not 8-byte aligned; otherwise had_left_pair_kernel runs.
 __global__ void __launch_bounds__(256, 2) had_left_kernel(float* __restrict__ x, int64_t k,
                                                           int64_t n) {
   const int t = threadIdx.x;

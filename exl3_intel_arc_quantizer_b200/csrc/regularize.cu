@@ -300,7 +300,8 @@ __global__ void __launch_bounds__(256) reg_rowfinal_kernel(
 }
 
 // work = H128 (work / su) on 128-row blocks: a CTA of 256 threads takes 64
-// columns of one row block, four threads per column (had_left_quad_cols)
+// columns of one row block, four threads per column (had_left_quad_cols).
+// Used when work is not 8-byte aligned; otherwise reg_left_pair_kernel runs.
 __global__ void __launch_bounds__(256, 2) reg_left_kernel(float* __restrict__ work,
                                                           const float* __restrict__ su,
                                                           int64_t k, int64_t n) {
