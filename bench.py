@@ -490,9 +490,11 @@ def run_storage(device, K=4, shapes=((4096, 4096), (12288, 4096)), reps=5):
         assert torch.equal(packed, container) and torch.equal(unpacked, states)
         # the floating-point stages on the same shape: in-place 128-block
         # Hadamards (8 B per weight), the device regularization (20 B per
-        # weight: column sums, W/sv + right FWHT, work/su + left FWHT) and the
-        # block-LDL fold of a (k, k) factor (4 B written per element, 4 B read
-        # below the diagonal)
+        # weight: column sums, W/sv + right FWHT, work/su + left FWHT; timed
+        # through the binding that leaves its four info words on the device,
+        # so the host's wake-up from the read-back sync is not in the kernel
+        # time) and the block-LDL fold of a (k, k) factor (4 B written per
+        # element, 4 B read below the diagonal)
         t_hl = timed(lambda: e.had128_left_(w))
         t_hr = timed(lambda: e.had128_right_(w))
         W0 = torch.randn((k, n), generator=g, device=device) * 0.02
@@ -501,7 +503,7 @@ def run_storage(device, K=4, shapes=((4096, 4096), (12288, 4096)), reps=5):
         hd = torch.rand(k, generator=g, device=device) + 0.5
         regs = [torch.empty_like(W0), torch.empty(k, device=device), torch.empty(n, device=device),
                 torch.empty(n, device=device), torch.empty(k, device=device)]
-        t_reg = timed(lambda: e.regularize_(W0, ones_k, ones_n, hd, -1, False, *regs))
+        t_reg = timed(lambda: e.regularize_device_(W0, ones_k, ones_n, hd, -1, False, *regs))
         a = torch.randn((k, k // 2), generator=g, device=device)
         chol = torch.linalg.cholesky(a @ a.T / k + 0.05 * torch.eye(k, device=device)).contiguous()
         L = torch.empty_like(chol)

@@ -152,12 +152,12 @@ void ldlq_(std::vector<at::Tensor> W, std::vector<at::Tensor> L, std::vector<at:
         "ldlq");
 }
 
-// Regularization on the device; returns (apply_out_scales, zeros, skew, mean)
-// read back once (the only host synchronisation of the stage).
-std::vector<double> regularize_(at::Tensor W, at::Tensor su_in, at::Tensor sv_in,
-                                c10::optional<at::Tensor> h_diag_src, int64_t force_out_scales,
-                                bool q_fallback, at::Tensor work, at::Tensor su_out,
-                                at::Tensor sv_out, at::Tensor out_scales, at::Tensor in_scales) {
+// Regularization on the device with no host synchronisation; returns the
+// device info words {apply_out_scales, zeros, skew bits, mean bits} (int32).
+at::Tensor regularize_device_(at::Tensor W, at::Tensor su_in, at::Tensor sv_in,
+                              c10::optional<at::Tensor> h_diag_src, int64_t force_out_scales,
+                              bool q_fallback, at::Tensor work, at::Tensor su_out,
+                              at::Tensor sv_out, at::Tensor out_scales, at::Tensor in_scales) {
   check_f32_cuda_2d(W, "weight");
   check_f32_cuda_2d(work, "work");
   const int64_t k = W.size(0), n = W.size(1);
@@ -193,7 +193,18 @@ std::vector<double> regularize_(at::Tensor W, at::Tensor su_in, at::Tensor sv_in
                         out_scales.data_ptr<float>(), in_scales.data_ptr<float>(),
                         info.data_ptr(), k, n, ws.data_ptr(), bytes, cur_stream(W)),
         "regularize");
-  auto host = info.cpu();
+  return info;
+}
+
+// Regularization on the device; returns (apply_out_scales, zeros, skew, mean)
+// read back once (the only host synchronisation of the stage).
+std::vector<double> regularize_(at::Tensor W, at::Tensor su_in, at::Tensor sv_in,
+                                c10::optional<at::Tensor> h_diag_src, int64_t force_out_scales,
+                                bool q_fallback, at::Tensor work, at::Tensor su_out,
+                                at::Tensor sv_out, at::Tensor out_scales, at::Tensor in_scales) {
+  auto host = regularize_device_(W, su_in, sv_in, h_diag_src, force_out_scales, q_fallback, work,
+                                 su_out, sv_out, out_scales, in_scales)
+                  .cpu();
   const int32_t* iv = host.data_ptr<int32_t>();
   float skew, mean;
   std::memcpy(&skew, iv + 2, 4);
@@ -223,6 +234,11 @@ void block_ldl_fold(at::Tensor chol, at::Tensor L, c10::optional<at::Tensor> inv
 }
 
 void register_linalg_ops(pybind11::module& m) {
+  m.def("regularize_device_", &regularize_device_, pybind11::arg("W"), pybind11::arg("su_in"),
+        pybind11::arg("sv_in"), pybind11::arg("H_diag"), pybind11::arg("force_out_scales"),
+        pybind11::arg("q_fallback"), pybind11::arg("work"), pybind11::arg("su_out"),
+        pybind11::arg("sv_out"), pybind11::arg("out_scales"), pybind11::arg("in_scales"),
+        "regularize_ without the host read-back: returns the int32 info words on the device");
   m.def("regularize_", &regularize_, pybind11::arg("W"), pybind11::arg("su_in"),
         pybind11::arg("sv_in"), pybind11::arg("H_diag"), pybind11::arg("force_out_scales"),
         pybind11::arg("q_fallback"), pybind11::arg("work"), pybind11::arg("su_out"),

@@ -388,3 +388,34 @@ def test_ldlq_schedule_spreads_short_jobs_and_keeps_results():
     for job, r in zip(jobs, together):
         one = ldlq_native([job], K=2)[0]
         assert torch.equal(one.weight_q, r.weight_q) and torch.equal(one.encoded, r.encoded)
+
+
+def test_regularize_device_binding_matches_the_read_back_one():
+    """regularize_device_ launches the same regularization as regularize_ but
+    returns its four info words as an int32 device tensor instead of reading
+    them back: same work, scales and flags."""
+    import struct
+
+    from exl3_intel_arc_quantizer_b200._ext import ext
+
+    g = torch.Generator(device="cpu").manual_seed(13)
+    k, n = 256, 384
+    W = (torch.randn(k, n, generator=g) * 0.02).to(DEV)
+    hdiag = (torch.rand(k, generator=g) + 0.5).to(DEV)
+    su = torch.ones(k, device=DEV)
+    sv = torch.ones(n, device=DEV)
+
+    def bufs():
+        return [torch.empty(k, n, device=DEV), torch.empty(k, device=DEV),
+                torch.empty(n, device=DEV), torch.empty(n, device=DEV), torch.empty(k, device=DEV)]
+
+    a, b = bufs(), bufs()
+    flags = ext().regularize_(W, su, sv, hdiag, -1, False, *a)
+    info = ext().regularize_device_(W, su, sv, hdiag, -1, False, *b)
+    assert info.is_cuda and info.dtype == torch.int32 and info.numel() == 4
+    iv = info.cpu().tolist()
+    skew, mean = (struct.unpack("<f", struct.pack("<i", v))[0] for v in iv[2:])
+    assert (iv[0], iv[1]) == (int(flags[0]), int(flags[1]))
+    assert skew == flags[2] and mean == flags[3]
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
