@@ -67,22 +67,35 @@ __device__ __forceinline__ float block_sum_f(float v, float* red) {
   return s;
 }
 
-// skew factor of sqrt(diag(H)): one CTA of 1024 threads
+// skew factor of sqrt(diag(H)): one CTA of 1024 threads. For d <= kSkewCacheKeys
+// the keys sqrt(H_ii) are read from H once (all loads of a thread in flight
+// together) into dynamic shared memory, and the four digit passes and the sums
+// read them there; larger d re-reads H_ii in every pass. Either way every
+// thread visits the same keys in the same order, so the sums are the same.
+constexpr int64_t kSkewCacheKeys = 32768;  // 128 KiB of shared memory
 __global__ void __launch_bounds__(1024) reg_skew_kernel(const float* __restrict__ hdiag,
                                                         int64_t stride, int64_t d,
                                                         RegInfo* __restrict__ info) {
+  extern __shared__ float keys_s[];  // d keys when cached
   __shared__ unsigned int hist[256];
   __shared__ float red[32];
   __shared__ uint32_t sel[2];  // digit prefix, remaining count
   const int t = threadIdx.x;
   const int64_t want = d / kSkewFraction;
+  const bool cached = d <= kSkewCacheKeys;
+  if (cached) {
+#pragma unroll 8
+    for (int64_t i = t; i < d; i += blockDim.x) keys_s[i] = sqrtf(hdiag[i * stride]);
+    __syncthreads();
+  }
+  auto key_at = [&](int64_t i) { return cached ? keys_s[i] : sqrtf(hdiag[i * stride]); };
   uint32_t prefix = 0u, mask = 0u;
   int64_t remaining = want;
   for (int shift = 24; shift >= 0 && want > 0; shift -= 8) {
     for (int i = t; i < 256; i += blockDim.x) hist[i] = 0u;
     __syncthreads();
     for (int64_t i = t; i < d; i += blockDim.x) {
-      const uint32_t key = __float_as_uint(sqrtf(hdiag[i * stride]));
+      const uint32_t key = __float_as_uint(key_at(i));
       if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
     }
     __syncthreads();
@@ -125,7 +138,7 @@ __global__ void __launch_bounds__(1024) reg_skew_kernel(const float* __restrict_
   // top = sum of keys above the want-th largest + remaining copies of it
   float top = 0.f, all = 0.f;
   for (int64_t i = t; i < d; i += blockDim.x) {
-    const float v = sqrtf(hdiag[i * stride]);
+    const float v = key_at(i);
     all += v;
     if (want > 0 && __float_as_uint(v) > prefix) top += v;
   }
@@ -480,7 +493,16 @@ extern "C" int exl3_regularize(const float* W, const float* su_in, const float* 
   EXL3_CUDA(cudaMemsetAsync(inf, 0xFF, sizeof(RegInfo), s));  // skew NaN until computed
   const int has_skew = (h_diag != nullptr && !q_fallback) ? 1 : 0;
   if (has_skew) {
-    reg_skew_kernel<<<1, 1024, 0, s>>>(h_diag, h_diag_stride, k, inf);
+    static DeviceBits attr_done;
+    int dev = 0;
+    EXL3_CUDA(cudaGetDevice(&dev));
+    if (!attr_done.has(dev)) {
+      EXL3_CUDA(cudaFuncSetAttribute(reg_skew_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)(kSkewCacheKeys * sizeof(float))));
+      attr_done.set(dev);
+    }
+    const size_t cache = k <= kSkewCacheKeys ? (size_t)k * sizeof(float) : 0;
+    reg_skew_kernel<<<1, 1024, cache, s>>>(h_diag, h_diag_stride, k, inf);
     EXL3_LAUNCHED();
   }
   const int64_t nb = (k + 31) / 32;

@@ -419,3 +419,31 @@ def test_regularize_device_binding_matches_the_read_back_one():
     assert skew == flags[2] and mean == flags[3]
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("k", [32768, 32896])
+def test_regularize_skew_with_and_without_the_key_cache(k):
+    """The skew's radix select keeps the keys sqrt(H_ii) in shared memory for
+    up to 32,768 rows and re-reads them from H above that (here through a
+    strided diagonal view). Both give (sum of the k/50 largest keys) / (sum
+    of all keys) as computed in float64 from the same fp32 keys, to 1e-6."""
+    import struct
+
+    from exl3_intel_arc_quantizer_b200._ext import ext
+
+    g = torch.Generator(device="cpu").manual_seed(k)
+    n = 128
+    W = (torch.randn(k, n, generator=g) * 0.02).to(DEV)
+    base = torch.rand(k, 3, generator=g) * 2.0 + 0.01
+    base[:40, 1] = 7.5                       # ties at the top
+    hdiag = base.to(DEV)[:, 1]               # stride 3
+    assert hdiag.stride(0) == 3
+    bufs = [torch.empty(k, n, device=DEV), torch.empty(k, device=DEV),
+            torch.empty(n, device=DEV), torch.empty(n, device=DEV), torch.empty(k, device=DEV)]
+    info = ext().regularize_device_(W, torch.ones(k, device=DEV), torch.ones(n, device=DEV),
+                                    hdiag, -1, False, *bufs).cpu().tolist()
+    skew = struct.unpack("<f", struct.pack("<i", info[2]))[0]
+    keys = torch.sqrt(base[:, 1].float()).double()
+    want = k // 50
+    ref = float(keys.sort(descending=True).values[:want].sum() / keys.sum())
+    assert abs(skew - ref) <= 1e-6 * ref, (skew, ref)
